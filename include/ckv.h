@@ -1,0 +1,187 @@
+/*
+ * ckv.h -- C ABI of libckv, the B200 (sm_100a) fixed-mode KV-page codec.
+ *
+ * Drop-in boundary for the reference's CuSZpWrapper
+ * (integration/cuszp_wrapper/cuszp_wrapper.h:9-158, exposed to Python by
+ * integration/cuszp_wrapper/pybind11_bindings.cpp:9-264).  Every wrapper
+ * method has one entry point here with the same arguments, as plain
+ * pointers and sizes: tensors become device pointers plus element counts,
+ * std::vector<torch::Tensor> becomes a host array of device pointers, and
+ * the Python-visible outputs (sizes, resolved bounds) are written to caller
+ * host arrays.  No torch types cross the boundary.
+ *
+ * Conventions
+ *   - Every call returns CKV_OK (0) or a nonzero ckv_status; the message is
+ *     available from ckv_last_error().  The reference returns bool and
+ *     prints to stderr; the Python module maps !CKV_OK to False plus the
+ *     message on stderr.
+ *   - `stream` is a cudaStream_t (0 = legacy default stream).  Compression
+ *     calls block until sizes and bounds are on the host, as the reference
+ *     does (cuszp_wrapper.cpp:530); decompression calls only enqueue work.
+ *   - Caller owns all data buffers.  A context owns grow-only device and
+ *     pinned-host workspaces and is not thread-safe (one per thread), like
+ *     one CuSZpWrapper instance.
+ *   - Bitstreams are byte-identical to the reference's batched BF16 kernels
+ *     (cuszp_batched_fixed.cu), except that rate bytes of blocks past the
+ *     last element -- never written by the reference -- are written as 0.
+ */
+#ifndef CKV_H
+#define CKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CKV_API __attribute__((visibility("default")))
+#else
+#define CKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int ckv_status;
+#define CKV_OK 0
+#define CKV_ERR_ARGUMENT 1      /* invalid argument / precondition */
+#define CKV_ERR_UNSUPPORTED 2   /* configuration outside the fixed 1D path */
+#define CKV_ERR_CUDA 3          /* CUDA runtime error */
+#define CKV_ERR_CAPACITY 4      /* compressed data larger than its buffer */
+#define CKV_ERR_STREAM 5        /* corrupt or truncated bitstream */
+#define CKV_ERR_INTERNAL 6      /* device-side consistency check failed */
+
+/* cuszp_dim_t / cuszp_mode_t / cuszp_type_t (pybind11_bindings.cpp:13-28). */
+#define CKV_DIM_1D 0
+#define CKV_DIM_2D 1
+#define CKV_DIM_3D 2
+#define CKV_MODE_FIXED 0
+#define CKV_MODE_PLAIN 1
+#define CKV_MODE_OUTLIER 2
+#define CKV_TYPE_FLOAT 0
+#define CKV_TYPE_DOUBLE 1
+
+/* CuSZpWrapper::CompressionConfig (cuszp_wrapper.h:11-17). */
+typedef struct {
+    float error_bound;          /* default 1e-4 */
+    int use_relative_error;     /* default 1 */
+    int processing_dim;         /* CKV_DIM_* */
+    int encoding_mode;          /* CKV_MODE_*; only FIXED is implemented */
+    int data_type;              /* CKV_TYPE_*; only FLOAT is implemented */
+} ckv_config;
+
+typedef struct ckv_ctx ckv_ctx;
+
+/* CuSZpWrapper(config, device_id)   cuszp_wrapper.cpp:23-39 */
+CKV_API ckv_status ckv_create(const ckv_config* config, int device_id, ckv_ctx** out);
+/* ~CuSZpWrapper()                   cuszp_wrapper.cpp:41-66 */
+CKV_API void ckv_destroy(ckv_ctx* ctx);
+/* get_config / update_config        cuszp_wrapper.h:126-127 */
+CKV_API ckv_status ckv_get_config(const ckv_ctx* ctx, ckv_config* out);
+CKV_API ckv_status ckv_update_config(ckv_ctx* ctx, const ckv_config* config);
+/* Message of the last failed call on this context ("" if none). */
+CKV_API const char* ckv_last_error(const ckv_ctx* ctx);
+/* estimate_compressed_buffer_size   cuszp_wrapper.cpp:1319-1321 (2 * bytes) */
+CKV_API size_t ckv_estimate_compressed_buffer_size(size_t original_bytes);
+/* Upper bound of the compressed size of n elements (every block at rate 31). */
+CKV_API size_t ckv_max_compressed_size(size_t n);
+
+/* compress(input, buffer, eps_override)   cuszp_wrapper.cpp:216-325.
+ * FP32 input of n elements, fixed mode.  The reference reallocates a
+ * too-small buffer; here the caller provides `capacity` bytes and gets
+ * CKV_ERR_CAPACITY (with *size = needed bytes) if it is too small. */
+CKV_API ckv_status ckv_compress(ckv_ctx* ctx, const float* input, size_t n,
+                        uint8_t* out, size_t capacity, float eps_override,
+                        size_t* size, float* bound, void* stream);
+
+/* compress_batch_fixed(inputs, outputs, eps)   cuszp_wrapper.cpp:327-429.
+ * `eps` may be NULL (config bound); eps[i] <= 0 also means config bound. */
+CKV_API ckv_status ckv_compress_batch_fixed(ckv_ctx* ctx, const float* const* inputs,
+                                    uint8_t* const* outputs, const float* eps,
+                                    size_t batch, size_t n, size_t capacity,
+                                    size_t* sizes, float* bounds, void* stream);
+
+/* compress_batch_fixed_bf16(inputs, outputs, eps)  cuszp_wrapper.cpp:431-544 */
+CKV_API ckv_status ckv_compress_batch_fixed_bf16(ckv_ctx* ctx, const void* const* inputs,
+                                         uint8_t* const* outputs, const float* eps,
+                                         size_t batch, size_t n, size_t capacity,
+                                         size_t* sizes, float* bounds, void* stream);
+
+/* compress_batch_fixed_bf16_indexed(...)       cuszp_wrapper.cpp:548-681.
+ * Pages are [prefix_count][source_layers][elements_per_layer] BF16; unit i
+ * is layers layer_indices[0..selected) (device int64 array) of page i. */
+CKV_API ckv_status ckv_compress_batch_fixed_bf16_indexed(
+    ckv_ctx* ctx, const void* const* inputs, uint8_t* const* outputs,
+    const int64_t* layer_indices, size_t selected, size_t prefix_count,
+    size_t source_layers, size_t elements_per_layer, const float* eps,
+    size_t batch, size_t capacity, size_t* sizes, float* bounds, void* stream);
+
+/* compress_batch_fixed_bf16_indexed_groups(...) cuszp_wrapper.cpp:683-868.
+ * Group g covers group_sizes[g] consecutive units and selects
+ * selected[g] layers from layer_indices[g] (device int64 arrays).  All
+ * groups go into ONE launch here (the reference launches per group).
+ * capacities[i] is unit i's buffer size in bytes. */
+CKV_API ckv_status ckv_compress_batch_fixed_bf16_indexed_groups(
+    ckv_ctx* ctx, const void* const* inputs, uint8_t* const* outputs,
+    const int64_t* const* layer_indices, const size_t* selected,
+    const size_t* group_sizes, size_t groups, size_t prefix_count,
+    size_t source_layers, size_t elements_per_layer, const float* eps,
+    size_t batch, const size_t* capacities, size_t* sizes, float* bounds,
+    void* stream);
+
+/* decompress(buffer, size, output, bound)      cuszp_wrapper.cpp:870-943.
+ * FP32 output of n elements, fixed mode. */
+CKV_API ckv_status ckv_decompress(ckv_ctx* ctx, const uint8_t* in, size_t size,
+                          float* out, size_t n, float bound, void* stream);
+
+/* decompress_batch(buffers, sizes, outputs, bounds) cuszp_wrapper.cpp:944-1033.
+ * FP32 outputs, n[i] elements each; one launch for the whole batch. */
+CKV_API ckv_status ckv_decompress_batch(ckv_ctx* ctx, const uint8_t* const* ins,
+                                const size_t* sizes, float* const* outs,
+                                const size_t* n, const float* bounds,
+                                size_t batch, void* stream);
+
+/* decompress_batch_fixed_bf16(...)             cuszp_wrapper.cpp:1034-1110.
+ * Page i decodes to out + i * n (BF16); out holds out_numel elements. */
+CKV_API ckv_status ckv_decompress_batch_fixed_bf16(ckv_ctx* ctx, const uint8_t* const* ins,
+                                           const size_t* sizes, size_t batch,
+                                           void* out, size_t out_numel, size_t n,
+                                           const float* bounds, void* stream);
+
+/* decompress_batch_fixed_bf16_scatter(...)     cuszp_wrapper.cpp:1111-1212.
+ * Page i decodes into outs[i * per_page + d], elements_per_dest each. */
+CKV_API ckv_status ckv_decompress_batch_fixed_bf16_scatter(
+    ckv_ctx* ctx, const uint8_t* const* ins, const size_t* sizes, size_t batch,
+    void* const* outs, size_t out_count, size_t n, size_t per_page,
+    size_t elements_per_dest, const float* bounds, void* stream);
+
+/* decompress_batch_fixed_bf16_indexed_scatter(...) cuszp_wrapper.cpp:1214-1313.
+ * Unit i decodes into layers layer_indices[0..selected) of page outs[i]. */
+CKV_API ckv_status ckv_decompress_batch_fixed_bf16_indexed_scatter(
+    ckv_ctx* ctx, const uint8_t* const* ins, const size_t* sizes, size_t batch,
+    void* const* outs, const int64_t* layer_indices, size_t selected,
+    size_t prefix_count, size_t source_layers, size_t elements_per_layer,
+    const float* bounds, void* stream);
+
+/* ---- extensions (no counterpart in the reference wrapper) ---------------- */
+
+/* Decode rate-0 blocks as zeros instead of leaving the destination as it was
+ * (the reference decoder does not write those blocks). */
+CKV_API ckv_status ckv_set_zero_fill(ckv_ctx* ctx, int zero_fill);
+
+/* OR of the device status bits recorded by asynchronous decode calls since
+ * the last call with reset != 0 (CKV_DEV_* below); waits for the work queued
+ * on `stream` first. */
+#define CKV_DEV_CAPACITY 1u
+#define CKV_DEV_RATE_CHECK 2u
+#define CKV_DEV_BAD_STREAM 4u
+#define CKV_DEV_TIMEOUT 8u
+CKV_API ckv_status ckv_device_status(ckv_ctx* ctx, void* stream, int reset, uint32_t* bits);
+
+/* Number of kernel launches libckv has issued since it was loaded. */
+CKV_API uint64_t ckv_kernel_launches(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CKV_H */

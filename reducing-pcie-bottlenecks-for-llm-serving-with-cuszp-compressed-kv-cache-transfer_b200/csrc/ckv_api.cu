@@ -1,0 +1,697 @@
+// C ABI of libckv (include/ckv.h): the CuSZpWrapper surface of the
+// reference (integration/cuszp_wrapper/cuszp_wrapper.cpp) on top of the
+// sm_100a encode / decode kernels.
+//
+// Each call turns its arguments into a list of units (one per page or
+// selected-layer group) plus element maps, uploads that list through a small
+// ring of pinned staging slots (one H2D copy per call), and issues ONE kernel
+// launch for the whole batch.  Compression results (sizes, resolved bounds,
+// status) are written by the kernel into mapped pinned memory, so the call
+// only has to synchronise the stream before returning them -- no per-page
+// device-to-host copies as in the reference (cuszp_wrapper.cpp:523-529).
+#include "../../include/ckv.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "ckv_launch.h"
+
+namespace ckv {
+
+static std::atomic<uint64_t> g_launches{0};
+uint64_t launches_issued() { return g_launches.load(); }
+void note_launch() { g_launches.fetch_add(1); }
+
+}  // namespace ckv
+
+using ckv::Map;
+using ckv::Unit;
+
+namespace {
+
+constexpr int kSlots = 4;
+
+struct Slot {
+    uint8_t* host = nullptr;   // pinned
+    uint8_t* dev = nullptr;
+    size_t cap = 0;
+    cudaEvent_t done = nullptr;
+    bool pending = false;
+};
+
+size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+}  // namespace
+
+struct ckv_ctx {
+    ckv_config config;
+    int device = 0;
+    bool zero_fill = false;
+    std::string err;
+    Slot slots[kSlots];
+    int next_slot = 0;
+    // compression results, mapped pinned memory
+    uint64_t* sizes = nullptr;
+    float* bounds = nullptr;
+    uint32_t* status = nullptr;
+    size_t results_cap = 0;
+    // decode status words (device), accumulated until read
+    uint32_t* dec_status = nullptr;
+    size_t dec_status_cap = 0;
+};
+
+namespace {
+
+ckv_status fail(ckv_ctx* ctx, ckv_status code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->err = buf;
+    return code;
+}
+
+ckv_status cuda_fail(ckv_ctx* ctx, const char* what, cudaError_t e) {
+    return fail(ctx, CKV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool fixed_1d_float(const ckv_config& c) {
+    return c.processing_dim == CKV_DIM_1D && c.data_type == CKV_TYPE_FLOAT &&
+           c.encoding_mode == CKV_MODE_FIXED;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// Descriptor list built on the host for one launch.
+struct Batch {
+    std::vector<Unit> units;
+    std::vector<Map> maps;
+    std::vector<void*> table;   // split-map destinations
+    uint32_t max_n = 0;
+};
+
+// Copies the batch to the device through the next staging slot; patches
+// map table pointers to their device addresses.
+ckv_status upload(ckv_ctx* ctx, Batch& b, cudaStream_t stream, Slot** used,
+                  const Unit** d_units, const Map** d_maps) {
+    const size_t units_bytes = align16(b.units.size() * sizeof(Unit));
+    const size_t maps_bytes = align16(b.maps.size() * sizeof(Map));
+    const size_t table_bytes = align16(b.table.size() * sizeof(void*));
+    const size_t need = units_bytes + maps_bytes + table_bytes;
+    Slot& s = ctx->slots[ctx->next_slot];
+    ctx->next_slot = (ctx->next_slot + 1) % kSlots;
+    if (s.pending) {
+        cudaError_t e = cudaEventSynchronize(s.done);
+        if (e != cudaSuccess) return cuda_fail(ctx, "waiting for a descriptor slot", e);
+        s.pending = false;
+    }
+    if (!s.done) {
+        cudaError_t e = cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming);
+        if (e != cudaSuccess) return cuda_fail(ctx, "creating an event", e);
+    }
+    if (need > s.cap) {
+        size_t cap = std::max<size_t>(need, 16384);
+        cudaFreeHost(s.host);
+        cudaFree(s.dev);
+        s.host = nullptr;
+        s.dev = nullptr;
+        s.cap = 0;
+        cudaError_t e = cudaMallocHost(&s.host, cap);
+        if (e != cudaSuccess) return cuda_fail(ctx, "allocating pinned descriptors", e);
+        e = cudaMalloc(&s.dev, cap);
+        if (e != cudaSuccess) return cuda_fail(ctx, "allocating device descriptors", e);
+        s.cap = cap;
+    }
+    uint8_t* h = s.host;
+    void** table_dev = reinterpret_cast<void**>(s.dev + units_bytes + maps_bytes);
+    for (Map& m : b.maps)
+        if (m.kind == ckv::kMapSplit)
+            m.table = table_dev + reinterpret_cast<uintptr_t>(m.table);  // offset -> address
+    std::memcpy(h, b.units.data(), b.units.size() * sizeof(Unit));
+    std::memcpy(h + units_bytes, b.maps.data(), b.maps.size() * sizeof(Map));
+    if (!b.table.empty())
+        std::memcpy(h + units_bytes + maps_bytes, b.table.data(), b.table.size() * sizeof(void*));
+    cudaError_t e = cudaMemcpyAsync(s.dev, h, need, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, "uploading descriptors", e);
+    *used = &s;
+    *d_units = reinterpret_cast<const Unit*>(s.dev);
+    *d_maps = reinterpret_cast<const Map*>(s.dev + units_bytes);
+    return CKV_OK;
+}
+
+void release(Slot* s, cudaStream_t stream) {
+    if (s && cudaEventRecord(s->done, stream) == cudaSuccess) s->pending = true;
+}
+
+ckv_status ensure_results(ckv_ctx* ctx, size_t count) {
+    if (count <= ctx->results_cap) return CKV_OK;
+    cudaFreeHost(ctx->sizes);
+    cudaFreeHost(ctx->bounds);
+    cudaFreeHost(ctx->status);
+    ctx->sizes = nullptr;
+    ctx->bounds = nullptr;
+    ctx->status = nullptr;
+    ctx->results_cap = 0;
+    const size_t cap = std::max<size_t>(count, 256);
+    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&ctx->sizes), cap * sizeof(uint64_t), cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostAlloc(reinterpret_cast<void**>(&ctx->bounds), cap * sizeof(float), cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostAlloc(reinterpret_cast<void**>(&ctx->status), cap * sizeof(uint32_t), cudaHostAllocMapped);
+    if (e != cudaSuccess) return cuda_fail(ctx, "allocating result buffers", e);
+    ctx->results_cap = cap;
+    return CKV_OK;
+}
+
+ckv_status ensure_dec_status(ckv_ctx* ctx, size_t count) {
+    if (count <= ctx->dec_status_cap) return CKV_OK;
+    // Keep the bits recorded so far.
+    uint32_t old = 0;
+    if (ctx->dec_status) {
+        std::vector<uint32_t> h(ctx->dec_status_cap);
+        cudaDeviceSynchronize();
+        cudaMemcpy(h.data(), ctx->dec_status, h.size() * 4, cudaMemcpyDeviceToHost);
+        for (uint32_t v : h) old |= v;
+        cudaFree(ctx->dec_status);
+        ctx->dec_status = nullptr;
+    }
+    const size_t cap = std::max<size_t>(count, 1024);
+    cudaError_t e = cudaMalloc(&ctx->dec_status, cap * sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(ctx, "allocating decode status", e);
+    e = cudaMemset(ctx->dec_status, 0, cap * sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(ctx, "clearing decode status", e);
+    if (old) cudaMemcpy(ctx->dec_status, &old, 4, cudaMemcpyHostToDevice);
+    ctx->dec_status_cap = cap;
+    return CKV_OK;
+}
+
+float eps_of(const ckv_ctx* ctx, const float* eps, size_t i) {
+    return (eps && eps[i] > 0.0f) ? eps[i] : ctx->config.error_bound;
+}
+
+ckv_status status_to_code(ckv_ctx* ctx, uint32_t bits) {
+    if (!bits) return CKV_OK;
+    if (bits & ckv::kErrCapacity)
+        return fail(ctx, CKV_ERR_CAPACITY, "compressed data larger than its output buffer");
+    if (bits & ckv::kErrBadStream)
+        return fail(ctx, CKV_ERR_STREAM, "corrupt or truncated compressed page");
+    if (bits & ckv::kErrTimeout)
+        return fail(ctx, CKV_ERR_CUDA, "a bounded wait in the kernel ran out");
+    return fail(ctx, CKV_ERR_INTERNAL, "kernel consistency check failed (status 0x%x)", bits);
+}
+
+// Encode a prepared batch and return sizes / bounds on the host.
+ckv_status run_encode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, size_t* sizes,
+                      float* bounds, void* stream_ptr) {
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (b.max_n > ckv::encode_max_elements(type))
+        return fail(ctx, CKV_ERR_UNSUPPORTED,
+                    "unit of %u elements exceeds the single-pass encoder limit (%u)",
+                    b.max_n, ckv::encode_max_elements(type));
+    DeviceGuard guard(ctx->device);
+    const size_t count = b.units.size();
+    ckv_status st = ensure_results(ctx, count);
+    if (st != CKV_OK) return st;
+    std::memset(ctx->status, 0, count * sizeof(uint32_t));
+    Slot* slot = nullptr;
+    const Unit* d_units;
+    const Map* d_maps;
+    st = upload(ctx, b, stream, &slot, &d_units, &d_maps);
+    if (st != CKV_OK) return st;
+    ckv::EncodeLaunch l{};
+    l.units = d_units;
+    l.maps = d_maps;
+    l.num_units = static_cast<uint32_t>(count);
+    l.max_n = b.max_n;
+    l.relative = ctx->config.use_relative_error != 0;
+    l.sizes = ctx->sizes;
+    l.bounds = ctx->bounds;
+    l.status = ctx->status;
+    l.type = type;
+    cudaError_t e = ckv::launch_encode(l, stream);
+    release(slot, stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, "encode launch", e);
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, "encode", e);
+    uint32_t bits = 0;
+    for (size_t i = 0; i < count; ++i) {
+        bits |= ctx->status[i];
+        sizes[i] = static_cast<size_t>(ctx->sizes[i]);
+        bounds[i] = ctx->bounds[i];
+    }
+    return status_to_code(ctx, bits);
+}
+
+ckv_status run_decode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, void* stream_ptr) {
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    DeviceGuard guard(ctx->device);
+    const size_t count = b.units.size();
+    ckv_status st = ensure_dec_status(ctx, count);
+    if (st != CKV_OK) return st;
+    Slot* slot = nullptr;
+    const Unit* d_units;
+    const Map* d_maps;
+    st = upload(ctx, b, stream, &slot, &d_units, &d_maps);
+    if (st != CKV_OK) return st;
+    ckv::DecodeLaunch l{};
+    l.units = d_units;
+    l.maps = d_maps;
+    l.num_units = static_cast<uint32_t>(count);
+    l.max_n = b.max_n;
+    l.zero_fill = ctx->zero_fill;
+    l.status = ctx->dec_status;
+    l.type = type;
+    cudaError_t e = ckv::launch_decode(l, stream);
+    release(slot, stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, "decode launch", e);
+    return CKV_OK;
+}
+
+Map identity_map() {
+    Map m{};
+    m.kind = ckv::kMapIdentity;
+    return m;
+}
+
+Map layers_map(const int64_t* layers, size_t selected, size_t source_layers,
+               size_t elements_per_layer) {
+    Map m{};
+    m.kind = ckv::kMapLayers;
+    m.run = static_cast<uint32_t>(elements_per_layer);
+    m.selected = static_cast<uint32_t>(selected);
+    m.source_layers = static_cast<uint32_t>(source_layers);
+    m.layers = layers;
+    return m;
+}
+
+bool fits_u32(size_t v) { return v > 0 && v <= 0xffffffffu; }
+
+ckv_status check_ctx(ckv_ctx* ctx) {
+    return ctx ? CKV_OK : CKV_ERR_ARGUMENT;
+}
+
+ckv_status check_fixed(ckv_ctx* ctx, const char* what) {
+    if (!fixed_1d_float(ctx->config))
+        return fail(ctx, CKV_ERR_UNSUPPORTED, "%s requires fixed-mode 1D float configuration", what);
+    return CKV_OK;
+}
+
+ckv_status check_stream_ptrs(ckv_ctx* ctx, const uint8_t* const* ins, const size_t* sizes,
+                             size_t batch) {
+    for (size_t i = 0; i < batch; ++i) {
+        if (!ins[i] || sizes[i] == 0)
+            return fail(ctx, CKV_ERR_ARGUMENT, "invalid compressed page %zu", i);
+        if (reinterpret_cast<uintptr_t>(ins[i]) & 3u)
+            return fail(ctx, CKV_ERR_ARGUMENT, "compressed page %zu is not 4-byte aligned", i);
+    }
+    return CKV_OK;
+}
+
+// Shared body of the BF16 / FP32 batched compressors.
+ckv_status compress_batch(ckv_ctx* ctx, const void* const* inputs, uint8_t* const* outputs,
+                          const float* eps, size_t batch, size_t n, size_t capacity,
+                          size_t elem_bytes, size_t* sizes, float* bounds, void* stream,
+                          ckv::ElemType type) {
+    if (check_ctx(ctx)) return CKV_ERR_ARGUMENT;
+    ctx->err.clear();
+    if (batch == 0 || !inputs || !outputs || !sizes || !bounds)
+        return fail(ctx, CKV_ERR_ARGUMENT, "empty batch or null argument");
+    if (ckv_status s = check_fixed(ctx, "batched compression")) return s;
+    if (!fits_u32(n)) return fail(ctx, CKV_ERR_ARGUMENT, "invalid element count %zu", n);
+    if (capacity < ckv_estimate_compressed_buffer_size(n * 4))
+        return fail(ctx, CKV_ERR_ARGUMENT, "output capacity %zu below %zu bytes", capacity,
+                    ckv_estimate_compressed_buffer_size(n * 4));
+    Batch b;
+    b.maps.push_back(identity_map());
+    b.max_n = static_cast<uint32_t>(n);
+    b.units.resize(batch);
+    for (size_t i = 0; i < batch; ++i) {
+        if (!inputs[i] || !outputs[i])
+            return fail(ctx, CKV_ERR_ARGUMENT, "null pointer for page %zu", i);
+        if (reinterpret_cast<uintptr_t>(inputs[i]) % elem_bytes)
+            return fail(ctx, CKV_ERR_ARGUMENT, "misaligned input page %zu", i);
+        Unit& u = b.units[i];
+        u = Unit{};
+        u.elems = inputs[i];
+        u.stream = outputs[i];
+        u.capacity = capacity;
+        u.n = static_cast<uint32_t>(n);
+        u.map = 0;
+        u.eb = eps_of(ctx, eps, i);
+    }
+    return run_encode(ctx, b, type, sizes, bounds, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t ckv_estimate_compressed_buffer_size(size_t original_bytes) {
+    return original_bytes * 2;
+}
+
+size_t ckv_max_compressed_size(size_t n) {
+    const size_t groups = (n + ckv::kGroup - 1) / ckv::kGroup;
+    const size_t blocks = (n + ckv::kBlock - 1) / ckv::kBlock;
+    return groups * (ckv::kGroup / ckv::kBlock) + blocks * (4 + 4 * 32);
+}
+
+uint64_t ckv_kernel_launches(void) { return ckv::launches_issued(); }
+
+ckv_status ckv_create(const ckv_config* config, int device_id, ckv_ctx** out) {
+    if (!config || !out) return CKV_ERR_ARGUMENT;
+    *out = nullptr;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || device_id < 0 || device_id >= count)
+        return CKV_ERR_CUDA;
+    ckv_ctx* ctx = new ckv_ctx();
+    ctx->config = *config;
+    ctx->device = device_id;
+    // The reference constructor makes the device current (cuszp_wrapper.cpp:37).
+    cudaSetDevice(device_id);
+    *out = ctx;
+    return CKV_OK;
+}
+
+void ckv_destroy(ckv_ctx* ctx) {
+    if (!ctx) return;
+    {
+        DeviceGuard guard(ctx->device);
+        for (Slot& s : ctx->slots) {
+            if (s.pending) cudaEventSynchronize(s.done);
+            if (s.done) cudaEventDestroy(s.done);
+            cudaFreeHost(s.host);
+            cudaFree(s.dev);
+        }
+        cudaFreeHost(ctx->sizes);
+        cudaFreeHost(ctx->bounds);
+        cudaFreeHost(ctx->status);
+        cudaFree(ctx->dec_status);
+    }
+    delete ctx;
+}
+
+ckv_status ckv_get_config(const ckv_ctx* ctx, ckv_config* out) {
+    if (!ctx || !out) return CKV_ERR_ARGUMENT;
+    *out = ctx->config;
+    return CKV_OK;
+}
+
+ckv_status ckv_update_config(ckv_ctx* ctx, const ckv_config* config) {
+    if (!ctx || !config) return CKV_ERR_ARGUMENT;
+    ctx->config = *config;
+    return CKV_OK;
+}
+
+const char* ckv_last_error(const ckv_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+ckv_status ckv_set_zero_fill(ckv_ctx* ctx, int zero_fill) {
+    if (!ctx) return CKV_ERR_ARGUMENT;
+    ctx->zero_fill = zero_fill != 0;
+    return CKV_OK;
+}
+
+ckv_status ckv_device_status(ckv_ctx* ctx, void* stream, int reset, uint32_t* bits) {
+    if (!ctx || !bits) return CKV_ERR_ARGUMENT;
+    *bits = 0;
+    if (!ctx->dec_status) return CKV_OK;
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    std::vector<uint32_t> h(ctx->dec_status_cap);
+    cudaError_t e = cudaMemcpyAsync(h.data(), ctx->dec_status, h.size() * 4,
+                                    cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(ctx, "reading decode status", e);
+    for (uint32_t v : h) *bits |= v;
+    if (reset) {
+        e = cudaMemsetAsync(ctx->dec_status, 0, h.size() * 4, s);
+        if (e != cudaSuccess) return cuda_fail(ctx, "clearing decode status", e);
+    }
+    return CKV_OK;
+}
+
+ckv_status ckv_compress(ckv_ctx* ctx, const float* input, size_t n, uint8_t* out,
+                        size_t capacity, float eps_override, size_t* size, float* bound,
+                        void* stream) {
+    if (check_ctx(ctx)) return CKV_ERR_ARGUMENT;
+    ctx->err.clear();
+    if (!input || !out || !size || !bound || !fits_u32(n))
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid compress arguments");
+    if (ctx->config.processing_dim != CKV_DIM_1D || ctx->config.data_type != CKV_TYPE_FLOAT ||
+        ctx->config.encoding_mode != CKV_MODE_FIXED)
+        return fail(ctx, CKV_ERR_UNSUPPORTED,
+                    "only the fixed-mode 1D float codec is implemented (mode %d)",
+                    ctx->config.encoding_mode);
+    const float eps = eps_override > 0.0f ? eps_override : ctx->config.error_bound;
+    Batch b;
+    b.maps.push_back(identity_map());
+    b.max_n = static_cast<uint32_t>(n);
+    Unit u{};
+    u.elems = input;
+    u.stream = out;
+    u.capacity = capacity;
+    u.n = static_cast<uint32_t>(n);
+    u.eb = eps;
+    b.units.push_back(u);
+    return run_encode(ctx, b, ckv::ElemType::kF32, size, bound, stream);
+}
+
+ckv_status ckv_compress_batch_fixed(ckv_ctx* ctx, const float* const* inputs,
+                                    uint8_t* const* outputs, const float* eps, size_t batch,
+                                    size_t n, size_t capacity, size_t* sizes, float* bounds,
+                                    void* stream) {
+    return compress_batch(ctx, reinterpret_cast<const void* const*>(inputs), outputs, eps,
+                          batch, n, capacity, 4, sizes, bounds, stream, ckv::ElemType::kF32);
+}
+
+ckv_status ckv_compress_batch_fixed_bf16(ckv_ctx* ctx, const void* const* inputs,
+                                         uint8_t* const* outputs, const float* eps,
+                                         size_t batch, size_t n, size_t capacity,
+                                         size_t* sizes, float* bounds, void* stream) {
+    return compress_batch(ctx, inputs, outputs, eps, batch, n, capacity, 2, sizes, bounds,
+                          stream, ckv::ElemType::kBF16);
+}
+
+ckv_status ckv_compress_batch_fixed_bf16_indexed(
+    ckv_ctx* ctx, const void* const* inputs, uint8_t* const* outputs,
+    const int64_t* layer_indices, size_t selected, size_t prefix_count, size_t source_layers,
+    size_t elements_per_layer, const float* eps, size_t batch, size_t capacity, size_t* sizes,
+    float* bounds, void* stream) {
+    if (check_ctx(ctx)) return CKV_ERR_ARGUMENT;
+    std::vector<size_t> caps(batch, capacity);
+    const int64_t* const idx[1] = {layer_indices};
+    const size_t sel[1] = {selected};
+    const size_t group[1] = {batch};
+    return ckv_compress_batch_fixed_bf16_indexed_groups(
+        ctx, inputs, outputs, idx, sel, group, 1, prefix_count, source_layers,
+        elements_per_layer, eps, batch, caps.data(), sizes, bounds, stream);
+}
+
+ckv_status ckv_compress_batch_fixed_bf16_indexed_groups(
+    ckv_ctx* ctx, const void* const* inputs, uint8_t* const* outputs,
+    const int64_t* const* layer_indices, const size_t* selected, const size_t* group_sizes,
+    size_t groups, size_t prefix_count, size_t source_layers, size_t elements_per_layer,
+    const float* eps, size_t batch, const size_t* capacities, size_t* sizes, float* bounds,
+    void* stream) {
+    if (check_ctx(ctx)) return CKV_ERR_ARGUMENT;
+    ctx->err.clear();
+    if (batch == 0 || groups == 0 || !inputs || !outputs || !layer_indices || !selected ||
+        !group_sizes || !capacities || !sizes || !bounds || prefix_count == 0 ||
+        source_layers == 0 || elements_per_layer == 0)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid indexed compression arguments");
+    if (ckv_status s = check_fixed(ctx, "indexed compression")) return s;
+    Batch b;
+    size_t total = 0;
+    for (size_t g = 0; g < groups; ++g) {
+        if (group_sizes[g] == 0 || selected[g] == 0 || selected[g] > source_layers ||
+            !layer_indices[g])
+            return fail(ctx, CKV_ERR_ARGUMENT, "invalid layer group %zu", g);
+        total += group_sizes[g];
+    }
+    if (total != batch) return fail(ctx, CKV_ERR_ARGUMENT, "group sizes do not cover the batch");
+    b.units.reserve(batch);
+    size_t i = 0;
+    for (size_t g = 0; g < groups; ++g) {
+        const size_t n = prefix_count * selected[g] * elements_per_layer;
+        if (!fits_u32(n)) return fail(ctx, CKV_ERR_ARGUMENT, "group %zu too large", g);
+        b.maps.push_back(layers_map(layer_indices[g], selected[g], source_layers,
+                                    elements_per_layer));
+        b.max_n = std::max<uint32_t>(b.max_n, static_cast<uint32_t>(n));
+        for (size_t k = 0; k < group_sizes[g]; ++k, ++i) {
+            if (!inputs[i] || !outputs[i])
+                return fail(ctx, CKV_ERR_ARGUMENT, "null pointer for unit %zu", i);
+            if (reinterpret_cast<uintptr_t>(inputs[i]) & 1u)
+                return fail(ctx, CKV_ERR_ARGUMENT, "misaligned input page %zu", i);
+            if (capacities[i] < ckv_estimate_compressed_buffer_size(n * 4))
+                return fail(ctx, CKV_ERR_ARGUMENT, "output %zu capacity %zu below %zu bytes", i,
+                            capacities[i], ckv_estimate_compressed_buffer_size(n * 4));
+            Unit u{};
+            u.elems = inputs[i];
+            u.stream = outputs[i];
+            u.capacity = capacities[i];
+            u.n = static_cast<uint32_t>(n);
+            u.map = static_cast<uint32_t>(g);
+            u.eb = eps_of(ctx, eps, i);
+            b.units.push_back(u);
+        }
+    }
+    return run_encode(ctx, b, ckv::ElemType::kBF16, sizes, bounds, stream);
+}
+
+ckv_status ckv_decompress(ckv_ctx* ctx, const uint8_t* in, size_t size, float* out, size_t n,
+                          float bound, void* stream) {
+    if (check_ctx(ctx)) return CKV_ERR_ARGUMENT;
+    float* outs[1] = {out};
+    const uint8_t* ins[1] = {in};
+    const size_t sizes[1] = {size};
+    const size_t ns[1] = {n};
+    const float bounds[1] = {bound};
+    return ckv_decompress_batch(ctx, ins, sizes, outs, ns, bounds, 1, stream);
+}
+
+ckv_status ckv_decompress_batch(ckv_ctx* ctx, const uint8_t* const* ins, const size_t* sizes,
+                                float* const* outs, const size_t* n, const float* bounds,
+                                size_t batch, void* stream) {
+    if (check_ctx(ctx)) return CKV_ERR_ARGUMENT;
+    ctx->err.clear();
+    if (batch == 0) return CKV_OK;
+    if (!ins || !sizes || !outs || !n || !bounds)
+        return fail(ctx, CKV_ERR_ARGUMENT, "null decompression argument");
+    if (ctx->config.processing_dim != CKV_DIM_1D || ctx->config.data_type != CKV_TYPE_FLOAT ||
+        ctx->config.encoding_mode != CKV_MODE_FIXED)
+        return fail(ctx, CKV_ERR_UNSUPPORTED,
+                    "only the fixed-mode 1D float codec is implemented (mode %d)",
+                    ctx->config.encoding_mode);
+    if (ckv_status s = check_stream_ptrs(ctx, ins, sizes, batch)) return s;
+    Batch b;
+    b.maps.push_back(identity_map());
+    for (size_t i = 0; i < batch; ++i) {
+        if (!outs[i] || !fits_u32(n[i]) || (reinterpret_cast<uintptr_t>(outs[i]) & 3u))
+            return fail(ctx, CKV_ERR_ARGUMENT, "invalid output %zu", i);
+        Unit u{};
+        u.elems = outs[i];
+        u.stream = const_cast<uint8_t*>(ins[i]);
+        u.capacity = sizes[i];
+        u.n = static_cast<uint32_t>(n[i]);
+        u.eb = bounds[i];
+        b.units.push_back(u);
+        b.max_n = std::max<uint32_t>(b.max_n, u.n);
+    }
+    return run_decode(ctx, b, ckv::ElemType::kF32, stream);
+}
+
+ckv_status ckv_decompress_batch_fixed_bf16(ckv_ctx* ctx, const uint8_t* const* ins,
+                                           const size_t* sizes, size_t batch, void* out,
+                                           size_t out_numel, size_t n, const float* bounds,
+                                           void* stream) {
+    if (check_ctx(ctx)) return CKV_ERR_ARGUMENT;
+    ctx->err.clear();
+    if (batch == 0) return CKV_OK;
+    if (!ins || !sizes || !out || !bounds || !fits_u32(n) || out_numel < batch * n)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid cuSZp fixed BF16 batch metadata");
+    if (ckv_status s = check_fixed(ctx, "BF16 batch decompression")) return s;
+    if (ckv_status s = check_stream_ptrs(ctx, ins, sizes, batch)) return s;
+    if (reinterpret_cast<uintptr_t>(out) & 1u)
+        return fail(ctx, CKV_ERR_ARGUMENT, "misaligned BF16 output");
+    Batch b;
+    b.maps.push_back(identity_map());
+    b.max_n = static_cast<uint32_t>(n);
+    for (size_t i = 0; i < batch; ++i) {
+        Unit u{};
+        u.elems = static_cast<uint16_t*>(out) + i * n;
+        u.stream = const_cast<uint8_t*>(ins[i]);
+        u.capacity = sizes[i];
+        u.n = static_cast<uint32_t>(n);
+        u.eb = bounds[i];
+        b.units.push_back(u);
+    }
+    return run_decode(ctx, b, ckv::ElemType::kBF16, stream);
+}
+
+ckv_status ckv_decompress_batch_fixed_bf16_scatter(ckv_ctx* ctx, const uint8_t* const* ins,
+                                                   const size_t* sizes, size_t batch,
+                                                   void* const* outs, size_t out_count,
+                                                   size_t n, size_t per_page,
+                                                   size_t elements_per_dest,
+                                                   const float* bounds, void* stream) {
+    if (check_ctx(ctx)) return CKV_ERR_ARGUMENT;
+    ctx->err.clear();
+    if (batch == 0) return CKV_OK;
+    if (!ins || !sizes || !outs || !bounds || per_page == 0 || elements_per_dest == 0 ||
+        n != per_page * elements_per_dest || out_count != batch * per_page || !fits_u32(n))
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid cuSZp direct-scatter metadata");
+    if (ckv_status s = check_fixed(ctx, "direct scatter")) return s;
+    if (ckv_status s = check_stream_ptrs(ctx, ins, sizes, batch)) return s;
+    Batch b;
+    Map m{};
+    m.kind = ckv::kMapSplit;
+    m.run = static_cast<uint32_t>(elements_per_dest);
+    m.per_unit = static_cast<uint32_t>(per_page);
+    m.table = nullptr;  // offset 0 in the uploaded table
+    b.maps.push_back(m);
+    b.table.assign(outs, outs + out_count);
+    for (size_t k = 0; k < out_count; ++k)
+        if (!outs[k] || (reinterpret_cast<uintptr_t>(outs[k]) & 1u))
+            return fail(ctx, CKV_ERR_ARGUMENT, "invalid BF16 direct-scatter destination");
+    b.max_n = static_cast<uint32_t>(n);
+    for (size_t i = 0; i < batch; ++i) {
+        Unit u{};
+        u.elems = nullptr;
+        u.stream = const_cast<uint8_t*>(ins[i]);
+        u.capacity = sizes[i];
+        u.n = static_cast<uint32_t>(n);
+        u.eb = bounds[i];
+        b.units.push_back(u);
+    }
+    return run_decode(ctx, b, ckv::ElemType::kBF16, stream);
+}
+
+ckv_status ckv_decompress_batch_fixed_bf16_indexed_scatter(
+    ckv_ctx* ctx, const uint8_t* const* ins, const size_t* sizes, size_t batch,
+    void* const* outs, const int64_t* layer_indices, size_t selected, size_t prefix_count,
+    size_t source_layers, size_t elements_per_layer, const float* bounds, void* stream) {
+    if (check_ctx(ctx)) return CKV_ERR_ARGUMENT;
+    ctx->err.clear();
+    if (batch == 0) return CKV_OK;
+    if (!ins || !sizes || !outs || !bounds || !layer_indices || prefix_count == 0 ||
+        source_layers == 0 || elements_per_layer == 0 || selected == 0 ||
+        selected > source_layers)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid indexed scatter arguments");
+    if (ckv_status s = check_fixed(ctx, "indexed scatter")) return s;
+    if (ckv_status s = check_stream_ptrs(ctx, ins, sizes, batch)) return s;
+    const size_t n = prefix_count * selected * elements_per_layer;
+    if (!fits_u32(n)) return fail(ctx, CKV_ERR_ARGUMENT, "unit too large");
+    Batch b;
+    b.maps.push_back(layers_map(layer_indices, selected, source_layers, elements_per_layer));
+    b.max_n = static_cast<uint32_t>(n);
+    for (size_t i = 0; i < batch; ++i) {
+        if (!outs[i] || (reinterpret_cast<uintptr_t>(outs[i]) & 1u))
+            return fail(ctx, CKV_ERR_ARGUMENT, "invalid indexed destination %zu", i);
+        Unit u{};
+        u.elems = outs[i];
+        u.stream = const_cast<uint8_t*>(ins[i]);
+        u.capacity = sizes[i];
+        u.n = static_cast<uint32_t>(n);
+        u.eb = bounds[i];
+        b.units.push_back(u);
+    }
+    return run_decode(ctx, b, ckv::ElemType::kBF16, stream);
+}
+
+}  // extern "C"

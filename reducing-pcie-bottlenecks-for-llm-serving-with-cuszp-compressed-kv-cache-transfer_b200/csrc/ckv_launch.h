@@ -1,0 +1,46 @@
+// Host-side launch interface between the C-ABI layer and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "ckv_device.cuh"
+
+namespace ckv {
+
+enum class ElemType { kBF16 = 0, kF32 = 1 };
+
+struct EncodeLaunch {
+    const Unit* units;         // device
+    const Map* maps;           // device
+    uint32_t num_units;
+    uint32_t max_n;            // largest unit (elements)
+    bool relative;
+    uint64_t* sizes;           // device-visible, one per unit
+    float* bounds;             // device-visible, one per unit
+    uint32_t* status;          // device-visible, one per unit
+    ElemType type;
+};
+
+struct DecodeLaunch {
+    const Unit* units;         // device
+    const Map* maps;           // device
+    uint32_t num_units;
+    uint32_t max_n;
+    bool zero_fill;            // write rate-0 blocks (the reference skips them)
+    uint32_t* status;          // device-visible, one per unit
+    ElemType type;             // destination element type
+};
+
+// Largest unit (elements) the single-pass clustered encoder accepts.
+uint32_t encode_max_elements(ElemType type);
+
+// Enqueue on `stream`; returns cudaSuccess or the launch error.
+cudaError_t launch_encode(const EncodeLaunch& l, cudaStream_t stream);
+cudaError_t launch_decode(const DecodeLaunch& l, cudaStream_t stream);
+
+// Kernel launches made since load (tests and bench count them).
+uint64_t launches_issued();
+void note_launch();
+
+}  // namespace ckv
