@@ -177,6 +177,23 @@ CKV_API ckv_status ckv_set_zero_fill(ckv_ctx* ctx, int zero_fill);
 #define CKV_DEV_TIMEOUT 8u
 CKV_API ckv_status ckv_device_status(ckv_ctx* ctx, void* stream, int reset, uint32_t* bits);
 
+/* Gather `count` compressed units (device pointers srcs[i], sizes[i] bytes)
+ * into the device slab `dst` (capacity bytes), unit i starting at
+ * offsets[i] = previous end rounded up to `align` bytes (a power of two,
+ * >= 4).  Writes the offsets to the host array and the slab's used length
+ * to *total.  One launch; asynchronous on `stream`.  The reference does
+ * this with torch.cat (vllm_v1_compressed_offload.py:403-427). */
+CKV_API ckv_status ckv_pack(ckv_ctx* ctx, const uint8_t* const* srcs, const size_t* sizes,
+                            size_t count, uint8_t* dst, size_t capacity, size_t align,
+                            size_t* offsets, size_t* total, void* stream);
+
+/* Record CUDA events immediately around every kernel this context launches
+ * (on the launch stream).  ckv_kernel_time returns the device duration of
+ * the last launch of the given kind (0 encode, 1 decode, 2 pack), in
+ * milliseconds, waiting for it to finish. */
+CKV_API ckv_status ckv_set_kernel_timing(ckv_ctx* ctx, int enable);
+CKV_API ckv_status ckv_kernel_time(ckv_ctx* ctx, int kind, float* ms);
+
 /* Number of kernel launches libckv has issued since it was loaded. */
 CKV_API uint64_t ckv_kernel_launches(void);
 

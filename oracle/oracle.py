@@ -262,7 +262,7 @@ class RefKernels:
         lib.ref_compress_bf16.argtypes = [
             c_void_p, c_void_p, c_size, c_size, c_size, c_void_p, c_int,
             c_void_p, c_size, c_size, c_size, c_size, c_void_p, c_void_p,
-            c_void_p]
+            c_void_p, c_int]
         lib.ref_decompress_bf16.restype = c_int
         lib.ref_decompress_bf16.argtypes = [
             c_void_p, c_size, c_size, c_void_p, c_int, c_void_p, c_size, c_size,
@@ -271,7 +271,8 @@ class RefKernels:
 
     def compress(self, input_ptrs, output_ptrs, capacity, n, eps, relative=True,
                  layer_indices_ptr=None, selected=0, prefix_count=0,
-                 source_layers=0, elements_per_layer=0, stream=0):
+                 source_layers=0, elements_per_layer=0, stream=0,
+                 zero_outputs=True):
         batch = len(input_ptrs)
         ip = (c_void_p * batch)(*input_ptrs)
         op = (c_void_p * batch)(*output_ptrs)
@@ -281,7 +282,8 @@ class RefKernels:
         rc = self.lib.ref_compress_bf16(
             ip, op, capacity, batch, n, e.ctypes.data, int(relative),
             layer_indices_ptr, selected, prefix_count, source_layers,
-            elements_per_layer, sizes.ctypes.data, bounds.ctypes.data, stream)
+            elements_per_layer, sizes.ctypes.data, bounds.ctypes.data, stream,
+            int(zero_outputs))
         if rc != 0:
             raise RuntimeError(f"reference compress failed ({rc})")
         return sizes, bounds

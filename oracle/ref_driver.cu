@@ -108,6 +108,8 @@ extern "C" {
 
 // Compress `batch` BF16 pages (device pointers in host array `inputs`) into
 // `outputs` (device pointers, capacity `out_capacity` bytes each).
+// zero_outputs != 0 clears the outputs first (golden generation); the
+// reference wrapper does not, and neither does the benchmark.
 // layer_indices == nullptr selects the plain kernel; otherwise the indexed
 // kernel over `selected` layers.  eps[i] is the requested bound per page.
 // Writes sizes and resolved bounds to host arrays.  Returns 0 on success.
@@ -117,15 +119,16 @@ int ref_compress_bf16(const void* const* inputs, unsigned char* const* outputs,
                       const int64_t* layer_indices, size_t selected,
                       size_t prefix_count, size_t source_layers,
                       size_t elements_per_layer, size_t* sizes,
-                      float* bounds, void* stream_ptr) {
+                      float* bounds, void* stream_ptr, int zero_outputs) {
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     size_t logical = layer_indices
         ? prefix_count * selected * elements_per_layer : n;
     size_t g = groups_of(logical);
     size_t entries = (g + 1) * batch;
     if (!g_ws.reserve(entries, batch, batch)) return 1;
-    for (size_t i = 0; i < batch; ++i)
-        cudaMemsetAsync(outputs[i], 0, out_capacity, stream);
+    if (zero_outputs)
+        for (size_t i = 0; i < batch; ++i)
+            cudaMemsetAsync(outputs[i], 0, out_capacity, stream);
     cudaMemcpyAsync(g_ws.ptrs_a, inputs, batch * sizeof(void*),
                     cudaMemcpyHostToDevice, stream);
     cudaMemcpyAsync(g_ws.ptrs_b, outputs, batch * sizeof(void*),

@@ -41,7 +41,8 @@ EXPORTS = (
     "ckv_decompress_batch", "ckv_decompress_batch_fixed_bf16",
     "ckv_decompress_batch_fixed_bf16_scatter",
     "ckv_decompress_batch_fixed_bf16_indexed_scatter", "ckv_set_zero_fill",
-    "ckv_device_status", "ckv_kernel_launches",
+    "ckv_device_status", "ckv_kernel_launches", "ckv_pack",
+    "ckv_set_kernel_timing", "ckv_kernel_time",
 )
 
 
@@ -91,6 +92,9 @@ def _declare(lib: C.CDLL) -> None:
         "ckv_set_zero_fill": (c_status, [P, c_int]),
         "ckv_device_status": (c_status, [P, P, c_int, C.POINTER(C.c_uint32)]),
         "ckv_kernel_launches": (C.c_uint64, []),
+        "ckv_pack": (c_status, [P, P, P, c_size, P, c_size, c_size, P, P, P]),
+        "ckv_set_kernel_timing": (c_status, [P, c_int]),
+        "ckv_kernel_time": (c_status, [P, c_int, C.POINTER(c_float)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

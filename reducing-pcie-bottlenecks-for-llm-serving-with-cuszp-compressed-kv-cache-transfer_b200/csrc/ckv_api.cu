@@ -65,6 +65,11 @@ struct ckv_ctx {
     // decode status words (device), accumulated until read
     uint32_t* dec_status = nullptr;
     size_t dec_status_cap = 0;
+    // optional kernel timing (encode, decode, pack)
+    bool timing = false;
+    cudaEvent_t t_start[3] = {nullptr, nullptr, nullptr};
+    cudaEvent_t t_stop[3] = {nullptr, nullptr, nullptr};
+    bool t_valid[3] = {false, false, false};
 };
 
 namespace {
@@ -108,14 +113,9 @@ struct Batch {
     uint32_t max_n = 0;
 };
 
-// Copies the batch to the device through the next staging slot; patches
-// map table pointers to their device addresses.
-ckv_status upload(ckv_ctx* ctx, Batch& b, cudaStream_t stream, Slot** used,
-                  const Unit** d_units, const Map** d_maps) {
-    const size_t units_bytes = align16(b.units.size() * sizeof(Unit));
-    const size_t maps_bytes = align16(b.maps.size() * sizeof(Map));
-    const size_t table_bytes = align16(b.table.size() * sizeof(void*));
-    const size_t need = units_bytes + maps_bytes + table_bytes;
+// Next staging slot with at least `need` bytes, once its previous upload
+// and the kernel that read it have finished.
+ckv_status acquire_slot(ckv_ctx* ctx, size_t need, Slot** out) {
     Slot& s = ctx->slots[ctx->next_slot];
     ctx->next_slot = (ctx->next_slot + 1) % kSlots;
     if (s.pending) {
@@ -140,6 +140,21 @@ ckv_status upload(ckv_ctx* ctx, Batch& b, cudaStream_t stream, Slot** used,
         if (e != cudaSuccess) return cuda_fail(ctx, "allocating device descriptors", e);
         s.cap = cap;
     }
+    *out = &s;
+    return CKV_OK;
+}
+
+// Copies the batch to the device through the next staging slot; patches
+// map table pointers to their device addresses.
+ckv_status upload(ckv_ctx* ctx, Batch& b, cudaStream_t stream, Slot** used,
+                  const Unit** d_units, const Map** d_maps) {
+    const size_t units_bytes = align16(b.units.size() * sizeof(Unit));
+    const size_t maps_bytes = align16(b.maps.size() * sizeof(Map));
+    const size_t table_bytes = align16(b.table.size() * sizeof(void*));
+    const size_t need = units_bytes + maps_bytes + table_bytes;
+    Slot* sp = nullptr;
+    if (ckv_status st = acquire_slot(ctx, need, &sp)) return st;
+    Slot& s = *sp;
     uint8_t* h = s.host;
     void** table_dev = reinterpret_cast<void**>(s.dev + units_bytes + maps_bytes);
     for (Map& m : b.maps)
@@ -157,8 +172,26 @@ ckv_status upload(ckv_ctx* ctx, Batch& b, cudaStream_t stream, Slot** used,
     return CKV_OK;
 }
 
+// Kernel timing: events recorded right around a launch when enabled.
+void timing_begin(ckv_ctx* ctx, int kind, cudaStream_t stream);
+void timing_end(ckv_ctx* ctx, int kind, cudaStream_t stream);
+
 void release(Slot* s, cudaStream_t stream) {
     if (s && cudaEventRecord(s->done, stream) == cudaSuccess) s->pending = true;
+}
+
+void timing_begin(ckv_ctx* ctx, int kind, cudaStream_t stream) {
+    if (!ctx->timing) return;
+    if (!ctx->t_start[kind]) {
+        cudaEventCreate(&ctx->t_start[kind]);
+        cudaEventCreate(&ctx->t_stop[kind]);
+    }
+    cudaEventRecord(ctx->t_start[kind], stream);
+}
+
+void timing_end(ckv_ctx* ctx, int kind, cudaStream_t stream) {
+    if (!ctx->timing) return;
+    ctx->t_valid[kind] = cudaEventRecord(ctx->t_stop[kind], stream) == cudaSuccess;
 }
 
 ckv_status ensure_results(ckv_ctx* ctx, size_t count) {
@@ -244,7 +277,9 @@ ckv_status run_encode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, size_t* sizes,
     l.bounds = ctx->bounds;
     l.status = ctx->status;
     l.type = type;
+    timing_begin(ctx, 0, stream);
     cudaError_t e = ckv::launch_encode(l, stream);
+    timing_end(ctx, 0, stream);
     release(slot, stream);
     if (e != cudaSuccess) return cuda_fail(ctx, "encode launch", e);
     e = cudaStreamSynchronize(stream);
@@ -277,7 +312,9 @@ ckv_status run_decode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, void* stream_p
     l.zero_fill = ctx->zero_fill;
     l.status = ctx->dec_status;
     l.type = type;
+    timing_begin(ctx, 1, stream);
     cudaError_t e = ckv::launch_decode(l, stream);
+    timing_end(ctx, 1, stream);
     release(slot, stream);
     if (e != cudaSuccess) return cuda_fail(ctx, "decode launch", e);
     return CKV_OK;
@@ -403,6 +440,10 @@ void ckv_destroy(ckv_ctx* ctx) {
         cudaFreeHost(ctx->bounds);
         cudaFreeHost(ctx->status);
         cudaFree(ctx->dec_status);
+        for (int k = 0; k < 3; ++k) {
+            if (ctx->t_start[k]) cudaEventDestroy(ctx->t_start[k]);
+            if (ctx->t_stop[k]) cudaEventDestroy(ctx->t_stop[k]);
+        }
     }
     delete ctx;
 }
@@ -692,6 +733,61 @@ ckv_status ckv_decompress_batch_fixed_bf16_indexed_scatter(
         b.units.push_back(u);
     }
     return run_decode(ctx, b, ckv::ElemType::kBF16, stream);
+}
+
+ckv_status ckv_pack(ckv_ctx* ctx, const uint8_t* const* srcs, const size_t* sizes, size_t count,
+                    uint8_t* dst, size_t capacity, size_t align, size_t* offsets, size_t* total,
+                    void* stream_ptr) {
+    if (check_ctx(ctx)) return CKV_ERR_ARGUMENT;
+    ctx->err.clear();
+    if (!srcs || !sizes || !dst || !offsets || !total || align < 4 || (align & (align - 1)))
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid pack arguments");
+    *total = 0;
+    if (count == 0) return CKV_OK;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    DeviceGuard guard(ctx->device);
+    Slot* slot = nullptr;
+    if (ckv_status st = acquire_slot(ctx, count * sizeof(ckv::PackUnit), &slot)) return st;
+    auto* units = reinterpret_cast<ckv::PackUnit*>(slot->host);
+    uint64_t pos = 0, max_size = 0;
+    for (size_t i = 0; i < count; ++i) {
+        if (!srcs[i]) return fail(ctx, CKV_ERR_ARGUMENT, "null source %zu", i);
+        pos = (pos + align - 1) & ~static_cast<uint64_t>(align - 1);
+        units[i] = ckv::PackUnit{srcs[i], sizes[i], pos};
+        offsets[i] = static_cast<size_t>(pos);
+        pos += sizes[i];
+        max_size = std::max<uint64_t>(max_size, sizes[i]);
+    }
+    if (pos > capacity)
+        return fail(ctx, CKV_ERR_CAPACITY, "packed size %llu exceeds capacity %zu",
+                    static_cast<unsigned long long>(pos), capacity);
+    *total = static_cast<size_t>(pos);
+    cudaError_t e = cudaMemcpyAsync(slot->dev, slot->host, count * sizeof(ckv::PackUnit),
+                                    cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, "uploading pack descriptors", e);
+    timing_begin(ctx, 2, stream);
+    e = ckv::launch_pack(reinterpret_cast<const ckv::PackUnit*>(slot->dev),
+                         static_cast<uint32_t>(count), max_size, dst, stream);
+    timing_end(ctx, 2, stream);
+    release(slot, stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, "pack launch", e);
+    return CKV_OK;
+}
+
+ckv_status ckv_set_kernel_timing(ckv_ctx* ctx, int enable) {
+    if (!ctx) return CKV_ERR_ARGUMENT;
+    ctx->timing = enable != 0;
+    return CKV_OK;
+}
+
+ckv_status ckv_kernel_time(ckv_ctx* ctx, int kind, float* ms) {
+    if (!ctx || !ms || kind < 0 || kind > 2) return CKV_ERR_ARGUMENT;
+    if (!ctx->t_valid[kind]) return fail(ctx, CKV_ERR_ARGUMENT, "no timed launch of kind %d", kind);
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = cudaEventSynchronize(ctx->t_stop[kind]);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(ms, ctx->t_start[kind], ctx->t_stop[kind]);
+    if (e != cudaSuccess) return cuda_fail(ctx, "reading kernel time", e);
+    return CKV_OK;
 }
 
 }  // extern "C"

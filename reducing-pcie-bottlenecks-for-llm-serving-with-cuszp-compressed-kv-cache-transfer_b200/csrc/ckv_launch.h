@@ -32,12 +32,20 @@ struct DecodeLaunch {
     ElemType type;             // destination element type
 };
 
+struct PackUnit {
+    const uint8_t* src;
+    uint64_t size;
+    uint64_t offset;           // byte offset in the destination slab
+};
+
 // Largest unit (elements) the single-pass clustered encoder accepts.
 uint32_t encode_max_elements(ElemType type);
 
 // Enqueue on `stream`; returns cudaSuccess or the launch error.
 cudaError_t launch_encode(const EncodeLaunch& l, cudaStream_t stream);
 cudaError_t launch_decode(const DecodeLaunch& l, cudaStream_t stream);
+cudaError_t launch_pack(const PackUnit* units, uint32_t count, uint64_t max_size,
+                        uint8_t* dst, cudaStream_t stream);
 
 // Kernel launches made since load (tests and bench count them).
 uint64_t launches_issued();
