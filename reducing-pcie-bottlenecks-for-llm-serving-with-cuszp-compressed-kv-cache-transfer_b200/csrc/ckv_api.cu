@@ -297,6 +297,13 @@ ckv_status run_decode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, void* stream_p
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     DeviceGuard guard(ctx->device);
     const size_t count = b.units.size();
+    uint32_t items = 0;
+    bool uniform = true;
+    for (Unit& u : b.units) {
+        u.item0 = items;
+        items += ckv::decode_items(u.n);
+        uniform = uniform && u.n == b.units[0].n;
+    }
     ckv_status st = ensure_dec_status(ctx, count);
     if (st != CKV_OK) return st;
     Slot* slot = nullptr;
@@ -305,6 +312,8 @@ ckv_status run_decode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, void* stream_p
     st = upload(ctx, b, stream, &slot, &d_units, &d_maps);
     if (st != CKV_OK) return st;
     ckv::DecodeLaunch l{};
+    l.total_items = items;
+    l.uniform_items = uniform ? ckv::decode_items(b.units[0].n) : 0u;
     l.units = d_units;
     l.maps = d_maps;
     l.num_units = static_cast<uint32_t>(count);

@@ -59,7 +59,7 @@ struct Unit {
     uint32_t n;
     uint32_t map;              // index into the launch's map table
     float eb;                  // encode: requested bound; decode: absolute bound
-    uint32_t pad;
+    uint32_t item0;            // decode: index of the unit's first work item
 };
 
 // ---------------------------------------------------------------------------

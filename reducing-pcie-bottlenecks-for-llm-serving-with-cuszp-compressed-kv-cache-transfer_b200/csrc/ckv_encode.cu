@@ -13,13 +13,21 @@
 //      eb = eps * fmaxf(max - min, 1e-6f) (cuszp_batched_fixed.cu:55-133);
 //   4. per block rate = bit length of max(|q(block min)|, |q(block max)|)
 //      -- the quantiser is monotone, so the extremes give the block's
-//      largest |q| (NaN contributes |q| = 1) -- then the CTAs exchange
-//      their slice byte totals -> each CTA knows where its output starts;
-//      no look-back chain, no global scratch;
-//   5. per block: quantise the 32 values, transpose them into the sign word
-//      and bit planes in registers, stage the round's output in shared
-//      memory and write it back with a TMA bulk store (plain stores for the
-//      unaligned head and tail words).
+//      largest |q| (NaN contributes |q| = 1) -- one CTA scan gives every
+//      block's payload offset, and the CTAs exchange their slice byte totals
+//      -> each CTA knows where its output starts; no look-back chain, no
+//      global scratch;
+//   5. per round of 256 blocks (one per thread): quantise the 32 values,
+//      transpose them into the sign word and bit planes in registers, and
+//      write them IN PLACE over the already consumed input in shared memory
+//      (a block of rate <= 15 packs into at most the 64 bytes it came from);
+//      at the end one TMA bulk store writes the slice's payload.
+//
+// Rate <= 15 blocks without NaN (every block at REL bounds >= 1e-5 on
+// two-sided data) use a quantiser that truncates with a round-toward-zero
+// add of 2^23 instead of a float->int conversion; it gives the reference's
+// integer for |q| < 2^15.  Other blocks use the reference's exact
+// instruction sequence and are written straight to global memory.
 //
 // The rate found in step 5 from the values themselves is checked against
 // the one from step 4; a mismatch sets kErrRateCheck.
@@ -35,31 +43,33 @@ namespace ckv {
 namespace {
 
 constexpr uint32_t kSliceBytes = 64 * 1024;
-constexpr uint32_t kStageCap = 16384 + 16;
+constexpr uint32_t kGuard = 16;     // in-place output may start up to 15 bytes early
 constexpr uint32_t kMaxCluster = 16;
 constexpr uint32_t kWaitPolls = 1u << 24;
 constexpr uint32_t kMaxPieces = 512;
+constexpr uint8_t kNanFlag = 0x80;
 
 template <typename T>
 struct Traits;
 template <>
 struct Traits<__nv_bfloat16> {
     static constexpr uint32_t kBytes = 2;
+    static constexpr int kWords = 16;   // 32-bit words per block
 };
 template <>
 struct Traits<float> {
     static constexpr uint32_t kBytes = 4;
+    static constexpr int kWords = 32;
 };
 
 template <typename T>
 struct Layout {
     static constexpr uint32_t kBlocks = kSliceBytes / (kBlock * Traits<T>::kBytes);
-    static constexpr uint32_t kSlice = 0;
-    static constexpr uint32_t kMinMax = kSliceBytes;
-    static constexpr uint32_t kRates = kMinMax + kBlocks * 8;
-    static constexpr uint32_t kStageStride = (kStageCap + 15) / 16 * 16;
-    static constexpr uint32_t kStage = kRates + (kBlocks + 15) / 16 * 16;
-    static constexpr uint32_t kTotal = kStage + 2 * kStageStride;
+    static constexpr uint32_t kRounds = kBlocks / kThreads;
+    static constexpr uint32_t kSlice = kGuard;
+    static constexpr uint32_t kExtremes = kGuard + kSliceBytes;   // 4 KB either type
+    static constexpr uint32_t kRates = kExtremes + 4096;
+    static constexpr uint32_t kTotal = kRates + (kBlocks + 15) / 16 * 16;
 };
 
 struct EncodeArgs {
@@ -72,14 +82,15 @@ struct EncodeArgs {
     uint32_t* status;
 };
 
+// ---- slice load ------------------------------------------------------------
+
 // Thread 0: plan the slice load [e0, e1) as bulk copies of 16-byte aligned
 // runs.  Returns false when some run cannot be bulk-copied (then every
 // element is copied by the threads).  *tail is the first element of the
 // sub-16-byte tail that the threads copy.
 template <typename T>
-__device__ bool plan_and_issue_load(const Unit& unit, const Map& m, uint32_t u,
-                                    uint32_t e0, uint32_t e1, uint8_t* slice,
-                                    uint64_t* bar, uint32_t* tail) {
+__device__ bool plan_and_issue_load(const Unit& unit, const Map& m, uint32_t u, uint32_t e0,
+                                    uint32_t e1, uint8_t* slice, uint64_t* bar, uint32_t* tail) {
     constexpr uint32_t B = Traits<T>::kBytes;
     const uint32_t L = run_len(unit, m);
     uint32_t total = 0, pieces = 0;
@@ -118,9 +129,8 @@ __device__ bool plan_and_issue_load(const Unit& unit, const Map& m, uint32_t u,
 }
 
 template <typename T>
-__device__ void copy_elements(const Unit& unit, const Map& m, uint32_t u,
-                              uint32_t from, uint32_t to, uint32_t e0,
-                              uint8_t* slice) {
+__device__ void copy_elements(const Unit& unit, const Map& m, uint32_t u, uint32_t from,
+                              uint32_t to, uint32_t e0, uint8_t* slice) {
     const uint32_t L = run_len(unit, m);
     T* dst = reinterpret_cast<T*>(slice);
     for (uint32_t i = from + threadIdx.x; i < to; i += kThreads) {
@@ -129,29 +139,143 @@ __device__ void copy_elements(const Unit& unit, const Map& m, uint32_t u,
     }
 }
 
-// ---- per-block extremes ---------------------------------------------------
+// ---- one block in registers ------------------------------------------------
 
-// rho rotates which 16-byte chunk a thread reads first, so that the eight
-// threads of a shared-memory phase hit eight different bank groups.
-__device__ __forceinline__ void block_extremes(const uint8_t* blk, int rho,
-                                               float& lo, float& hi, bool& nan,
-                                               __nv_bfloat16) {
+// The words of one block.  rho rotates which 8-element byte lane a thread
+// reads first, so that the eight threads of a shared-memory phase hit eight
+// different bank groups; register element e = 8*j + u holds block element
+// 8*((j + rho) & 3) + u.
+template <typename T>
+__device__ __forceinline__ void load_block(const uint8_t* blk, int rho,
+                                           uint32_t (&w)[Traits<T>::kWords]) {
     const uint4* p = reinterpret_cast<const uint4*>(blk);
-    __nv_bfloat162 w[16];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const uint4 c = p[(j + rho) & 3];
-        w[4 * j + 0] = *reinterpret_cast<const __nv_bfloat162*>(&c.x);
-        w[4 * j + 1] = *reinterpret_cast<const __nv_bfloat162*>(&c.y);
-        w[4 * j + 2] = *reinterpret_cast<const __nv_bfloat162*>(&c.z);
-        w[4 * j + 3] = *reinterpret_cast<const __nv_bfloat162*>(&c.w);
+        const int c = (j + rho) & 3;
+        if constexpr (sizeof(T) == 2) {
+            const uint4 a = p[c];
+            w[4 * j + 0] = a.x;
+            w[4 * j + 1] = a.y;
+            w[4 * j + 2] = a.z;
+            w[4 * j + 3] = a.w;
+        } else {
+            const uint4 a = p[2 * c], b = p[2 * c + 1];
+            w[8 * j + 0] = a.x;
+            w[8 * j + 1] = a.y;
+            w[8 * j + 2] = a.z;
+            w[8 * j + 3] = a.w;
+            w[8 * j + 4] = b.x;
+            w[8 * j + 5] = b.y;
+            w[8 * j + 6] = b.z;
+            w[8 * j + 7] = b.w;
+        }
     }
+}
+
+template <typename T>
+__device__ __forceinline__ float elem(const uint32_t (&w)[Traits<T>::kWords], int e) {
+    if constexpr (sizeof(T) == 2)
+        return (e & 1) ? bf16_hi(w[e >> 1]) : bf16_lo(w[e >> 1]);
+    else
+        return __uint_as_float(w[e]);
+}
+
+__device__ __forceinline__ bool masked(int e, int rho, uint32_t valid) {
+    return static_cast<uint32_t>(8 * (((e >> 3) + rho) & 3) + (e & 7)) >= valid;
+}
+
+// (|q| << 1) | sign for |q| < 2^15 and no NaN: truncation by a
+// round-toward-zero add of 2^23 (exact for |t| < 2^23), the rest as
+// batch_quantization (cuszp_batched_fixed.cu:10-25).
+__device__ __forceinline__ uint32_t narrow_row(float x, float recip) {
+    const float r = __fmul_rn(x, recip);
+    const float t = __fadd_rn(r, 0.5f);
+    const float z = __fadd_rz(fabsf(t), 8388608.0f);
+    const uint32_t twice = (__float_as_uint(z) << 1) - 0x96000000u;  // 2 * trunc(|t|)
+    return r >= -0.5f ? twice : twice + 3u;  // |q| = trunc(|t|) + s, sign = s
+}
+
+// Rows of the 16x32 bit matrix for a narrow block: A[k] holds rows k and
+// k + 16, then the transpose turns them into the sign word (A[0]) and the
+// planes (A[1 + b]).  Elements past the end of the unit were set to +0 in
+// shared memory, which quantises to 0 for a finite 0.5 / eb.  Returns the
+// OR of all rows.
+template <typename T>
+__device__ __forceinline__ uint32_t narrow_block(const uint32_t (&w)[Traits<T>::kWords],
+                                                 float recip, uint32_t (&A)[16]) {
+    uint32_t orv = 0;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const int e = bitpos(k);
+        const uint32_t lo = narrow_row(elem<T>(w, e), recip);
+        const uint32_t hi = narrow_row(elem<T>(w, e + 16), recip);
+        orv |= lo | hi;
+        A[k] = __byte_perm(lo, hi, 0x5410);
+    }
+    transpose16(A);
+    return orv;
+}
+
+// Exact quantiser (the reference's instruction sequence) for one element.
+template <typename T>
+__device__ __forceinline__ int exact_q(const uint32_t (&w)[Traits<T>::kWords], int e, int rho,
+                                       float recip, uint32_t valid) {
+    if (valid < kBlock && masked(e, rho, valid)) return 0;
+    return quantize(elem<T>(w, e), recip);
+}
+
+// Any block: sign word and `rate` planes to out[0..rate] (nothing for rate
+// 0), two 16-row transposes (low and high halves of |q|).  Returns the OR
+// of |q|.
+template <typename T>
+__device__ __forceinline__ uint32_t wide_block(const uint32_t (&w)[Traits<T>::kWords], int rho,
+                                               float recip, uint32_t valid, uint32_t rate,
+                                               uint32_t* out) {
+    const uint32_t sh = 8u * rho;
+    uint32_t sign = 0, orv = 0;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        uint32_t A[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const int e = bitpos(k);
+            const int q1 = exact_q<T>(w, e, rho, recip, valid);
+            const int q2 = exact_q<T>(w, e + 16, rho, recip, valid);
+            const uint32_t a1 = uabs(q1), a2 = uabs(q2);
+            if (half == 0) {
+                sign |= (static_cast<uint32_t>(q1) >> 31) << k;
+                sign |= (static_cast<uint32_t>(q2) >> 31) << (k + 16);
+                orv |= a1 | a2;
+                A[k] = __byte_perm(a1, a2, 0x5410);
+            } else {
+                A[k] = __byte_perm(a1, a2, 0x7632);
+            }
+        }
+        transpose16(A);
+#pragma unroll
+        for (int b = 0; b < 16; ++b)
+            if (16 * half + b < static_cast<int>(rate))
+                out[1 + 16 * half + b] = __funnelshift_l(A[b], A[b], sh);
+    }
+    if (rate) out[0] = __funnelshift_l(sign, sign, sh);
+    return orv;
+}
+
+template <typename T>
+__device__ __forceinline__ void block_extremes(const uint32_t (&w)[Traits<T>::kWords], float& lo,
+                                               float& hi, bool& nan);
+
+template <>
+__device__ __forceinline__ void block_extremes<__nv_bfloat16>(const uint32_t (&w)[16], float& lo,
+                                                              float& hi, bool& nan) {
     __nv_bfloat162 mn[8], mx[8], mz[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        mn[k] = __hmin2(w[2 * k], w[2 * k + 1]);
-        mx[k] = __hmax2(w[2 * k], w[2 * k + 1]);
-        mz[k] = __hmax2_nan(w[2 * k], w[2 * k + 1]);
+        const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&w[2 * k]);
+        const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[2 * k + 1]);
+        mn[k] = __hmin2(a, b);
+        mx[k] = __hmax2(a, b);
+        mz[k] = __hmax2_nan(a, b);
     }
 #pragma unroll
     for (int s = 4; s >= 1; s >>= 1) {
@@ -174,30 +298,16 @@ __device__ __forceinline__ float nanmax(float a, float b) {
     return r;
 }
 
-__device__ __forceinline__ void block_extremes(const uint8_t* blk, int rho,
-                                               float& lo, float& hi, bool& nan,
-                                               float) {
-    const uint4* p = reinterpret_cast<const uint4*>(blk);
-    float x[32];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int c = (j + rho) & 3;
-        const uint4 a = p[2 * c], b = p[2 * c + 1];
-        x[8 * j + 0] = __uint_as_float(a.x);
-        x[8 * j + 1] = __uint_as_float(a.y);
-        x[8 * j + 2] = __uint_as_float(a.z);
-        x[8 * j + 3] = __uint_as_float(a.w);
-        x[8 * j + 4] = __uint_as_float(b.x);
-        x[8 * j + 5] = __uint_as_float(b.y);
-        x[8 * j + 6] = __uint_as_float(b.z);
-        x[8 * j + 7] = __uint_as_float(b.w);
-    }
+template <>
+__device__ __forceinline__ void block_extremes<float>(const uint32_t (&w)[32], float& lo,
+                                                      float& hi, bool& nan) {
     float mn[16], mx[16], mz[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
-        mn[k] = fminf(x[2 * k], x[2 * k + 1]);
-        mx[k] = fmaxf(x[2 * k], x[2 * k + 1]);
-        mz[k] = nanmax(x[2 * k], x[2 * k + 1]);
+        const float a = __uint_as_float(w[2 * k]), b = __uint_as_float(w[2 * k + 1]);
+        mn[k] = fminf(a, b);
+        mx[k] = fmaxf(a, b);
+        mz[k] = nanmax(a, b);
     }
 #pragma unroll
     for (int s = 8; s >= 1; s >>= 1) {
@@ -214,120 +324,39 @@ __device__ __forceinline__ void block_extremes(const uint8_t* blk, int rho,
 }
 
 template <typename T>
-__device__ __forceinline__ float elem_value(const uint8_t* blk, int v) {
-    if constexpr (sizeof(T) == 2) {
-        const uint16_t b = reinterpret_cast<const uint16_t*>(blk)[v];
-        return __uint_as_float(static_cast<uint32_t>(b) << 16);
-    } else {
+__device__ __forceinline__ float elem_at(const uint8_t* blk, int v) {
+    if constexpr (sizeof(T) == 2)
+        return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(blk)[v]) << 16);
+    else
         return reinterpret_cast<const float*>(blk)[v];
-    }
 }
 
-// ---- packing --------------------------------------------------------------
-
-// Quantised values of one block in register order e = 8*j + u, where
-// register byte lane j holds block byte lane (j + rho) & 3.
-template <typename T>
-__device__ __forceinline__ void quantise_block(const uint8_t* blk, int rho,
-                                               float recip, uint32_t valid,
-                                               int (&q)[32]) {
-    if constexpr (sizeof(T) == 2) {
-        const uint4* p = reinterpret_cast<const uint4*>(blk);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint4 c = p[(j + rho) & 3];
-            const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                q[8 * j + 2 * m] = quantize(bf16_lo(w[m]), recip);
-                q[8 * j + 2 * m + 1] = quantize(bf16_hi(w[m]), recip);
-            }
-        }
-    } else {
-        const uint4* p = reinterpret_cast<const uint4*>(blk);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int c = (j + rho) & 3;
-            const uint4 a = p[2 * c], b = p[2 * c + 1];
-            const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-            for (int m = 0; m < 8; ++m)
-                q[8 * j + m] = quantize(__uint_as_float(w[m]), recip);
-        }
-    }
-    if (valid < 32) {
-        // Elements past the end of the unit count as zero
-        // (cuszp_batched_fixed.cu:200-211).
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            const uint32_t v = 8u * (((e >> 3) + rho) & 3) + (e & 7);
-            if (v >= valid) q[e] = 0;
-        }
-    }
-}
-
-__device__ __forceinline__ uint32_t signed_row(int q) {
-    // (|q| << 1) | sign: bit 0 of every row becomes the sign word.
-    return (uabs(q) << 1) | (static_cast<uint32_t>(q) >> 31);
-}
-
-// Writes the sign word and `rate` planes of one block to out[0..rate].
-template <bool kWide>
-__device__ __forceinline__ void emit_block(const int (&q)[32], int rho,
-                                           uint32_t rate, uint32_t* out) {
-    const uint32_t sh = 8u * rho;
-    if constexpr (!kWide) {
-        uint32_t A[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const int e = bitpos(k);
-            A[k] = signed_row(q[e]) | (signed_row(q[e + 16]) << 16);
-        }
-        transpose16(A);
-#pragma unroll
-        for (int t = 0; t < 16; ++t)
-            if (t <= static_cast<int>(rate)) out[t] = __funnelshift_l(A[t], A[t], sh);
-    } else {
-        uint32_t R[32];
-        uint32_t sign = 0;
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-            const int e = bitpos(k);
-            R[k] = uabs(q[e]);
-            sign |= (static_cast<uint32_t>(q[e]) >> 31) << k;
-        }
-        transpose32(R);
-        out[0] = __funnelshift_l(sign, sign, sh);
-#pragma unroll
-        for (int b = 0; b < 32; ++b)
-            if (b < static_cast<int>(rate)) out[1 + b] = __funnelshift_l(R[b], R[b], sh);
-    }
-}
-
-// ---- the kernel -------------------------------------------------------------
+// ---- the kernel --------------------------------------------------------------
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 2) encode_kernel(EncodeArgs a) {
+__global__ void __launch_bounds__(kThreads, 3) encode_kernel(EncodeArgs a) {
     using L = Layout<T>;
-    constexpr uint32_t B = Traits<T>::kBytes;
+    constexpr uint32_t BB = kBlock * Traits<T>::kBytes;  // input bytes per block
+    constexpr int R = static_cast<int>(L::kRounds);
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* slice = smem + L::kSlice;
-    float2* extremes = reinterpret_cast<float2*>(smem + L::kMinMax);
+    float2* ext32 = reinterpret_cast<float2*>(smem + L::kExtremes);
+    uint32_t* ext16 = reinterpret_cast<uint32_t*>(smem + L::kExtremes);
     uint8_t* rates = smem + L::kRates;
-    uint8_t* stage0 = smem + L::kStage;
+    uint32_t* offs = reinterpret_cast<uint32_t*>(smem + L::kExtremes);  // after phase 4
 
     __shared__ uint64_t bar;
-    __shared__ uint32_t scratch[kWarps + 1];
+    __shared__ uint32_t wsum[R][kWarps];
     __shared__ float red_lo[kWarps], red_hi[kWarps];
     __shared__ float2 s_extremes;     // read by the other CTAs of the cluster
     __shared__ uint32_t s_total;      // read by the other CTAs of the cluster
-    __shared__ uint32_t s_base, s_unit_total, s_tail, s_bulk_ok, s_status;
+    __shared__ uint32_t s_base, s_unit_total, s_tail, s_status;
     __shared__ float s_eb;
 
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t rank = cluster.block_rank();
     const uint32_t csize = cluster.num_blocks();
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rho = (sizeof(T) == 2) ? ((tid >> 1) & 3) : (tid & 3);
 
     if (tid == 0) {
@@ -349,41 +378,49 @@ __global__ void __launch_bounds__(kThreads, 2) encode_kernel(EncodeArgs a) {
         const uint32_t hdr = (n + kGroup - 1) / kGroup * (kGroup / kBlock);
         uint32_t status = 0;
 
-        // 1. bring the slice on chip
+        // 1. the slice on chip
         if (tid == 0) {
             s_status = 0;
             uint32_t tail;
-            s_bulk_ok = plan_and_issue_load<T>(unit, map, u, e0, e1, slice, &bar, &tail);
+            plan_and_issue_load<T>(unit, map, u, e0, e1, slice, &bar, &tail);
             s_tail = tail;
         }
         __syncthreads();
         copy_elements<T>(unit, map, u, s_tail, e1, e0, slice);
         if (!mbar_wait_bounded(&bar, parity, kWaitPolls)) status |= kErrTimeout;
         parity ^= 1u;
+        // +0 past the end of the unit (the last block may be partial)
+        if (b1 == nb && nbs && tid < static_cast<int>(b1 * kBlock - e1))
+            reinterpret_cast<T*>(slice)[e1 - e0 + tid] = T(0.0f);
         __syncthreads();
 
         // 2. block extremes
         float tlo = FLT_MAX, thi = -FLT_MAX;
         for (uint32_t i = tid; i < nbs; i += kThreads) {
-            const uint8_t* blk = slice + i * kBlock * B;
+            const uint8_t* blk = slice + i * BB;
             float lo, hi;
             bool nan;
             const uint32_t valid = min(n - (b0 + i) * kBlock, uint32_t(kBlock));
             if (valid == kBlock) {
-                block_extremes(blk, rho, lo, hi, nan, T());
+                uint32_t w[Traits<T>::kWords];
+                load_block<T>(blk, rho, w);
+                block_extremes<T>(w, lo, hi, nan);
             } else {
                 lo = __int_as_float(0x7fffffff);
                 hi = lo;
                 nan = false;
                 for (uint32_t v = 0; v < valid; ++v) {
-                    const float x = elem_value<T>(blk, v);
+                    const float x = elem_at<T>(blk, v);
                     lo = fminf(lo, x);
                     hi = fmaxf(hi, x);
                     nan |= x != x;
                 }
             }
-            extremes[i] = make_float2(lo, hi);
-            rates[i] = nan ? 1 : 0;
+            if constexpr (sizeof(T) == 2)
+                ext16[i] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+            else
+                ext32[i] = make_float2(lo, hi);
+            rates[i] = nan ? kNanFlag : 0;
             tlo = fminf(tlo, lo);
             thi = fmaxf(thi, hi);
         }
@@ -392,9 +429,9 @@ __global__ void __launch_bounds__(kThreads, 2) encode_kernel(EncodeArgs a) {
             tlo = fminf(tlo, __shfl_xor_sync(0xffffffffu, tlo, d));
             thi = fmaxf(thi, __shfl_xor_sync(0xffffffffu, thi, d));
         }
-        if ((tid & 31) == 0) {
-            red_lo[tid >> 5] = tlo;
-            red_hi[tid >> 5] = thi;
+        if (lane == 0) {
+            red_lo[warp] = tlo;
+            red_hi[warp] = thi;
         }
         __syncthreads();
         if (tid == 0) {
@@ -422,19 +459,57 @@ __global__ void __launch_bounds__(kThreads, 2) encode_kernel(EncodeArgs a) {
         const float eb = s_eb;
         const float recip = __fdiv_rn(0.5f, eb);
 
-        // 4. rates and slice size, then slice offsets across the cluster
-        uint32_t mine = 0;
-        for (uint32_t i = tid; i < nbs; i += kThreads) {
-            const float2 mm = extremes[i];
-            uint32_t m = 0;
-            if (mm.x == mm.x)
-                m = max(uabs(quantize(mm.x, recip)), uabs(quantize(mm.y, recip)));
-            if (rates[i]) m = max(m, 1u);
-            const uint32_t r = 32 - __clz(m);
-            rates[i] = static_cast<uint8_t>(r);
-            mine += r ? 4 + 4 * r : 0;
+        // 4. rates, payload offsets (one scan for all rounds), slice size
+        uint32_t off[R];
+        bool any_wide = !(recip <= FLT_MAX);  // 0.5 / eb must be finite for +0 padding
+#pragma unroll
+        for (int k = 0; k < R; ++k) {
+            const uint32_t i = k * kThreads + tid;
+            uint32_t sz = 0;
+            if (i < nbs) {
+                float lo, hi;
+                if constexpr (sizeof(T) == 2) {
+                    const uint32_t p = ext16[i];
+                    lo = __uint_as_float(p << 16);
+                    hi = __uint_as_float(p & 0xffff0000u);
+                } else {
+                    lo = ext32[i].x;
+                    hi = ext32[i].y;
+                }
+                const bool nan = rates[i] & kNanFlag;
+                uint32_t m = 0;
+                if (lo == lo) m = max(uabs(quantize(lo, recip)), uabs(quantize(hi, recip)));
+                if (nan) m = max(m, 1u);
+                const uint32_t r = 32 - __clz(m);
+                rates[i] = static_cast<uint8_t>(r | (nan ? kNanFlag : 0));
+                any_wide |= nan || r > 15;
+                sz = r ? 4 + 4 * r : 0u;
+            }
+            uint32_t x = sz;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, x, d);
+                if (lane >= d) x += y;
+            }
+            if (lane == 31) wsum[k][warp] = x;
+            off[k] = x - sz;
         }
-        const uint32_t slice_total = cta_sum(mine, scratch);
+        const bool inplace = !__syncthreads_or(any_wide);
+        // every extremes word has been read: the region now holds offsets
+        uint32_t slice_total = 0;
+#pragma unroll
+        for (int k = 0; k < R; ++k) {
+            uint32_t pre = 0, tot = 0;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const uint32_t s = wsum[k][w];
+                pre += w < warp ? s : 0u;
+                tot += s;
+            }
+            const uint32_t i = k * kThreads + tid;
+            if (i < nbs) offs[i] = slice_total + off[k] + pre;
+            slice_total += tot;
+        }
         if (tid == 0) s_total = slice_total;
         cluster.sync();
         if (tid == 0) {
@@ -459,83 +534,94 @@ __global__ void __launch_bounds__(kThreads, 2) encode_kernel(EncodeArgs a) {
 
         if (fits) {
             uint8_t* stream = unit.stream;
-            // rate bytes of this slice; the last CTA zeroes the unused ones
-            for (uint32_t i = tid; i < nbs; i += kThreads) stream[b0 + i] = rates[i];
+            for (uint32_t i = tid; i < nbs; i += kThreads) stream[b0 + i] = rates[i] & 0x3f;
             if (rank == csize - 1)
                 for (uint32_t j = nb + tid; j < hdr; j += kThreads) stream[j] = 0;
 
-            // 5. pack, round by round (one block per thread per round)
-            uint32_t running = hdr + s_base;
+            // 5. pack round by round
+            const uint64_t start = static_cast<uint64_t>(hdr) + s_base;
+            const uint32_t shift =
+                static_cast<uint32_t>((reinterpret_cast<uintptr_t>(stream) + start) & 15u);
+            uint8_t* out_smem = smem + shift;   // slice payload byte 0 (in place)
+            const uint32_t sh = 8u * rho;
             const uint32_t rounds = (nbs + kThreads - 1) / kThreads;
+#pragma unroll 1
             for (uint32_t k = 0; k < rounds; ++k) {
-                if (tid == 0 && k >= 2) bulk_wait_read<1>();
                 const uint32_t i = k * kThreads + tid;
-                const uint32_t r = i < nbs ? rates[i] : 0u;
-                uint32_t round_total;
-                const uint32_t off = cta_exclusive_scan(r ? 4 + 4 * r : 0u, scratch, &round_total);
-                const uint32_t start = running;
-                const uint32_t shift = start & 15u;
-                uint8_t* stage = stage0 + (k & 1) * L::kStageStride;
-                const bool staged = shift + round_total <= kStageCap;
-                uint32_t* out = reinterpret_cast<uint32_t*>(
-                    staged ? stage + shift + off : stream + start + off);
-                const bool wide = __any_sync(0xffffffffu, r > 15);
-                if (r) {
-                    int q[32];
-                    const uint32_t valid = min(n - (b0 + i) * kBlock, uint32_t(kBlock));
-                    quantise_block<T>(slice + i * kBlock * B, rho, recip, valid, q);
-                    uint32_t orv = 0;
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) orv |= uabs(q[e]);
-                    if (32u - __clz(orv) != r) status |= kErrRateCheck;
-                    if (wide)
-                        emit_block<true>(q, rho, r, out);
-                    else
-                        emit_block<false>(q, rho, r, out);
-                } else if (i < nbs) {
-                    // A rate-0 block must really be all zeros.
-                    int q[32];
-                    const uint32_t valid = min(n - (b0 + i) * kBlock, uint32_t(kBlock));
-                    quantise_block<T>(slice + i * kBlock * B, rho, recip, valid, q);
-                    uint32_t orv = 0;
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) orv |= uabs(q[e]);
-                    if (orv) status |= kErrRateCheck;
-                }
-                if (staged) {
-                    fence_proxy_async_smem();
-                    __syncthreads();
-                    const uint32_t end = start + round_total;
-                    const uint32_t a0 = (start + 15u) & ~15u, a1 = end & ~15u;
-                    const bool body = a1 > a0;
-                    const uint32_t head_end = body ? a0 : end;
-                    if (body && tid == 0) {
-                        bulk_store(stream + a0, stage + shift + (a0 - start), a1 - a0);
-                        bulk_commit();
+                const bool active = i < nbs;
+                const uint32_t rb = active ? rates[i] : 0u;
+                const uint32_t r = rb & 0x3f;
+                const uint32_t valid =
+                    active ? min(n - (b0 + i) * kBlock, uint32_t(kBlock)) : uint32_t(kBlock);
+                const uint32_t pos = active ? offs[i] : 0u;
+                uint32_t w[Traits<T>::kWords];
+                if (active) load_block<T>(slice + i * BB, rho, w);
+                if (inplace) {
+                    uint32_t A[16];
+                    if (active) {
+                        const uint32_t orv = narrow_block<T>(w, recip, A);
+                        if (32u - __clz(orv >> 1) != r) status |= kErrRateCheck;
                     }
-                    const uint32_t head_words = (head_end - start) >> 2;
-                    const uint32_t tail_words = body ? (end - a1) >> 2 : 0u;
-                    if (tid < head_words) {
-                        reinterpret_cast<uint32_t*>(stream + start)[tid] =
-                            reinterpret_cast<const uint32_t*>(stage + shift)[tid];
-                    } else if (tid >= 32 && tid - 32 < tail_words) {
-                        const uint32_t t = tid - 32;
-                        reinterpret_cast<uint32_t*>(stream + a1)[t] =
-                            reinterpret_cast<const uint32_t*>(stage + shift + (a1 - start))[t];
+                    __syncthreads();  // every input of this round is in registers
+                    if (active && r) {
+                        uint32_t* out = reinterpret_cast<uint32_t*>(out_smem + pos);
+#pragma unroll
+                        for (int t = 0; t < 16; ++t)
+                            if (t <= static_cast<int>(r)) out[t] = __funnelshift_l(A[t], A[t], sh);
                     }
                 } else {
-                    __syncthreads();
+                    const bool narrow_ok = !(rb & kNanFlag) && r <= 15;
+                    const bool wide = __any_sync(0xffffffffu, active && !narrow_ok);
+                    if (active) {
+                        uint32_t* out = reinterpret_cast<uint32_t*>(stream + start + pos);
+                        uint32_t orv;
+                        if (!wide) {
+                            uint32_t A[16];
+                            orv = narrow_block<T>(w, recip, A) >> 1;
+#pragma unroll
+                            for (int t = 0; t < 16; ++t)
+                                if (r && t <= static_cast<int>(r))
+                                    out[t] = __funnelshift_l(A[t], A[t], sh);
+                        } else {
+                            orv = wide_block<T>(w, rho, recip, valid, r, out);
+                        }
+                        if (32u - __clz(orv) != r) status |= kErrRateCheck;
+                    }
                 }
-                running += round_total;
             }
-            if (tid == 0) bulk_wait<0>();
+            if (inplace) {
+                fence_proxy_async_smem();
+                __syncthreads();
+                const uint64_t g_end = start + slice_total;
+                const uint64_t a0 = (reinterpret_cast<uintptr_t>(stream) + start + 15u) & ~uint64_t(15);
+                const uint64_t a1 = (reinterpret_cast<uintptr_t>(stream) + g_end) & ~uint64_t(15);
+                const uint64_t s0 = reinterpret_cast<uintptr_t>(stream) + start;
+                const uint64_t s1 = reinterpret_cast<uintptr_t>(stream) + g_end;
+                const bool body = a1 > a0;
+                const uint64_t head_end = body ? a0 : s1;
+                if (body && tid == 0) {
+                    bulk_store(reinterpret_cast<void*>(a0), out_smem + (a0 - s0),
+                               static_cast<uint32_t>(a1 - a0));
+                    bulk_commit();
+                }
+                const uint32_t head_words = static_cast<uint32_t>(head_end - s0) >> 2;
+                const uint32_t tail_words = body ? static_cast<uint32_t>(s1 - a1) >> 2 : 0u;
+                if (static_cast<uint32_t>(tid) < head_words) {
+                    reinterpret_cast<uint32_t*>(s0)[tid] =
+                        reinterpret_cast<const uint32_t*>(out_smem)[tid];
+                } else if (tid >= 32 && static_cast<uint32_t>(tid - 32) < tail_words) {
+                    const uint32_t t = tid - 32;
+                    reinterpret_cast<uint32_t*>(a1)[t] =
+                        reinterpret_cast<const uint32_t*>(out_smem + (a1 - s0))[t];
+                }
+                if (tid == 0) bulk_wait<0>();
+            }
         }
         if (status) atomicOr(&s_status, status);
         __syncthreads();
         // Status lives in mapped host memory: a plain store (no atomics over
         // PCIe); any CTA that saw an error leaves a nonzero word.
-        if (tid == 0 && s_status)
-            *reinterpret_cast<volatile uint32_t*>(&a.status[u]) = s_status;
+        if (tid == 0 && s_status) *reinterpret_cast<volatile uint32_t*>(&a.status[u]) = s_status;
         cluster.barrier_wait(std::move(done_reading));
     }
 }
@@ -548,8 +634,8 @@ cudaError_t launch_encode_t(const EncodeLaunch& l, cudaStream_t stream) {
     if (c == 0) c = 1;
     if (c > kMaxCluster || l.num_units == 0) return cudaErrorInvalidValue;
     auto kernel = encode_kernel<T>;
-    cudaError_t err = cudaFuncSetAttribute(
-        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           L::kTotal);
     if (err != cudaSuccess) return err;
     if (c > 8) {
         err = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);

@@ -30,6 +30,8 @@ struct DecodeLaunch {
     bool zero_fill;            // write rate-0 blocks (the reference skips them)
     uint32_t* status;          // device-visible, one per unit
     ElemType type;             // destination element type
+    uint32_t total_items;      // sum of decode_items(unit.n)
+    uint32_t uniform_items;    // items per unit if all units have the same n, else 0
 };
 
 struct PackUnit {
@@ -37,6 +39,9 @@ struct PackUnit {
     uint64_t size;
     uint64_t offset;           // byte offset in the destination slab
 };
+
+// Work items (256 blocks each) of a unit of n elements in the decoder.
+uint32_t decode_items(uint32_t n);
 
 // Largest unit (elements) the single-pass clustered encoder accepts.
 uint32_t encode_max_elements(ElemType type);
