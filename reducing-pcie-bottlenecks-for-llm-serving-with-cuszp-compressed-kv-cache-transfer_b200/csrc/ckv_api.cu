@@ -9,7 +9,7 @@
 // status) are written by the kernel into mapped pinned memory, so the call
 // only has to synchronise the stream before returning them -- no per-page
 // device-to-host copies as in the reference (cuszp_wrapper.cpp:523-529).
-#include "../../include/ckv.h"
+#include "ckv.h"
 
 #include <cuda_runtime.h>
 

@@ -208,11 +208,19 @@ __device__ __forceinline__ void open_item(const DecodeArgs& a, uint32_t u, uint3
 }
 
 // The item after `it` in item order (the next unit starts at its item 0).
+// Within a unit the descriptor fields are carried over, so only the rate
+// byte is loaded.
 __device__ __forceinline__ void next_item(const DecodeArgs& a, const Item& it, Item& nx) {
-    if (it.s + 1 < it.items)
-        open_item(a, it.u, it.s + 1, nx);
-    else
+    if (it.s + 1 < it.items) {
+        nx = it;
+        nx.s = it.s + 1;
+        nx.b0 = nx.s * kItemBlocks;
+        const uint32_t nb = (it.n + kBlock - 1) / kBlock;
+        nx.nbs = min(kItemBlocks, nb - nx.b0);
+        nx.rate = threadIdx.x < nx.nbs ? __ldg(it.stream + nx.b0 + threadIdx.x) : 0u;
+    } else {
         open_item(a, it.u + 1, 0, nx);
+    }
 }
 
 template <typename T>
@@ -280,12 +288,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_kernel(DecodeArgs
         if (!cur.valid && tid == 0) atomicOr(&a.status[cur.u], kErrBadStream);
     }
 
-    // Issue the payload copy of an item into buffer `b`.
+    // Issue the payload copy of an item into buffer `b`.  The bulk copy is
+    // rounded out to 16-byte boundaries; where rounding up the end would pass
+    // the end of the unit's stream, the last few words are loaded by the
+    // threads instead.
     auto issue = [&](const Item& it, int b) {
         uint8_t* buf = smem + b * kBufStride;
         const uintptr_t g0 = reinterpret_cast<uintptr_t>(it.stream + it.start);
         const uintptr_t g1 = g0 + (it.valid ? it.total : 0u);
-        const uintptr_t ga = g0 & ~uintptr_t(15), gb = g1 & ~uintptr_t(15);
+        const uintptr_t limit = reinterpret_cast<uintptr_t>(it.stream) + it.size;
+        const uintptr_t up = (g1 + 15) & ~uintptr_t(15);
+        const uintptr_t ga = g0 & ~uintptr_t(15);
+        const uintptr_t gb = (it.valid && up <= limit) ? up : (g1 & ~uintptr_t(15));
         const bool body = gb > ga;
         if (tid == 0) {
             mbar_arrive_expect_tx(&bar[b], body ? static_cast<uint32_t>(gb - ga) : 0u);
@@ -297,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_kernel(DecodeArgs
             *reinterpret_cast<uint32_t*>(buf + (g - ga)) =
                 __ldg(reinterpret_cast<const uint32_t*>(g));
     };
+    static_assert(kBufStride >= kItemBlocks * (4 + 4 * 32) + 32, "payload buffer");
     issue(cur, 0);
 
     uint32_t status = 0;

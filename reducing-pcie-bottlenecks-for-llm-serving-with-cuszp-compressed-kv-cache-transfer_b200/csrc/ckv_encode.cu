@@ -9,7 +9,8 @@
 //      contiguous run of the element map);
 //   2. per block, min / max / NaN-presence (packed BF16 min/max);
 //   3. the CTAs exchange their slice extremes through distributed shared
-//      memory -> every CTA resolves the same absolute bound
+//      memory (each CTA stores into every peer before a cluster barrier and
+//      reads locally after it) -> every CTA resolves the same absolute bound
 //      eb = eps * fmaxf(max - min, 1e-6f) (cuszp_batched_fixed.cu:55-133);
 //   4. per block rate = bit length of max(|q(block min)|, |q(block max)|)
 //      -- the quantiser is monotone, so the extremes give the block's
@@ -348,10 +349,12 @@ __global__ void __launch_bounds__(kThreads, 3) encode_kernel(EncodeArgs a) {
     __shared__ uint64_t bar;
     __shared__ uint32_t wsum[R][kWarps];
     __shared__ float red_lo[kWarps], red_hi[kWarps];
-    __shared__ float2 s_extremes;     // read by the other CTAs of the cluster
-    __shared__ uint32_t s_total;      // read by the other CTAs of the cluster
+    // Written by every CTA of the cluster into every CTA (distributed shared
+    // memory stores before a cluster barrier), read locally after it.
+    __shared__ float2 s_extremes[kMaxCluster];
+    __shared__ uint32_t s_totals[kMaxCluster];
     __shared__ uint32_t s_base, s_unit_total, s_tail, s_status;
-    __shared__ float s_eb;
+    __shared__ float s_eb, s_recip;
 
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t rank = cluster.block_rank();
@@ -434,30 +437,41 @@ __global__ void __launch_bounds__(kThreads, 3) encode_kernel(EncodeArgs a) {
             red_hi[warp] = thi;
         }
         __syncthreads();
-        if (tid == 0) {
-            float lo = FLT_MAX, hi = -FLT_MAX;
+        // 3. unit extremes through distributed shared memory -> bound: lane r
+        // of warp 0 stores this slice's extremes into CTA r
+        if (warp == 0) {
+            float lo = lane < kWarps ? red_lo[lane] : FLT_MAX;
+            float hi = lane < kWarps ? red_hi[lane] : -FLT_MAX;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                lo = fminf(lo, red_lo[w]);
-                hi = fmaxf(hi, red_hi[w]);
+            for (int d = 16; d > 0; d >>= 1) {
+                lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, d));
+                hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, d));
             }
-            s_extremes = make_float2(lo, hi);
+            if (static_cast<uint32_t>(lane) < csize)
+                *cluster.map_shared_rank(&s_extremes[rank], static_cast<uint32_t>(lane)) =
+                    make_float2(lo, hi);
         }
-
-        // 3. unit extremes through distributed shared memory -> bound
         cluster.sync();
-        if (tid == 0) {
+        if (warp == 0) {
             float lo = FLT_MAX, hi = -FLT_MAX;
-            for (uint32_t r = 0; r < csize; ++r) {
-                const float2 v = *cluster.map_shared_rank(&s_extremes, r);
-                lo = fminf(lo, v.x);
-                hi = fmaxf(hi, v.y);
+            if (static_cast<uint32_t>(lane) < csize) {
+                lo = s_extremes[lane].x;
+                hi = s_extremes[lane].y;
             }
-            s_eb = resolve_bound(unit.eb, lo, hi, a.relative != 0);
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) {
+                lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, d));
+                hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, d));
+            }
+            if (lane == 0) {
+                const float eb = resolve_bound(unit.eb, lo, hi, a.relative != 0);
+                s_eb = eb;
+                s_recip = __fdiv_rn(0.5f, eb);
+            }
         }
         __syncthreads();
         const float eb = s_eb;
-        const float recip = __fdiv_rn(0.5f, eb);
+        const float recip = s_recip;
 
         // 4. rates, payload offsets (one scan for all rounds), slice size
         uint32_t off[R];
@@ -510,19 +524,22 @@ __global__ void __launch_bounds__(kThreads, 3) encode_kernel(EncodeArgs a) {
             if (i < nbs) offs[i] = slice_total + off[k] + pre;
             slice_total += tot;
         }
-        if (tid == 0) s_total = slice_total;
+        if (warp == 0 && static_cast<uint32_t>(lane) < csize)
+            *cluster.map_shared_rank(&s_totals[rank], static_cast<uint32_t>(lane)) = slice_total;
         cluster.sync();
-        if (tid == 0) {
-            uint32_t base = 0, all = 0;
-            for (uint32_t r = 0; r < csize; ++r) {
-                const uint32_t t = *cluster.map_shared_rank(&s_total, r);
-                base += r < rank ? t : 0u;
-                all += t;
+        if (warp == 0) {
+            const uint32_t t = static_cast<uint32_t>(lane) < csize ? s_totals[lane] : 0u;
+            uint32_t base = static_cast<uint32_t>(lane) < rank ? t : 0u, all = t;
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) {
+                base += __shfl_xor_sync(0xffffffffu, base, d);
+                all += __shfl_xor_sync(0xffffffffu, all, d);
             }
-            s_base = base;
-            s_unit_total = all;
+            if (lane == 0) {
+                s_base = base;
+                s_unit_total = all;
+            }
         }
-        auto done_reading = cluster.barrier_arrive();
         __syncthreads();
         const uint64_t unit_bytes = static_cast<uint64_t>(hdr) + s_unit_total;
         const bool fits = unit_bytes <= unit.capacity;
@@ -622,7 +639,9 @@ __global__ void __launch_bounds__(kThreads, 3) encode_kernel(EncodeArgs a) {
         // Status lives in mapped host memory: a plain store (no atomics over
         // PCIe); any CTA that saw an error leaves a nonzero word.
         if (tid == 0 && s_status) *reinterpret_cast<volatile uint32_t*>(&a.status[u]) = s_status;
-        cluster.barrier_wait(std::move(done_reading));
+        // No CTA reads another's shared memory after the second cluster
+        // barrier, and the next unit's stores into s_extremes / s_totals come
+        // after barriers this CTA only reaches once it has read them.
     }
 }
 
