@@ -194,6 +194,28 @@ CKV_API ckv_status ckv_pack(ckv_ctx* ctx, const uint8_t* const* srcs, const size
 CKV_API ckv_status ckv_set_kernel_timing(ckv_ctx* ctx, int enable);
 CKV_API ckv_status ckv_kernel_time(ckv_ctx* ctx, int kind, float* ms);
 
+/* ckv_compress_batch_fixed_bf16 for callers that cannot allocate memory.
+ * No counterpart in the reference.  Some callers cannot call cudaMalloc when
+ * they compress: a serving engine that reserved all free HBM for its KV
+ * cache at start-up (a later allocation fails or evicts cache), or code that
+ * must not risk the device-wide synchronisation a cudaFree implies.  This
+ * entry point needs no context and allocates nothing: its scratch (unit
+ * descriptors, pointer tables, sizes, bounds, status) is one fixed
+ * file-scope device array of CKV_NOALLOC_MAX_UNITS units (about 270 KB),
+ * held by every GPU that loads the library until the process exits.
+ * Larger batches are rejected with CKV_ERR_ARGUMENT and a message on stderr.
+ * The first call on a device looks up the array's device address (with that
+ * device current), so make it before any stream capture.  All calls share
+ * the array: calls that overlap on the GPU race.  Otherwise as
+ * ckv_compress_batch_fixed_bf16: `error_bound` and `relative` replace the
+ * context's configuration, eps may be NULL, the call blocks until sizes and
+ * bounds are on the host, and the bitstreams are identical. */
+#define CKV_NOALLOC_MAX_UNITS 4096
+CKV_API ckv_status ckv_compress_batch_fixed_bf16_noalloc(
+    const void* const* inputs, uint8_t* const* outputs, const float* eps, size_t batch,
+    size_t n, size_t capacity, float error_bound, int relative, size_t* sizes,
+    float* bounds, void* stream);
+
 /* Number of kernel launches libckv has issued since it was loaded. */
 CKV_API uint64_t ckv_kernel_launches(void);
 

@@ -42,7 +42,7 @@ EXPORTS = (
     "ckv_decompress_batch_fixed_bf16_scatter",
     "ckv_decompress_batch_fixed_bf16_indexed_scatter", "ckv_set_zero_fill",
     "ckv_device_status", "ckv_kernel_launches", "ckv_pack",
-    "ckv_set_kernel_timing", "ckv_kernel_time",
+    "ckv_set_kernel_timing", "ckv_kernel_time", "ckv_compress_batch_fixed_bf16_noalloc",
 )
 
 
@@ -95,6 +95,8 @@ def _declare(lib: C.CDLL) -> None:
         "ckv_pack": (c_status, [P, P, P, c_size, P, c_size, c_size, P, P, P]),
         "ckv_set_kernel_timing": (c_status, [P, c_int]),
         "ckv_kernel_time": (c_status, [P, c_int, C.POINTER(c_float)]),
+        "ckv_compress_batch_fixed_bf16_noalloc": (
+            c_status, [P, P, P, c_size, c_size, c_size, c_float, c_int, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
