@@ -96,28 +96,79 @@ def ncu_traffic(kernel: str) -> tuple[float | None, str | None]:
 
 
 class ClockSampler:
-    """nvidia-smi samples (200 ms) during the timed region."""
+    """SM clock and clock-event reasons sampled every ~2 ms during the timed
+    region (the timed regions last milliseconds, far below nvidia-smi's
+    polling period), read through NVML; nvidia-smi at 200 ms otherwise."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4}
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, device: torch.device, physical_index: int, period_s: float = 0.002):
+        self.period = period_s
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.source = None
+        self.nvml = None
+        self.handle = None
         self.proc = None
+        self.lines: list[str] = []
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            try:
+                uuid = str(torch.cuda.get_device_properties(device).uuid)
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(
+                    uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(physical_index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle,
+                                                                  pynvml.NVML_CLOCK_SM))
+            self.nvml = pynvml
+            self.source = "nvml, 2 ms"
+        except Exception:
+            self.nvml = None
+            self.physical = physical_index
+
+    def _reasons(self) -> int:
+        try:
+            return int(self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle))
+        except Exception:
+            return int(self.nvml.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = int(self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+                self.samples.append((float(mhz), self._reasons()))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
 
     def __enter__(self):
+        if self.nvml is not None:
+            import threading
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+            return self
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)],
+                ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.physical)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi, 200 ms"
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.nvml is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+            return
         if self.proc is None:
             return
         time.sleep(0.25)
@@ -127,27 +178,30 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
             out = ""
-        self.lines = [ln for ln in out.splitlines() if ln.strip()]
-
-    def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in out.splitlines():
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                mhz, self.max_mhz = float(parts[1]), float(parts[2])
             except ValueError:
                 continue
+            bits = 0
             for name, val in zip(names, parts[5:9]):
                 if val.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                    bits |= self.REASONS[name]
+            self.samples.append((mhz, bits))
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "source": self.source}
+        reasons = sorted(name for name, bit in self.REASONS.items()
+                         if any(b & bit for _, b in self.samples))
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": self.source}
 
 
 # ---------------------------------------------------------------------------
@@ -467,7 +521,7 @@ def main() -> int:
     visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     ids = [v for v in visible.split(",") if v.strip()]
     physical = int(ids[local]) if len(ids) > local and ids[local].strip().isdigit() else local
-    with ClockSampler(physical) as clocks:
+    with ClockSampler(device, physical) as clocks:
         step_ms, _ = timed_steps(codec.step, args.steps, flush, device, after=kernel_times)
         barrier()
         launches_value = codec.launches() - launches0

@@ -296,6 +296,13 @@ ckv_status run_encode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, size_t* sizes,
 ckv_status run_decode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, void* stream_ptr) {
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     DeviceGuard guard(ctx->device);
+    // Empty units decode to nothing and own no work items; the decoder walks
+    // units by item order, so they are dropped here (only identity-mapped
+    // batches can hold them, and those index nothing by unit).
+    b.units.erase(std::remove_if(b.units.begin(), b.units.end(),
+                                 [](const Unit& u) { return u.n == 0; }),
+                  b.units.end());
+    if (b.units.empty()) return CKV_OK;
     const size_t count = b.units.size();
     uint32_t items = 0;
     bool uniform = true;

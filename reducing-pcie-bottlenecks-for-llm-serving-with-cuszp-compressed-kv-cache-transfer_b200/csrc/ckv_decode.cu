@@ -1,30 +1,35 @@
 // Decoder for the fixed-mode codec (sm_100a).
 //
-// Persistent CTAs stream "items" of 256 blocks (8192 elements): one block per
-// thread per item.  A CTA owns a contiguous range of items, so consecutive
-// items usually belong to the same unit and the payload offset of the next
-// item is the current one plus the current item's size; only a CTA's first
-// item (when it starts mid-unit) sums the rate bytes before it.  While a CTA
-// decodes item k, the TMA bulk copy of item k+1's payload is already in
-// flight into the other half of a double buffer.
+// Persistent CTAs stream "items" of 256 blocks (8192 elements).  A CTA owns
+// a contiguous range of items, so consecutive items usually belong to the
+// same unit and the payload offset of the next item is the current one plus
+// the current item's size; only a CTA's first item (when it starts mid-unit)
+// sums the rate bytes before it.
 //
-// Per item:
-//   1. each thread holds its block's rate (loaded one item ahead); one CTA
-//      pass computes the exclusive scan of block sizes for item k (payload
-//      offsets) and the total size of item k+1;
-//   2. thread 0 issues item k+1's payload copy (16-byte aligned body by TMA,
-//      the sub-16-byte tail by plain word loads);
-//   3. wait for item k's payload; each thread turns its sign word and bit
-//      planes back into 32 values with a register transpose and writes them
-//      with 16-byte stores through the element map (contiguous page, one of
-//      several destinations, or layer-indexed page).
+// Each CTA is one producer warp and eight consumer warps around a ring of
+// four slots in shared memory, with a "full" and an "empty" mbarrier per
+// slot and no CTA-wide barrier in the loop:
+//
+//   producer warp, per item: its 256 rate bytes (loaded one item ahead) ->
+//     block sizes -> per-block payload offsets (warp scan); once the slot is
+//     empty it stores offsets, rates and the item's description in the slot
+//     and starts one TMA bulk copy of the item's payload into it, completing
+//     on the slot's full barrier;
+//   consumer warps (one block per thread): wait for full, turn the sign word
+//     and bit planes back into 32 values with a register transpose,
+//     dequantise, write 16-byte stores through the element map (contiguous
+//     page, one of several destinations, or layer-indexed page), arrive on
+//     empty.
+//
+// An item whose payload does not fit a slot (many blocks of rate > 15) is
+// decoded straight from global memory.
 //
 // Dequantisation is (float)q * eb * 2.0f rounded to BF16 as the reference
-// does (cuszp_batched_fixed.cu:535-549).  For the common case (|q| < 2^15,
-// eb a normal number far from overflow) it is evaluated as one fused
-// multiply-add on a magic-number float, fma(2^23 + |q|, 2eb, -2^23 * 2eb),
-// which rounds exactly once, to the same value, as the reference's two
-// multiplies; other blocks use the two multiplies.
+// does (cuszp_batched_fixed.cu:535-549).  For |q| < 2^15 and eb in
+// [2^-100, 2^100] it is evaluated as one fused multiply-add on a
+// magic-number float, fma(2^23 + |q|, 2eb, -2^23 * 2eb), which rounds exactly
+// once, to the same value, as the reference's two multiplies; other blocks
+// use the two multiplies.
 //
 // Blocks whose rate is zero are not written, as in the reference decoder
 // (cuszp_batched_fixed.cu:496-623 stores only inside `if (fixed_rate)`);
@@ -34,10 +39,16 @@
 namespace ckv {
 namespace {
 
-constexpr uint32_t kItemBlocks = kThreads;                     // 256
-constexpr uint32_t kBufStride = (kItemBlocks * (4 + 4 * 32) + 32 + 15) / 16 * 16;
-constexpr uint32_t kSmem = 2 * kBufStride;
-constexpr uint32_t kWaitPolls = 1u << 24;
+constexpr uint32_t kItemBlocks = kThreads;               // 256, one per consumer thread
+constexpr int kConsumerWarps = kThreads / 32;            // 8
+constexpr int kCtaThreads = kThreads + 32;               // + the producer warp
+constexpr int kSlots = 4;
+constexpr uint32_t kPayloadCap = kItemBlocks * 64 + 32;  // every block of rate <= 15
+constexpr uint32_t kOffsAt = kPayloadCap;
+constexpr uint32_t kRatesAt = kOffsAt + kItemBlocks * 4;
+constexpr uint32_t kSlotBytes = (kRatesAt + kItemBlocks + 127) / 128 * 128;
+constexpr uint32_t kSmem = kSlots * kSlotBytes;
+constexpr uint32_t kWaitPolls = 1u << 22;
 constexpr int kCtasPerSm = 3;
 
 struct DecodeArgs {
@@ -49,6 +60,19 @@ struct DecodeArgs {
     uint32_t zero_fill;
     uint32_t* status;
 };
+
+// What the consumers need of the item a slot holds.
+struct SlotMeta {
+    const void* elems;        // destination base of the unit
+    const uint8_t* payload;   // the item's payload in global memory
+    uint32_t u, b0, nbs, n;
+    uint32_t map, kind;       // element map index and kind
+    uint32_t flags;           // kValid, kInSlot
+    uint32_t lead;            // payload byte 0 sits at slot byte `lead`
+    float eb;
+    uint32_t pad[3];
+};
+enum : uint32_t { kValid = 1, kInSlot = 2 };
 
 __device__ __forceinline__ uint32_t block_bytes(uint32_t r) { return r ? 4 + 4 * r : 0u; }
 
@@ -122,27 +146,48 @@ __device__ __forceinline__ void store_elem(__nv_bfloat16* p, float v) { *p = __f
 __device__ __forceinline__ void store_elem(float* p, float v) { *p = v; }
 
 template <typename T>
-__device__ __forceinline__ void write_block(const Unit& unit, const Map& map, uint32_t u,
-                                            uint32_t jb, uint32_t valid, const float (&f)[32]) {
+__device__ __forceinline__ void store_block16(T* dst, const float (&f)[32]) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    if constexpr (sizeof(T) == 2) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            d[c] = make_uint4(pack_bf16x2(f[8 * c + 0], f[8 * c + 1]),
+                              pack_bf16x2(f[8 * c + 2], f[8 * c + 3]),
+                              pack_bf16x2(f[8 * c + 4], f[8 * c + 5]),
+                              pack_bf16x2(f[8 * c + 6], f[8 * c + 7]));
+    } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            d[c] = make_uint4(__float_as_uint(f[4 * c + 0]), __float_as_uint(f[4 * c + 1]),
+                              __float_as_uint(f[4 * c + 2]), __float_as_uint(f[4 * c + 3]));
+    }
+}
+
+// Writes block jb of unit u (its first `valid` values) through its map.
+template <typename T>
+__device__ __forceinline__ void write_block(const DecodeArgs& a, const SlotMeta& m, uint32_t jb,
+                                            uint32_t valid, const float (&f)[32]) {
     const uint32_t e0 = jb * kBlock;
-    const uint32_t L = run_len(unit, map);
-    const uint32_t r0 = e0 / L, off = e0 - r0 * L;
-    T* dst = run_base<T>(unit, map, u, r0) + off;
-    if (valid == kBlock && off + kBlock <= L && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-        uint4* d = reinterpret_cast<uint4*>(dst);
-        if constexpr (sizeof(T) == 2) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-                d[c] = make_uint4(pack_bf16x2(f[8 * c + 0], f[8 * c + 1]),
-                                  pack_bf16x2(f[8 * c + 2], f[8 * c + 3]),
-                                  pack_bf16x2(f[8 * c + 4], f[8 * c + 5]),
-                                  pack_bf16x2(f[8 * c + 6], f[8 * c + 7]));
-        } else {
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                d[c] = make_uint4(__float_as_uint(f[4 * c + 0]), __float_as_uint(f[4 * c + 1]),
-                                  __float_as_uint(f[4 * c + 2]), __float_as_uint(f[4 * c + 3]));
+    if (m.kind == kMapIdentity) {
+        T* dst = static_cast<T*>(const_cast<void*>(m.elems)) + e0;
+        if (valid == kBlock && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+            store_block16(dst, f);
+            return;
         }
+#pragma unroll
+        for (int v = 0; v < 32; ++v)
+            if (static_cast<uint32_t>(v) < valid) store_elem(dst + v, f[v]);
+        return;
+    }
+    const Map map = a.maps[m.map];
+    Unit unit;
+    unit.elems = m.elems;
+    unit.n = m.n;
+    const uint32_t L = map.run;
+    const uint32_t r0 = e0 / L, off = e0 - r0 * L;
+    T* dst = run_base<T>(unit, map, m.u, r0) + off;
+    if (valid == kBlock && off + kBlock <= L && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+        store_block16(dst, f);
         return;
     }
 #pragma unroll
@@ -150,7 +195,7 @@ __device__ __forceinline__ void write_block(const Unit& unit, const Map& map, ui
         if (static_cast<uint32_t>(v) < valid) {
             const uint32_t i = e0 + v;
             const uint32_t r = i / L;
-            store_elem(run_base<T>(unit, map, u, r) + (i - r * L), f[v]);
+            store_elem(run_base<T>(unit, map, m.u, r) + (i - r * L), f[v]);
         }
     }
 }
@@ -163,7 +208,7 @@ __device__ __forceinline__ void locate(const DecodeArgs& a, uint32_t item, uint3
         s = item - u * a.uniform_items;
         return;
     }
-    uint32_t lo = 0, hi = a.num_units;  // last unit with first_item <= item
+    uint32_t lo = 0, hi = a.num_units;  // last unit with item0 <= item
     while (hi - lo > 1) {
         const uint32_t mid = (lo + hi) / 2;
         if (a.units[mid].item0 <= item)
@@ -175,59 +220,77 @@ __device__ __forceinline__ void locate(const DecodeArgs& a, uint32_t item, uint3
     s = item - a.units[lo].item0;
 }
 
-struct Item {
-    uint32_t u, s;       // unit, item within unit
-    uint32_t b0, nbs;    // first block, blocks in the item
-    uint64_t start;      // payload byte offset within the unit's stream
-    uint32_t total;      // payload bytes of the item
-    uint32_t rate;       // this thread's block rate (0 if none)
-    bool valid;
-    // the unit's descriptor fields
+// The producer's view of an item: the unit's fields and this lane's 8 rate
+// bytes (blocks 8*lane .. 8*lane+7 of the item).
+struct PItem {
     const uint8_t* stream;
+    const void* elems;
     uint64_t size;
-    uint32_t n, hdr, map, items;
+    uint32_t u, s, b0, nbs, items, n, hdr, map, kind;
     float eb;
+    uint32_t r_lo, r_hi;
 };
 
-// Sets up an item and starts the load of this thread's rate byte.
-__device__ __forceinline__ void open_item(const DecodeArgs& a, uint32_t u, uint32_t s, Item& it) {
-    const Unit unit = a.units[u];
-    it.u = u;
-    it.s = s;
-    it.stream = unit.stream;
-    it.size = unit.capacity;
-    it.n = unit.n;
-    it.eb = unit.eb;
-    it.map = unit.map;
-    it.hdr = (unit.n + kGroup - 1) / kGroup * (kGroup / kBlock);
-    it.items = items_of(unit.n);
-    it.b0 = s * kItemBlocks;
-    const uint32_t nb = (unit.n + kBlock - 1) / kBlock;
-    it.nbs = min(kItemBlocks, nb - it.b0);
-    it.rate = threadIdx.x < it.nbs ? __ldg(unit.stream + it.b0 + threadIdx.x) : 0u;
+__device__ __forceinline__ void p_rates(PItem& it) {
+    const uint32_t first = 8 * (threadIdx.x & 31);
+    const uint8_t* p = it.stream + it.b0 + first;
+    it.r_lo = 0;
+    it.r_hi = 0;
+    if (first + 8 <= it.nbs) {
+        // b0 is a multiple of 256 and streams are 4-byte aligned
+        it.r_lo = __ldg(reinterpret_cast<const uint32_t*>(p));
+        it.r_hi = __ldg(reinterpret_cast<const uint32_t*>(p) + 1);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (first + j < it.nbs) {
+                const uint32_t byte = __ldg(p + j);
+                if (j < 4)
+                    it.r_lo |= byte << (8 * j);
+                else
+                    it.r_hi |= byte << (8 * (j - 4));
+            }
+        }
+    }
 }
 
-// The item after `it` in item order (the next unit starts at its item 0).
-// Within a unit the descriptor fields are carried over, so only the rate
-// byte is loaded.
-__device__ __forceinline__ void next_item(const DecodeArgs& a, const Item& it, Item& nx) {
+__device__ __forceinline__ void p_open(const DecodeArgs& a, uint32_t u, uint32_t s, PItem& it) {
+    const Unit unit = a.units[u];
+    it.stream = unit.stream;
+    it.elems = unit.elems;
+    it.size = unit.capacity;
+    it.u = u;
+    it.n = unit.n;
+    it.hdr = (unit.n + kGroup - 1) / kGroup * (kGroup / kBlock);
+    it.items = items_of(unit.n);
+    it.map = unit.map;
+    it.kind = a.maps[unit.map].kind;
+    it.eb = unit.eb;
+    it.s = s;
+    it.b0 = s * kItemBlocks;
+    it.nbs = min(kItemBlocks, (unit.n + kBlock - 1) / kBlock - it.b0);
+    p_rates(it);
+}
+
+// The item after `it` in item order; within a unit only the rate bytes load.
+__device__ __forceinline__ void p_next(const DecodeArgs& a, const PItem& it, PItem& nx) {
     if (it.s + 1 < it.items) {
         nx = it;
         nx.s = it.s + 1;
         nx.b0 = nx.s * kItemBlocks;
-        const uint32_t nb = (it.n + kBlock - 1) / kBlock;
-        nx.nbs = min(kItemBlocks, nb - nx.b0);
-        nx.rate = threadIdx.x < nx.nbs ? __ldg(it.stream + nx.b0 + threadIdx.x) : 0u;
+        nx.nbs = min(kItemBlocks, (it.n + kBlock - 1) / kBlock - nx.b0);
+        p_rates(nx);
     } else {
-        open_item(a, it.u + 1, 0, nx);
+        p_open(a, it.u + 1, 0, nx);
     }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t bar[2];
-    __shared__ uint32_t scan_w[kWarps], next_w[kWarps], bad_w[kWarps];
+    __shared__ uint64_t full[kSlots], empty[kSlots];
+    __shared__ SlotMeta meta[kSlots];
+    __shared__ uint32_t red[kCtaThreads / 32][2];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     const uint32_t begin = static_cast<uint32_t>(
@@ -236,169 +299,208 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) decode_kernel(DecodeArgs
         (static_cast<uint64_t>(a.total_items) * (blockIdx.x + 1)) / gridDim.x);
     if (begin >= end) return;
     if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+        for (int s = 0; s < kSlots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
         fence_mbar_init();
     }
-    __syncthreads();
-    uint32_t parity = 0;  // bit b: phase parity of bar[b]
 
-    // First item: its payload offset needs the sizes of all blocks before it.
-    Item cur, nxt, nn;
+    // The first item's payload offset: the sizes of all blocks before it,
+    // summed by the whole CTA.
+    uint32_t u0, s0;
+    locate(a, begin, u0, s0);
+    uint64_t first_start;
+    bool first_ok;
     {
-        uint32_t u, s;
-        locate(a, begin, u, s);
-        open_item(a, u, s, cur);
-    }
-    if (begin + 1 < end) next_item(a, cur, nxt);
-    {
-        const uint32_t* words = reinterpret_cast<const uint32_t*>(cur.stream);
+        const Unit unit = a.units[u0];
+        const uint32_t* words = reinterpret_cast<const uint32_t*>(unit.stream);
         uint32_t acc = 0, bad = 0;
-        for (uint32_t w = tid; w < cur.b0 / 4; w += kThreads) {
+        for (uint32_t w = tid; w < s0 * (kItemBlocks / 4); w += kCtaThreads) {
             const uint32_t x = __ldg(words + w);
             acc += __dp4a(x, 0x01010101u, 0u) + __dp4a(__vsetne4(x, 0u), 0x01010101u, 0u);
             bad |= __vcmpgtu4(x, 0x1f1f1f1fu);
         }
-        bad |= cur.rate > 31;
-        uint32_t mine = block_bytes(cur.rate);
 #pragma unroll
         for (int d = 16; d > 0; d >>= 1) {
             acc += __shfl_xor_sync(0xffffffffu, acc, d);
-            mine += __shfl_xor_sync(0xffffffffu, mine, d);
             bad |= __shfl_xor_sync(0xffffffffu, bad, d);
         }
         if (lane == 0) {
-            scan_w[warp] = acc;
-            next_w[warp] = mine;
-            bad_w[warp] = bad;
+            red[warp][0] = acc;
+            red[warp][1] = bad;
         }
         __syncthreads();
-        uint32_t prefix = 0, total = 0;
+        acc = 0;
         bad = 0;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-            prefix += scan_w[w];
-            total += next_w[w];
-            bad |= bad_w[w];
+        for (int w = 0; w < kCtaThreads / 32; ++w) {
+            acc += red[w][0];
+            bad |= red[w][1];
         }
-        __syncthreads();
-        cur.start = static_cast<uint64_t>(cur.hdr) + 4ull * prefix;
-        cur.total = total;
-        cur.valid = !bad && cur.size >= cur.hdr && cur.start + total <= cur.size;
-        if (!cur.valid && tid == 0) atomicOr(&a.status[cur.u], kErrBadStream);
+        const uint32_t hdr = (unit.n + kGroup - 1) / kGroup * (kGroup / kBlock);
+        first_start = static_cast<uint64_t>(hdr) + 4ull * acc;
+        first_ok = !bad;
     }
 
-    // Issue the payload copy of an item into buffer `b`.  The bulk copy is
-    // rounded out to 16-byte boundaries; where rounding up the end would pass
-    // the end of the unit's stream, the last few words are loaded by the
-    // threads instead.
-    auto issue = [&](const Item& it, int b) {
-        uint8_t* buf = smem + b * kBufStride;
-        const uintptr_t g0 = reinterpret_cast<uintptr_t>(it.stream + it.start);
-        const uintptr_t g1 = g0 + (it.valid ? it.total : 0u);
-        const uintptr_t limit = reinterpret_cast<uintptr_t>(it.stream) + it.size;
-        const uintptr_t up = (g1 + 15) & ~uintptr_t(15);
-        const uintptr_t ga = g0 & ~uintptr_t(15);
-        const uintptr_t gb = (it.valid && up <= limit) ? up : (g1 & ~uintptr_t(15));
-        const bool body = gb > ga;
-        if (tid == 0) {
-            mbar_arrive_expect_tx(&bar[b], body ? static_cast<uint32_t>(gb - ga) : 0u);
-            if (body)
-                bulk_load(buf, reinterpret_cast<const void*>(ga), static_cast<uint32_t>(gb - ga),
-                          &bar[b]);
-        }
-        for (uintptr_t g = (body ? gb : g0) + 4 * tid; g < g1; g += 4 * kThreads)
-            *reinterpret_cast<uint32_t*>(buf + (g - ga)) =
-                __ldg(reinterpret_cast<const uint32_t*>(g));
-    };
-    static_assert(kBufStride >= kItemBlocks * (4 + 4 * 32) + 32, "payload buffer");
-    issue(cur, 0);
+    if (warp == kConsumerWarps) {
+        // ------------------------------ producer ------------------------------
+        uint32_t status = 0;
+        PItem cur, nxt;
+        p_open(a, u0, s0, cur);
+        uint64_t start = first_start;
+        bool unit_ok = first_ok;
+        if (!first_ok && lane == 0) atomicOr(&a.status[cur.u], kErrBadStream);
+        uint32_t k = 0;
+        for (uint32_t item = begin; item < end; ++item, ++k) {
+            const int slot = static_cast<int>(k % kSlots);
+            const uint32_t use = k / kSlots;
+            // the next item's rate bytes load while this one is set up and
+            // while the producer waits for a free slot
+            if (item + 1 < end) p_next(a, cur, nxt);
 
+            // block sizes of this lane's 8 blocks, then a warp scan
+            uint32_t sz[8], lane_total = 0, bad = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t r = ((j < 4 ? cur.r_lo : cur.r_hi) >> (8 * (j & 3))) & 0xffu;
+                sz[j] = lane_total;
+                lane_total += block_bytes(r);
+                bad |= r > 31;
+            }
+            uint32_t x = lane_total;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, x, d);
+                if (lane >= d) x += y;
+            }
+            const uint32_t lane_off = x - lane_total;
+            const uint32_t total = __shfl_sync(0xffffffffu, x, 31);
+            bad = __any_sync(0xffffffffu, bad);
+            const bool valid =
+                unit_ok && !bad && cur.size >= cur.hdr && start + total <= cur.size;
+            if (!valid && unit_ok && lane == 0) atomicOr(&a.status[cur.u], kErrBadStream);
+            unit_ok = valid;
+
+            const uintptr_t g0 = reinterpret_cast<uintptr_t>(cur.stream + start);
+            const uintptr_t g1 = g0 + total;
+            const uintptr_t limit = reinterpret_cast<uintptr_t>(cur.stream) + cur.size;
+            const uint32_t lead = static_cast<uint32_t>(g0 & 15u);
+            const bool in_slot = valid && lead + total + 16 <= kPayloadCap;
+            // 16-byte aligned body by TMA; where rounding the end up would
+            // pass the end of the stream, the words after the last 16-byte
+            // boundary are copied by the lanes
+            const uintptr_t ga = g0 & ~uintptr_t(15);
+            const uintptr_t up = (g1 + 15) & ~uintptr_t(15);
+            const uintptr_t gb = up <= limit ? up : (g1 & ~uintptr_t(15));
+            const uint32_t body = in_slot && gb > ga ? static_cast<uint32_t>(gb - ga) : 0u;
+
+            if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1u, kWaitPolls)) {
+                status |= kErrTimeout;
+                break;
+            }
+            uint8_t* base = smem + slot * kSlotBytes;
+            uint32_t* offs = reinterpret_cast<uint32_t*>(base + kOffsAt);
+            reinterpret_cast<uint4*>(offs)[2 * lane] =
+                make_uint4(lane_off + sz[0], lane_off + sz[1], lane_off + sz[2], lane_off + sz[3]);
+            reinterpret_cast<uint4*>(offs)[2 * lane + 1] =
+                make_uint4(lane_off + sz[4], lane_off + sz[5], lane_off + sz[6], lane_off + sz[7]);
+            reinterpret_cast<uint2*>(base + kRatesAt)[lane] = make_uint2(cur.r_lo, cur.r_hi);
+            if (in_slot)
+                for (uintptr_t g = (body ? gb : g0) + 4 * lane; g < g1; g += 128)
+                    *reinterpret_cast<uint32_t*>(base + (g - ga)) =
+                        __ldg(reinterpret_cast<const uint32_t*>(g));
+            if (lane == 0) {
+                SlotMeta m;
+                m.elems = cur.elems;
+                m.payload = cur.stream + start;
+                m.u = cur.u;
+                m.b0 = cur.b0;
+                m.nbs = cur.nbs;
+                m.n = cur.n;
+                m.map = cur.map;
+                m.kind = cur.kind;
+                m.flags = (valid ? kValid : 0u) | (in_slot ? kInSlot : 0u);
+                m.lead = lead;
+                m.eb = cur.eb;
+                m.pad[0] = m.pad[1] = m.pad[2] = 0;
+                meta[slot] = m;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                // releases the lanes' stores above to the consumers
+                mbar_arrive_expect_tx(&full[slot], body);
+                if (body) bulk_load(base, reinterpret_cast<const void*>(ga), body, &full[slot]);
+            }
+
+            if (item + 1 < end) {
+                if (nxt.u == cur.u) {
+                    start += total;
+                } else {
+                    start = nxt.hdr;
+                    unit_ok = true;
+                }
+                cur = nxt;
+            }
+        }
+        // Every copy this warp started has landed before the CTA can exit.
+        for (uint32_t j = k > kSlots ? k - kSlots : 0; j < k; ++j)
+            if (!mbar_wait_bounded(&full[j % kSlots], (j / kSlots) & 1u, kWaitPolls)) {
+                status |= kErrTimeout;
+                break;
+            }
+        if (status && lane == 0) atomicOr(&a.status[0], status);
+        return;
+    }
+
+    // ------------------------------ consumers ------------------------------
     uint32_t status = 0;
-    int b = 0;
-    for (uint32_t item = begin; item < end; ++item, b ^= 1) {
-        const bool has_next = item + 1 < end;
-        // rate bytes two items ahead: their load overlaps this item's decode
-        if (item + 2 < end) next_item(a, nxt, nn);
-
-        // exclusive scan of this item's block sizes + total of the next item
-        const uint32_t sz = block_bytes(cur.rate);
-        uint32_t x = sz;
-#pragma unroll
-        for (int d = 1; d < 32; d <<= 1) {
-            const uint32_t y = __shfl_up_sync(0xffffffffu, x, d);
-            if (lane >= d) x += y;
+    const bool safe_fill = a.zero_fill != 0;
+    uint32_t k = 0;
+    for (uint32_t item = begin; item < end; ++item, ++k) {
+        const int slot = static_cast<int>(k % kSlots);
+        if (!mbar_wait_bounded(&full[slot], (k / kSlots) & 1u, kWaitPolls)) {
+            status |= kErrTimeout;
+            break;
         }
-        const uint32_t nrate = has_next ? nxt.rate : 0u;
-        uint32_t nsz = block_bytes(nrate), nbad = nrate > 31;
-#pragma unroll
-        for (int d = 16; d > 0; d >>= 1) {
-            nsz += __shfl_xor_sync(0xffffffffu, nsz, d);
-            nbad |= __shfl_xor_sync(0xffffffffu, nbad, d);
-        }
-        if (lane == 31) scan_w[warp] = x;
-        if (lane == 0) {
-            next_w[warp] = nsz;
-            bad_w[warp] = nbad;
-        }
-        __syncthreads();
-        uint32_t off = x - sz, next_total = 0;
-        nbad = 0;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-            off += w < warp ? scan_w[w] : 0u;
-            next_total += next_w[w];
-            nbad |= bad_w[w];
-        }
-        __syncthreads();
-
-        if (has_next) {
-            nxt.start = nxt.u == cur.u ? cur.start + cur.total : static_cast<uint64_t>(nxt.hdr);
-            nxt.total = next_total;
-            nxt.valid = (nxt.u == cur.u ? cur.valid : true) && !nbad && nxt.size >= nxt.hdr &&
-                        nxt.start + next_total <= nxt.size;
-            if (!nxt.valid && tid == 0) atomicOr(&a.status[nxt.u], kErrBadStream);
-            issue(nxt, b ^ 1);
-        }
-
-        // The tail words of this item's payload were stored by the threads
-        // before the scan's barriers; the TMA body completes on bar[b].
-        if (!mbar_wait_bounded(&bar[b], (parity >> b) & 1u, kWaitPolls)) status |= kErrTimeout;
-        parity ^= 1u << b;
-
-        if (cur.valid && tid < static_cast<int>(cur.nbs) && (cur.rate || a.zero_fill)) {
-            const uint32_t jb = cur.b0 + tid;
-            const uint32_t valid = min(cur.n - jb * kBlock, uint32_t(kBlock));
-            const float eb = cur.eb;
+        const uint8_t* base = smem + slot * kSlotBytes;
+        const SlotMeta m = meta[slot];
+        const uint32_t off = reinterpret_cast<const uint32_t*>(base + kOffsAt)[tid];
+        const uint32_t rate = base[kRatesAt + tid];
+        const uint32_t bytes = block_bytes(rate);
+        const bool readable = !(m.flags & kInSlot) || m.lead + off + bytes <= kPayloadCap;
+        if ((m.flags & kValid) && readable && static_cast<uint32_t>(tid) < m.nbs &&
+            (rate || safe_fill)) {
+            const uint32_t jb = m.b0 + tid;
+            const uint32_t valid = min(m.n - jb * kBlock, uint32_t(kBlock));
+            const float eb = m.eb;
             float f[32];
-            if (cur.rate) {
-                const uintptr_t g0 = reinterpret_cast<uintptr_t>(cur.stream + cur.start);
-                const uint32_t* words = reinterpret_cast<const uint32_t*>(
-                    smem + b * kBufStride + (g0 & 15u) + off);
+            if (rate) {
+                const uint32_t* words =
+                    (m.flags & kInSlot)
+                        ? reinterpret_cast<const uint32_t*>(base + m.lead + off)
+                        : reinterpret_cast<const uint32_t*>(m.payload + off);
                 // eb in [2^-100, 2^100]: every nonzero |q| * 2eb is a normal
                 // float, so one rounding of |q| * 2eb equals the reference's
                 // rounding of |q| * eb followed by an exact doubling.
                 const bool safe = eb >= 7.8886091e-31f && eb <= 1.2676506e30f;
-                if (cur.rate <= 15 && safe) {
+                if (rate <= 15 && safe) {
                     const float eb2 = __fmul_rn(eb, 2.0f);
-                    unpack_fast(words, cur.rate, eb2, __fmul_rn(eb2, -8388608.0f), f);
+                    unpack_fast(words, rate, eb2, __fmul_rn(eb2, -8388608.0f), f);
                 } else {
-                    unpack_general(words, cur.rate, eb, f);
+                    unpack_general(words, rate, eb, f);
                 }
             } else {
                 const float z = dequantize(0, eb);
 #pragma unroll
                 for (int v = 0; v < 32; ++v) f[v] = z;
             }
-            Unit unit;
-            unit.elems = a.units[cur.u].elems;
-            unit.n = cur.n;
-            write_block<T>(unit, a.maps[cur.map], cur.u, jb, valid, f);
+            write_block<T>(a, m, jb, valid, f);
         }
-        cur = nxt;
-        nxt = nn;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    if (status && tid == 0) atomicOr(&a.status[0], status);
+    if (status && lane == 0) atomicOr(&a.status[0], status);
 }
 
 int sm_count() {
@@ -426,7 +528,7 @@ cudaError_t launch_decode_t(const DecodeLaunch& l, cudaStream_t stream) {
     const uint32_t grid = l.total_items < ctas ? l.total_items : ctas;
     if (grid == 0) return cudaSuccess;
     note_launch();
-    decode_kernel<T><<<grid, kThreads, kSmem, stream>>>(args);
+    decode_kernel<T><<<grid, kCtaThreads, kSmem, stream>>>(args);
     return cudaGetLastError();
 }
 
