@@ -271,6 +271,23 @@ class OurCodec:
         self.bounds = (C.c_float * count)()
         self.offsets = (C.c_size_t * count)()
         self.total = C.c_size_t(0)
+        # store / restore pipeline (ckv_pipe_*): two page-locked host slabs;
+        # step k stores into slab k % 2 while restoring step k-1's slab
+        # one chunk per job: the codec is ~20x faster than the link, so a
+        # store and a restore in flight together keep both directions busy
+        # without splitting the job (smaller chunks bound the staging memory)
+        self.pipe = C.c_void_p()
+        self._check(self.lib.ckv_pipe_create(self.ctx, count, C.byref(self.pipe)), "pipe")
+        host_cap = int(self.lib.ckv_pipe_host_capacity(count, n))
+        self.hslab = [torch.empty(host_cap, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        self.hmeta = [{"offsets": (C.c_size_t * count)(), "sizes": (C.c_size_t * count)(),
+                       "bounds": (C.c_float * count)(), "total": C.c_size_t(0)} for _ in range(2)]
+        self.restored_e2e = torch.empty_like(pages_dev)
+        self.dst_e2e = _ckv.ptr_array([self.restored_e2e[i].data_ptr() for i in range(count)])
+        self.e2e_k = 0
+        self.t_store = 0
+        self.t_restore = 0
+        self.side = torch.cuda.Stream(device)
 
     def _check(self, status: int, what: str):
         if status != 0:
@@ -307,6 +324,41 @@ class OurCodec:
         ins = self.ckv.ptr_array([base + o for o in self.offsets])
         self.restore(ins)
         return total
+
+    def step_e2e_pipelined(self):
+        """Store this step's pages into one host slab while the previous
+        step's slab is restored: both directions of the link at once."""
+        k = self.e2e_k
+        self.e2e_k += 1
+        main = torch.cuda.current_stream(self.device)
+        a, b = self.hmeta[k % 2], self.hmeta[(k + 1) % 2]
+        prev_restore = self.t_restore   # the last reader of slab k % 2
+        restored = 0
+        if k > 0:
+            # queued first, on a side stream: the restore never blocks the
+            # host, so its copies start while the store below is being queued
+            self.side.wait_stream(main)
+            t_rest = C.c_uint64(0)
+            self._check(self.lib.ckv_pipe_restore_bf16(
+                self.pipe, self.hslab[(k + 1) % 2].data_ptr(), b["offsets"], b["sizes"],
+                b["bounds"], self.count, self.n, self.dst_e2e, self.t_store, C.byref(t_rest),
+                self.side.cuda_stream), "pipe restore")
+            self.t_restore = t_rest.value
+            restored = b["total"].value
+        t_store = C.c_uint64(0)
+        self._check(self.lib.ckv_pipe_store_bf16(
+            self.pipe, self.in_ptrs, None, self.count, self.n, self.hslab[k % 2].data_ptr(),
+            self.hslab[k % 2].numel(), a["offsets"], a["sizes"], a["bounds"],
+            C.byref(a["total"]), prev_restore, C.byref(t_store), main.cuda_stream), "pipe store")
+        self.t_store = t_store.value
+        self._check(self.lib.ckv_pipe_join(self.pipe, self.t_store, main.cuda_stream),
+                    "pipe join")
+        main.wait_stream(self.side)
+        return a["total"].value, restored
+
+    def e2e_matches(self) -> bool:
+        torch.cuda.synchronize(self.device)
+        return bool(torch.equal(self.restored_e2e.view(torch.int16), self.restored.view(torch.int16)))
 
     def kernel_ms(self, kind: int) -> float:
         ms = C.c_float(0.0)
@@ -439,6 +491,34 @@ def raw_pcie(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -
     return 2 * src.numel() / (statistics.mean(times) / 1e3) / 1e9
 
 
+def raw_pcie_duplex(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -> float:
+    """Raw pinned D2H and H2D of the uncompressed pages at the same time on two
+    streams (the link ceiling for a store overlapped with a restore)."""
+    src = pages_dev.view(-1).view(torch.uint8)
+    pinned_out = torch.empty(src.numel(), dtype=torch.uint8, pin_memory=True)
+    pinned_in = torch.empty(src.numel(), dtype=torch.uint8, pin_memory=True)
+    back = torch.empty_like(src)
+    s1 = torch.cuda.Stream(device)
+    s2 = torch.cuda.Stream(device)
+    main_stream = torch.cuda.current_stream(device)
+
+    def step():
+        s1.wait_stream(main_stream)
+        s2.wait_stream(main_stream)
+        with torch.cuda.stream(s1):
+            pinned_out.copy_(src, non_blocking=True)
+        with torch.cuda.stream(s2):
+            back.copy_(pinned_in, non_blocking=True)
+        main_stream.wait_stream(s1)
+        main_stream.wait_stream(s2)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(device)
+    times, _ = timed_steps(step, steps, flush, device)
+    return 2 * src.numel() / (statistics.mean(times) / 1e3) / 1e9
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -495,9 +575,12 @@ def main() -> int:
         return 0
 
     codec = OurCodec(device, pages_dev) if impl == "ours" else RefCodec(device, pages_dev)
+    pipelined = impl == "ours"
     for _ in range(args.warmup):
         codec.step()
         codec.step_e2e()
+        if pipelined:
+            codec.step_e2e_pipelined()
     torch.cuda.synchronize(device)
     ok = codec.verify()
 
@@ -525,24 +608,35 @@ def main() -> int:
         step_ms, _ = timed_steps(codec.step, args.steps, flush, device, after=kernel_times)
         barrier()
         launches_value = codec.launches() - launches0
-        e2e_ms, totals = timed_steps(codec.step_e2e, args.steps, flush, device)
+        e2e_ms, totals = timed_steps(
+            codec.step_e2e_pipelined if pipelined else codec.step_e2e, args.steps, flush, device)
         barrier()
     launches_total = codec.launches() - launches0
+    e2e_serial_ms = None
+    if pipelined:
+        # the same step through the plain calls: compress, pack, one D2H, one
+        # H2D, decompress, one after the other (outside the clock sampling)
+        e2e_serial_ms, _ = timed_steps(codec.step_e2e, args.steps, flush, device)
+        barrier()
     if impl == "ours":
         pack_ms.append(codec.kernel_ms(2))
     compressed = codec.compressed_bytes()
     ok = ok and codec.verify()
 
+    e2e_match = codec.e2e_matches() if pipelined else None
     t_step = sum(step_ms) / 1e3
     t_e2e = sum(e2e_ms) / 1e3
+    t_serial = sum(e2e_serial_ms) / 1e3 if e2e_serial_ms else 0.0
     if dist is not None:
-        t = torch.tensor([t_step, t_e2e], device=device, dtype=torch.float64)
+        t = torch.tensor([t_step, t_e2e, t_serial], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_step, t_e2e = float(t[0]), float(t[1])
+        t_step, t_e2e, t_serial = float(t[0]), float(t[1]), float(t[2])
     total_units = world * raw_bytes * 2 * args.steps
     value = total_units / t_step / 1e9
     e2e = total_units / t_e2e / 1e9
+    e2e_serial = total_units / t_serial / 1e9 if t_serial else None
     pcie = raw_pcie(pages_dev, min(args.steps, 10), flush, device) if rank == 0 else None
+    pcie_duplex = raw_pcie_duplex(pages_dev, min(args.steps, 10), flush, device) if rank == 0 else None
 
     if rank != 0:
         if dist is not None:
@@ -574,11 +668,21 @@ def main() -> int:
         "compression_ratio": round(raw_bytes / compressed, 4),
         "store_restore_ok": ok,
         "e2e": {"value": round(e2e, 3), "unit": "GB/s",
-                "h2d_bytes_per_step": int(totals[-1]) if totals else compressed,
-                "d2h_bytes_per_step": int(totals[-1]) if totals else compressed,
+                "h2d_bytes_per_step": (int(totals[-1][1]) if pipelined else int(totals[-1]))
+                if totals else compressed,
+                "d2h_bytes_per_step": (int(totals[-1][0]) if pipelined else int(totals[-1]))
+                if totals else compressed,
                 "ms_per_step": round(t_e2e * 1e3 / args.steps, 4),
+                "path": ("ckv_pipe_store_bf16 of step k's pages into one pinned slab, "
+                         "overlapped with ckv_pipe_restore_bf16 of step k-1's slab; one chunk per "
+                         "job") if pipelined else
+                        "compress, torch.cat pack, one D2H, one H2D, decompress (in order)",
+                "serial_value": round(e2e_serial, 3) if e2e_serial else None,
+                "restore_matches_kernel_path": e2e_match,
                 "pcie_raw_gbps": round(pcie, 3) if pcie else None,
-                "fraction_of_raw_pcie": round(e2e / pcie, 4) if pcie else None},
+                "pcie_raw_duplex_gbps": round(pcie_duplex, 3) if pcie_duplex else None,
+                "fraction_of_raw_pcie": round(e2e / (pcie_duplex if pipelined else pcie), 4)
+                if pcie and pcie_duplex else None},
     }
     if impl == "ours":
         enc = statistics.mean(enc_ms) / 1e3

@@ -194,6 +194,57 @@ CKV_API ckv_status ckv_pack(ckv_ctx* ctx, const uint8_t* const* srcs, const size
 CKV_API ckv_status ckv_set_kernel_timing(ckv_ctx* ctx, int enable);
 CKV_API ckv_status ckv_kernel_time(ckv_ctx* ctx, int kind, float* ms);
 
+/* Store / restore pipeline (replaces the job path of the reference's
+ * connector: CompressedPageStore.put_many_packed,
+ * vllm_v1_compressed_offload.py:371-447, which compresses a whole job, packs
+ * it with torch.cat into one pinned slab and synchronises; and
+ * _decompress_bundles_batched, :1618-1711, which copies the whole slab back
+ * before decoding; transfer_async, :2365-2385, orders the jobs).  A pipeline
+ * owns its CUDA streams (compute, device-to-host, host-to-device, decode)
+ * and double-buffered device staging, and runs a job in chunks of
+ * `chunk_pages` pages: the device-to-host copy of chunk k overlaps the
+ * compression of chunk k+1, the host-to-device copy of chunk k+1 the
+ * decompression of chunk k, and a store and a restore in flight together use
+ * both directions of the link.  Not thread-safe; one pipeline per context. */
+typedef struct ckv_pipe ckv_pipe;
+CKV_API ckv_status ckv_pipe_create(ckv_ctx* ctx, size_t chunk_pages, ckv_pipe** out);
+CKV_API void ckv_pipe_destroy(ckv_pipe* pipe);
+
+/* Compresses `count` BF16 pages of n elements (eps as in
+ * ckv_compress_batch_fixed_bf16) into page-locked host memory: page i at
+ * host + offsets[i] (16-byte aligned, pages packed in order), *total bytes
+ * used.  The compression waits for work already on `stream` (the pages);
+ * the copies wait for ticket `after` (0: none), e.g. a restore still reading
+ * the same host buffer.  Returns when sizes, bounds and offsets are on the
+ * host and every copy is queued; *ticket completes with the last copy. */
+CKV_API ckv_status ckv_pipe_store_bf16(ckv_pipe* pipe, const void* const* pages,
+                                       const float* eps, size_t count, size_t n,
+                                       uint8_t* host, size_t capacity, size_t* offsets,
+                                       size_t* sizes, float* bounds, size_t* total,
+                                       uint64_t after, uint64_t* ticket, void* stream);
+
+/* Decompresses `count` pages from page-locked host memory (offsets, sizes
+ * and bounds as a store returned them) into the BF16 pages dst[i] of n
+ * elements.  The copies wait for ticket `after` (0: none), e.g. the store
+ * that wrote the host buffer; the decode waits for work already on
+ * `stream`, and `stream` waits for the decode (asynchronous, like
+ * ckv_decompress_batch_fixed_bf16). */
+CKV_API ckv_status ckv_pipe_restore_bf16(ckv_pipe* pipe, const uint8_t* host,
+                                         const size_t* offsets, const size_t* sizes,
+                                         const float* bounds, size_t count, size_t n,
+                                         void* const* dst, uint64_t after, uint64_t* ticket,
+                                         void* stream);
+
+/* Make `stream` wait for a ticket (device side); wait for it on the host;
+ * query it (1 done, 0 pending, -1 unknown).  A pipeline keeps the last 64
+ * tickets. */
+CKV_API ckv_status ckv_pipe_join(ckv_pipe* pipe, uint64_t ticket, void* stream);
+CKV_API ckv_status ckv_pipe_wait(ckv_pipe* pipe, uint64_t ticket);
+CKV_API int ckv_pipe_done(ckv_pipe* pipe, uint64_t ticket);
+
+/* Host bytes that always hold `count` compressed pages of n elements. */
+CKV_API size_t ckv_pipe_host_capacity(size_t count, size_t n);
+
 /* ckv_compress_batch_fixed_bf16 for callers that cannot allocate memory.
  * No counterpart in the reference.  Some callers cannot call cudaMalloc when
  * they compress: a serving engine that reserved all free HBM for its KV

@@ -43,6 +43,8 @@ EXPORTS = (
     "ckv_decompress_batch_fixed_bf16_indexed_scatter", "ckv_set_zero_fill",
     "ckv_device_status", "ckv_kernel_launches", "ckv_pack",
     "ckv_set_kernel_timing", "ckv_kernel_time", "ckv_compress_batch_fixed_bf16_noalloc",
+    "ckv_pipe_create", "ckv_pipe_destroy", "ckv_pipe_store_bf16", "ckv_pipe_restore_bf16",
+    "ckv_pipe_join", "ckv_pipe_wait", "ckv_pipe_done", "ckv_pipe_host_capacity",
 )
 
 
@@ -97,6 +99,16 @@ def _declare(lib: C.CDLL) -> None:
         "ckv_kernel_time": (c_status, [P, c_int, C.POINTER(c_float)]),
         "ckv_compress_batch_fixed_bf16_noalloc": (
             c_status, [P, P, P, c_size, c_size, c_size, c_float, c_int, P, P, P]),
+        "ckv_pipe_create": (c_status, [P, c_size, C.POINTER(c_void_p)]),
+        "ckv_pipe_destroy": (None, [P]),
+        "ckv_pipe_store_bf16": (
+            c_status, [P, P, P, c_size, c_size, P, c_size, P, P, P, P, C.c_uint64, P, P]),
+        "ckv_pipe_restore_bf16": (
+            c_status, [P, P, P, P, P, c_size, c_size, P, C.c_uint64, P, P]),
+        "ckv_pipe_join": (c_status, [P, C.c_uint64, P]),
+        "ckv_pipe_wait": (c_status, [P, C.c_uint64]),
+        "ckv_pipe_done": (c_int, [P, C.c_uint64]),
+        "ckv_pipe_host_capacity": (c_size, [c_size, c_size]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

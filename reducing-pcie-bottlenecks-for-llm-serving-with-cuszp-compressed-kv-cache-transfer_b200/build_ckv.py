@@ -34,8 +34,12 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not _stale():
         return LIB
     LIB.parent.mkdir(parents=True, exist_ok=True)
-    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
-           "-Xcompiler", "-fvisibility=hidden", "-shared",
+    # -fmad=false: no multiply/add pair may be contracted into an FMA (the
+    # reference rounds its quantiser's and dequantiser's operations
+    # separately).  Intended FMAs are explicit fma intrinsics, which the flag
+    # does not touch.
+    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-fmad=false",
+           "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-shared",
            "-I", str(ROOT / "include"), "-I", str(CSRC)]
     if verbose:
         cmd += ["-Xptxas", "-v"]

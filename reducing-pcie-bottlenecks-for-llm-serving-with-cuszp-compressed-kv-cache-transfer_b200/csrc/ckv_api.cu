@@ -36,10 +36,15 @@ using ckv::Unit;
 
 namespace {
 
-constexpr int kSlots = 4;
+// Descriptor staging slots per context.  A slot is reused once the kernel that
+// read it has finished; enough of them that the calls of a store and a
+// restore in flight together (one slot per chunk launch) never wait on each
+// other.
+constexpr int kSlots = 32;
 
 struct Slot {
-    uint8_t* host = nullptr;   // pinned
+    uint8_t* host = nullptr;   // pinned, mapped
+    uint8_t* host_dev = nullptr;   // its device-side address
     uint8_t* dev = nullptr;
     size_t cap = 0;
     cudaEvent_t done = nullptr;
@@ -134,7 +139,8 @@ ckv_status acquire_slot(ckv_ctx* ctx, size_t need, Slot** out) {
         s.host = nullptr;
         s.dev = nullptr;
         s.cap = 0;
-        cudaError_t e = cudaMallocHost(&s.host, cap);
+        cudaError_t e = cudaHostAlloc(&s.host, cap, cudaHostAllocMapped);
+        if (e == cudaSuccess) e = cudaHostGetDevicePointer(&s.host_dev, s.host, 0);
         if (e != cudaSuccess) return cuda_fail(ctx, "allocating pinned descriptors", e);
         e = cudaMalloc(&s.dev, cap);
         if (e != cudaSuccess) return cuda_fail(ctx, "allocating device descriptors", e);
@@ -164,7 +170,7 @@ ckv_status upload(ckv_ctx* ctx, Batch& b, cudaStream_t stream, Slot** used,
     std::memcpy(h + units_bytes, b.maps.data(), b.maps.size() * sizeof(Map));
     if (!b.table.empty())
         std::memcpy(h + units_bytes + maps_bytes, b.table.data(), b.table.size() * sizeof(void*));
-    cudaError_t e = cudaMemcpyAsync(s.dev, h, need, cudaMemcpyHostToDevice, stream);
+    cudaError_t e = ckv::launch_fetch(s.host_dev, s.dev, need, stream);
     if (e != cudaSuccess) return cuda_fail(ctx, "uploading descriptors", e);
     *used = &s;
     *d_units = reinterpret_cast<const Unit*>(s.dev);
@@ -259,6 +265,9 @@ ckv_status run_encode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, size_t* sizes,
                     b.max_n, ckv::encode_max_elements(type));
     DeviceGuard guard(ctx->device);
     const size_t count = b.units.size();
+    for (size_t i = 0; i < count; ++i)   // the kernels write the bitstream as 32-bit words
+        if (reinterpret_cast<uintptr_t>(b.units[i].stream) & 3u)
+            return fail(ctx, CKV_ERR_ARGUMENT, "compressed output %zu is not 4-byte aligned", i);
     ckv_status st = ensure_results(ctx, count);
     if (st != CKV_OK) return st;
     std::memset(ctx->status, 0, count * sizeof(uint32_t));
@@ -763,7 +772,7 @@ ckv_status ckv_pack(ckv_ctx* ctx, const uint8_t* const* srcs, const size_t* size
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     DeviceGuard guard(ctx->device);
     Slot* slot = nullptr;
-    if (ckv_status st = acquire_slot(ctx, count * sizeof(ckv::PackUnit), &slot)) return st;
+    if (ckv_status st = acquire_slot(ctx, align16(count * sizeof(ckv::PackUnit)), &slot)) return st;
     auto* units = reinterpret_cast<ckv::PackUnit*>(slot->host);
     uint64_t pos = 0, max_size = 0;
     for (size_t i = 0; i < count; ++i) {
@@ -778,8 +787,8 @@ ckv_status ckv_pack(ckv_ctx* ctx, const uint8_t* const* srcs, const size_t* size
         return fail(ctx, CKV_ERR_CAPACITY, "packed size %llu exceeds capacity %zu",
                     static_cast<unsigned long long>(pos), capacity);
     *total = static_cast<size_t>(pos);
-    cudaError_t e = cudaMemcpyAsync(slot->dev, slot->host, count * sizeof(ckv::PackUnit),
-                                    cudaMemcpyHostToDevice, stream);
+    cudaError_t e = ckv::launch_fetch(slot->host_dev, slot->dev,
+                                      align16(count * sizeof(ckv::PackUnit)), stream);
     if (e != cudaSuccess) return cuda_fail(ctx, "uploading pack descriptors", e);
     timing_begin(ctx, 2, stream);
     e = ckv::launch_pack(reinterpret_cast<const ckv::PackUnit*>(slot->dev),
@@ -804,6 +813,323 @@ ckv_status ckv_kernel_time(ckv_ctx* ctx, int kind, float* ms) {
     if (e == cudaSuccess) e = cudaEventElapsedTime(ms, ctx->t_start[kind], ctx->t_stop[kind]);
     if (e != cudaSuccess) return cuda_fail(ctx, "reading kernel time", e);
     return CKV_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Store / restore pipeline (CompressedPageStore.put_many_packed,
+// vllm_v1_compressed_offload.py:371-447; _decompress_bundles_batched,
+// :1618-1711; transfer_async, :2365-2385).  The reference compresses a whole
+// job, packs it with torch.cat, copies it to a fresh pinned slab and
+// synchronises; on restore it copies the whole slab back before the first
+// decode.  Here a job runs in chunks of pages on the pipeline's own streams:
+// the device-to-host copy of chunk k overlaps the compression of chunk k+1,
+// the host-to-device copy of chunk k+1 the decompression of chunk k, and a
+// store and a restore issued together use both directions of the link.
+
+struct ckv_pipe {
+    ckv_ctx* ctx = nullptr;
+    size_t chunk = 0;   // pages per chunk
+    cudaStream_t s_enc = nullptr, s_d2h = nullptr, s_h2d = nullptr, s_dec = nullptr;
+    // two of each: per-page compressed staging, packed chunk, landing chunk
+    uint8_t* enc[2] = {nullptr, nullptr};
+    uint8_t* packed[2] = {nullptr, nullptr};
+    uint8_t* land[2] = {nullptr, nullptr};
+    size_t page_cap = 0;   // staging bytes per page
+    size_t land_cap = 0;   // landing bytes per buffer
+    cudaEvent_t ev_packed[2] = {nullptr, nullptr}, ev_copied[2] = {nullptr, nullptr};
+    cudaEvent_t ev_landed[2] = {nullptr, nullptr}, ev_decoded[2] = {nullptr, nullptr};
+    bool copied_used[2] = {false, false}, decoded_used[2] = {false, false};
+    cudaEvent_t ev_in = nullptr;
+    static constexpr int kTickets = 64;
+    cudaEvent_t tickets[kTickets] = {};
+    uint64_t next_ticket = 1;
+    std::vector<const uint8_t*> srcs;
+    std::vector<size_t> local;
+};
+
+namespace {
+
+// Largest compressed page of n elements: header plus every block at rate 32.
+size_t worst_page(size_t n) {
+    const size_t nb = (n + ckv::kBlock - 1) / ckv::kBlock;
+    const size_t hdr = (n + ckv::kGroup - 1) / ckv::kGroup * (ckv::kGroup / ckv::kBlock);
+    return align16(hdr + nb * (4 + 4 * 32));
+}
+
+ckv_status pipe_staging(ckv_pipe* p, size_t n) {
+    const size_t need = worst_page(n);
+    if (need <= p->page_cap) return CKV_OK;
+    for (int k = 0; k < 2; ++k) {
+        cudaFree(p->enc[k]);
+        cudaFree(p->packed[k]);
+        p->enc[k] = p->packed[k] = nullptr;
+    }
+    p->page_cap = 0;
+    for (int k = 0; k < 2; ++k) {
+        cudaError_t e = cudaMalloc(&p->enc[k], need * p->chunk);
+        if (e == cudaSuccess) e = cudaMalloc(&p->packed[k], need * p->chunk);
+        if (e != cudaSuccess) return cuda_fail(p->ctx, "allocating pipeline staging", e);
+    }
+    p->page_cap = need;
+    return CKV_OK;
+}
+
+ckv_status pipe_landing(ckv_pipe* p, size_t bytes) {
+    if (bytes <= p->land_cap) return CKV_OK;
+    for (int k = 0; k < 2; ++k) {
+        cudaFree(p->land[k]);
+        p->land[k] = nullptr;
+    }
+    p->land_cap = 0;
+    const size_t cap = align16(bytes);
+    for (int k = 0; k < 2; ++k) {
+        cudaError_t e = cudaMalloc(&p->land[k], cap);
+        if (e != cudaSuccess) return cuda_fail(p->ctx, "allocating pipeline landing", e);
+    }
+    p->land_cap = cap;
+    return CKV_OK;
+}
+
+cudaEvent_t pipe_ticket_event(ckv_pipe* p, uint64_t ticket) {
+    return p->tickets[ticket % ckv_pipe::kTickets];
+}
+
+// Records a new ticket on `stream`.
+ckv_status pipe_issue(ckv_pipe* p, cudaStream_t stream, uint64_t* ticket) {
+    const uint64_t t = p->next_ticket++;
+    cudaError_t e = cudaEventRecord(pipe_ticket_event(p, t), stream);
+    if (e != cudaSuccess) return cuda_fail(p->ctx, "recording a pipeline ticket", e);
+    if (ticket) *ticket = t;
+    return CKV_OK;
+}
+
+ckv_status pipe_after(ckv_pipe* p, uint64_t after, cudaStream_t stream) {
+    if (!after) return CKV_OK;
+    if (after >= p->next_ticket) return fail(p->ctx, CKV_ERR_ARGUMENT, "unknown ticket");
+    cudaError_t e = cudaStreamWaitEvent(stream, pipe_ticket_event(p, after), 0);
+    if (e != cudaSuccess) return cuda_fail(p->ctx, "ordering after a ticket", e);
+    return CKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+ckv_status ckv_pipe_create(ckv_ctx* ctx, size_t chunk_pages, ckv_pipe** out) {
+    if (check_ctx(ctx) || !out || chunk_pages == 0) return CKV_ERR_ARGUMENT;
+    *out = nullptr;
+    DeviceGuard guard(ctx->device);
+    auto* p = new ckv_pipe();
+    p->ctx = ctx;
+    p->chunk = chunk_pages;
+    cudaError_t e = cudaSuccess;
+    for (cudaStream_t* s : {&p->s_enc, &p->s_d2h, &p->s_h2d, &p->s_dec})
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(s, cudaStreamNonBlocking);
+    for (int k = 0; k < 2 && e == cudaSuccess; ++k)
+        for (cudaEvent_t* ev : {&p->ev_packed[k], &p->ev_copied[k], &p->ev_landed[k], &p->ev_decoded[k]})
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->ev_in, cudaEventDisableTiming);
+    for (int k = 0; k < ckv_pipe::kTickets && e == cudaSuccess; ++k)
+        e = cudaEventCreateWithFlags(&p->tickets[k], cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        ckv_pipe_destroy(p);
+        return cuda_fail(ctx, "creating the pipeline", e);
+    }
+    *out = p;
+    return CKV_OK;
+}
+
+void ckv_pipe_destroy(ckv_pipe* p) {
+    if (!p) return;
+    DeviceGuard guard(p->ctx->device);
+    for (cudaStream_t s : {p->s_enc, p->s_d2h, p->s_h2d, p->s_dec})
+        if (s) cudaStreamSynchronize(s);
+    for (int k = 0; k < 2; ++k) {
+        cudaFree(p->enc[k]);
+        cudaFree(p->packed[k]);
+        cudaFree(p->land[k]);
+        for (cudaEvent_t ev : {p->ev_packed[k], p->ev_copied[k], p->ev_landed[k], p->ev_decoded[k]})
+            if (ev) cudaEventDestroy(ev);
+    }
+    if (p->ev_in) cudaEventDestroy(p->ev_in);
+    for (cudaEvent_t ev : p->tickets)
+        if (ev) cudaEventDestroy(ev);
+    for (cudaStream_t s : {p->s_enc, p->s_d2h, p->s_h2d, p->s_dec})
+        if (s) cudaStreamDestroy(s);
+    delete p;
+}
+
+ckv_status ckv_pipe_store_bf16(ckv_pipe* p, const void* const* pages, const float* eps,
+                               size_t count, size_t n, uint8_t* host, size_t capacity,
+                               size_t* offsets, size_t* sizes, float* bounds, size_t* total,
+                               uint64_t after, uint64_t* ticket, void* stream_ptr) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    ckv_ctx* ctx = p->ctx;
+    ctx->err.clear();
+    if (!pages || !host || !offsets || !sizes || !bounds || !total || !fits_u32(n) || n == 0)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid pipeline store arguments");
+    if (ckv_status s = check_fixed(ctx, "pipeline store")) return s;
+    *total = 0;
+    if (count == 0) return pipe_issue(p, static_cast<cudaStream_t>(stream_ptr), ticket);
+    DeviceGuard guard(ctx->device);
+    if (ckv_status st = pipe_staging(p, n)) return st;
+    cudaStream_t caller = static_cast<cudaStream_t>(stream_ptr);
+    cudaError_t e = cudaEventRecord(p->ev_in, caller);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_enc, p->ev_in, 0);
+    if (e != cudaSuccess) return cuda_fail(ctx, "ordering the pipeline store", e);
+    if (ckv_status st = pipe_after(p, after, p->s_d2h)) return st;
+    size_t pos = 0;
+    for (size_t c0 = 0, c = 0; c0 < count; c0 += p->chunk, ++c) {
+        const int k = static_cast<int>(c & 1);
+        const size_t cnt = std::min(p->chunk, count - c0);
+        // the staging of chunk c - 2 has been copied out
+        if (p->copied_used[k] && (e = cudaStreamWaitEvent(p->s_enc, p->ev_copied[k], 0)))
+            return cuda_fail(ctx, "ordering the pipeline store", e);
+        Batch b;
+        b.maps.push_back(identity_map());
+        b.max_n = static_cast<uint32_t>(n);
+        p->srcs.resize(cnt);
+        for (size_t i = 0; i < cnt; ++i) {
+            const void* page = pages[c0 + i];
+            if (!page || (reinterpret_cast<uintptr_t>(page) & 1u))
+                return fail(ctx, CKV_ERR_ARGUMENT, "invalid page %zu", c0 + i);
+            Unit u{};
+            u.elems = page;
+            u.stream = p->enc[k] + i * p->page_cap;
+            u.capacity = p->page_cap;
+            u.n = static_cast<uint32_t>(n);
+            u.eb = eps_of(ctx, eps, c0 + i);
+            b.units.push_back(u);
+            p->srcs[i] = u.stream;
+        }
+        // compress (returns once the sizes are on the host), then pack
+        if (ckv_status st = run_encode(ctx, b, ckv::ElemType::kBF16, sizes + c0, bounds + c0, p->s_enc))
+            return st;
+        p->local.resize(cnt);
+        size_t ctotal = 0;
+        if (ckv_status st = ckv_pack(ctx, p->srcs.data(), sizes + c0, cnt, p->packed[k],
+                                     p->page_cap * p->chunk, 16, p->local.data(), &ctotal, p->s_enc))
+            return st;
+        if (pos + ctotal > capacity)
+            return fail(ctx, CKV_ERR_CAPACITY, "host buffer of %zu bytes too small", capacity);
+        e = cudaEventRecord(p->ev_packed[k], p->s_enc);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_d2h, p->ev_packed[k], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(host + pos, p->packed[k], ctotal, cudaMemcpyDeviceToHost, p->s_d2h);
+        if (e == cudaSuccess) e = cudaEventRecord(p->ev_copied[k], p->s_d2h);
+        if (e != cudaSuccess) return cuda_fail(ctx, "pipeline store copy", e);
+        p->copied_used[k] = true;
+        for (size_t i = 0; i < cnt; ++i) offsets[c0 + i] = pos + p->local[i];
+        pos = align16(pos + ctotal);
+    }
+    *total = pos;
+    return pipe_issue(p, p->s_d2h, ticket);
+}
+
+ckv_status ckv_pipe_restore_bf16(ckv_pipe* p, const uint8_t* host, const size_t* offsets,
+                                 const size_t* sizes, const float* bounds, size_t count, size_t n,
+                                 void* const* dst, uint64_t after, uint64_t* ticket,
+                                 void* stream_ptr) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    ckv_ctx* ctx = p->ctx;
+    ctx->err.clear();
+    if (!host || !offsets || !sizes || !bounds || !dst || !fits_u32(n) || n == 0)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid pipeline restore arguments");
+    if (ckv_status s = check_fixed(ctx, "pipeline restore")) return s;
+    cudaStream_t caller = static_cast<cudaStream_t>(stream_ptr);
+    if (count == 0) return pipe_issue(p, caller, ticket);
+    DeviceGuard guard(ctx->device);
+    // each chunk's pages are copied as one span of the host buffer
+    size_t span_max = 0;
+    for (size_t c0 = 0; c0 < count; c0 += p->chunk) {
+        const size_t cnt = std::min(p->chunk, count - c0);
+        size_t lo = SIZE_MAX, hi = 0;
+        for (size_t i = c0; i < c0 + cnt; ++i) {
+            if (sizes[i] == 0 || (offsets[i] & 3u) || !dst[i] ||
+                (reinterpret_cast<uintptr_t>(dst[i]) & 1u))
+                return fail(ctx, CKV_ERR_ARGUMENT, "invalid restored page %zu", i);
+            lo = std::min(lo, offsets[i]);
+            hi = std::max(hi, offsets[i] + sizes[i]);
+        }
+        span_max = std::max(span_max, hi - (lo & ~size_t(15)));
+    }
+    if (ckv_status st = pipe_landing(p, span_max)) return st;
+    cudaError_t e = cudaEventRecord(p->ev_in, caller);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_dec, p->ev_in, 0);
+    if (e != cudaSuccess) return cuda_fail(ctx, "ordering the pipeline restore", e);
+    if (ckv_status st = pipe_after(p, after, p->s_h2d)) return st;
+    for (size_t c0 = 0, c = 0; c0 < count; c0 += p->chunk, ++c) {
+        const int k = static_cast<int>(c & 1);
+        const size_t cnt = std::min(p->chunk, count - c0);
+        size_t lo = SIZE_MAX, hi = 0;
+        for (size_t i = c0; i < c0 + cnt; ++i) {
+            lo = std::min(lo, offsets[i]);
+            hi = std::max(hi, offsets[i] + sizes[i]);
+        }
+        lo &= ~size_t(15);
+        // the landing buffer of chunk c - 2 has been decoded
+        if (p->decoded_used[k] && (e = cudaStreamWaitEvent(p->s_h2d, p->ev_decoded[k], 0)))
+            return cuda_fail(ctx, "ordering the pipeline restore", e);
+        e = cudaMemcpyAsync(p->land[k], host + lo, hi - lo, cudaMemcpyHostToDevice, p->s_h2d);
+        if (e == cudaSuccess) e = cudaEventRecord(p->ev_landed[k], p->s_h2d);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_dec, p->ev_landed[k], 0);
+        if (e != cudaSuccess) return cuda_fail(ctx, "pipeline restore copy", e);
+        Batch b;
+        b.maps.push_back(identity_map());
+        b.max_n = static_cast<uint32_t>(n);
+        for (size_t i = c0; i < c0 + cnt; ++i) {
+            Unit u{};
+            u.elems = dst[i];
+            u.stream = p->land[k] + (offsets[i] - lo);
+            u.capacity = sizes[i];
+            u.n = static_cast<uint32_t>(n);
+            u.eb = bounds[i];
+            b.units.push_back(u);
+        }
+        if (ckv_status st = run_decode(ctx, b, ckv::ElemType::kBF16, p->s_dec)) return st;
+        if ((e = cudaEventRecord(p->ev_decoded[k], p->s_dec)))
+            return cuda_fail(ctx, "pipeline restore", e);
+        p->decoded_used[k] = true;
+    }
+    uint64_t t = 0;
+    if (ckv_status st = pipe_issue(p, p->s_dec, &t)) return st;
+    // like the reference's decompress calls: asynchronous on the caller's stream
+    e = cudaStreamWaitEvent(caller, pipe_ticket_event(p, t), 0);
+    if (e != cudaSuccess) return cuda_fail(ctx, "joining the pipeline restore", e);
+    if (ticket) *ticket = t;
+    return CKV_OK;
+}
+
+ckv_status ckv_pipe_join(ckv_pipe* p, uint64_t ticket, void* stream) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    DeviceGuard guard(p->ctx->device);
+    return pipe_after(p, ticket, static_cast<cudaStream_t>(stream));
+}
+
+ckv_status ckv_pipe_wait(ckv_pipe* p, uint64_t ticket) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    if (!ticket) return CKV_OK;
+    if (ticket >= p->next_ticket) return fail(p->ctx, CKV_ERR_ARGUMENT, "unknown ticket");
+    DeviceGuard guard(p->ctx->device);
+    cudaError_t e = cudaEventSynchronize(pipe_ticket_event(p, ticket));
+    if (e != cudaSuccess) return cuda_fail(p->ctx, "waiting for a pipeline ticket", e);
+    return CKV_OK;
+}
+
+int ckv_pipe_done(ckv_pipe* p, uint64_t ticket) {
+    if (!p || ticket >= p->next_ticket) return -1;
+    if (!ticket) return 1;
+    DeviceGuard guard(p->ctx->device);
+    const cudaError_t e = cudaEventQuery(pipe_ticket_event(p, ticket));
+    if (e == cudaSuccess) return 1;
+    if (e == cudaErrorNotReady) return 0;
+    return -1;
+}
+
+size_t ckv_pipe_host_capacity(size_t count, size_t n) {
+    return count * (worst_page(n) + 16);
 }
 
 }  // extern "C"

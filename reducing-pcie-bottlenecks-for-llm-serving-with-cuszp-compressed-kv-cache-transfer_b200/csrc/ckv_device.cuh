@@ -59,7 +59,7 @@ struct Unit {
     uint32_t n;
     uint32_t map;              // index into the launch's map table
     float eb;                  // encode: requested bound; decode: absolute bound
-    uint32_t item0;            // decode: index of the unit's first work item
+    uint32_t item0;            // index of the unit's first work item (decode) or chunk (encode)
 };
 
 // ---------------------------------------------------------------------------
@@ -113,12 +113,16 @@ __device__ __forceinline__ float bf16_hi(uint32_t w) {
 // ---------------------------------------------------------------------------
 // Register bit-matrix transposes.  A[i] is row i, bit b its column b.
 
+// Exchanges the bits of b selected by mask with the bits of a selected by
+// mask << J, written as two bit-selects (shift + 3-input logic op each).
 template <int J>
 __device__ __forceinline__ void delta_swap(uint32_t& a, uint32_t& b,
                                            uint32_t mask) {
-    const uint32_t t = ((a >> J) ^ b) & mask;
-    b ^= t;
-    a ^= t << J;
+    const uint32_t hi = mask << J;
+    const uint32_t na = (a & ~hi) | ((b << J) & hi);
+    const uint32_t nb = (b & ~mask) | ((a >> J) & mask);
+    a = na;
+    b = nb;
 }
 
 // The 8-bit step as two byte permutes.

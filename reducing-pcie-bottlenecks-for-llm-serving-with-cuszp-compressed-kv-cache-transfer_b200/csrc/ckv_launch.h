@@ -51,6 +51,9 @@ cudaError_t launch_encode(const EncodeLaunch& l, cudaStream_t stream);
 cudaError_t launch_decode(const DecodeLaunch& l, cudaStream_t stream);
 cudaError_t launch_pack(const PackUnit* units, uint32_t count, uint64_t max_size,
                         uint8_t* dst, cudaStream_t stream);
+// Copies `bytes` (a multiple of 16, both addresses 16-byte aligned) from
+// mapped page-locked host memory to device memory with a kernel.
+cudaError_t launch_fetch(const void* mapped_src, void* dst, size_t bytes, cudaStream_t stream);
 
 // Kernel launches made since load (tests and bench count them).
 uint64_t launches_issued();

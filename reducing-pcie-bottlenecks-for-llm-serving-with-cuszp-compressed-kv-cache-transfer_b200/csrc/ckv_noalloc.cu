@@ -112,7 +112,8 @@ extern "C" ckv_status ckv_compress_batch_fixed_bf16_noalloc(
     if (n > ckv::encode_max_elements(ckv::ElemType::kBF16)) return CKV_ERR_UNSUPPORTED;
     if (capacity < ckv_estimate_compressed_buffer_size(n * 4)) return CKV_ERR_ARGUMENT;
     for (size_t i = 0; i < batch; ++i)
-        if (!inputs[i] || !outputs[i] || (reinterpret_cast<uintptr_t>(inputs[i]) & 1u))
+        if (!inputs[i] || !outputs[i] || (reinterpret_cast<uintptr_t>(inputs[i]) & 1u) ||
+            (reinterpret_cast<uintptr_t>(outputs[i]) & 3u))
             return CKV_ERR_ARGUMENT;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     int device = 0;

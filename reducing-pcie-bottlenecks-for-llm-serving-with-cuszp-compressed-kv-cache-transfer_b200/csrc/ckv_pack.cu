@@ -33,7 +33,28 @@ __global__ void __launch_bounds__(kThreads) pack_kernel(const PackUnit* units,
     }
 }
 
+// Descriptor upload: one CTA copies `words` 16-byte words from mapped
+// page-locked host memory (read over PCIe by the SM) into device memory.  A
+// host-to-device cudaMemcpyAsync would queue on a copy engine behind any
+// large host-to-device copy in flight on another stream; this does not.
+__global__ void __launch_bounds__(kThreads) fetch_kernel(const uint4* src, uint4* dst,
+                                                         uint32_t words) {
+    for (uint32_t i = threadIdx.x; i < words; i += kThreads) dst[i] = src[i];
+}
+
 }  // namespace
+
+cudaError_t launch_fetch(const void* mapped_src, void* dst, size_t bytes, cudaStream_t stream) {
+    if (bytes == 0) return cudaSuccess;
+    if ((bytes & 15u) || ((reinterpret_cast<uintptr_t>(mapped_src) |
+                           reinterpret_cast<uintptr_t>(dst)) & 15u))
+        return cudaErrorInvalidValue;
+    note_launch();
+    fetch_kernel<<<1, kThreads, 0, stream>>>(static_cast<const uint4*>(mapped_src),
+                                            static_cast<uint4*>(dst),
+                                            static_cast<uint32_t>(bytes / 16));
+    return cudaGetLastError();
+}
 
 cudaError_t launch_pack(const PackUnit* units, uint32_t count, uint64_t max_size,
                         uint8_t* dst, cudaStream_t stream) {
