@@ -33,13 +33,15 @@ __global__ void __launch_bounds__(kThreads) pack_kernel(const PackUnit* units,
     }
 }
 
-// Descriptor upload: one CTA copies `words` 16-byte words from mapped
-// page-locked host memory (read over PCIe by the SM) into device memory.  A
-// host-to-device cudaMemcpyAsync would queue on a copy engine behind any
-// large host-to-device copy in flight on another stream; this does not.
+// Descriptor upload: copies `words` 16-byte words from mapped page-locked
+// host memory (read over PCIe by the SMs) into device memory, one word per
+// thread so that the whole copy is one PCIe round trip.  A host-to-device
+// cudaMemcpyAsync would queue on a copy engine behind any large
+// host-to-device copy in flight on another stream; this does not.
 __global__ void __launch_bounds__(kThreads) fetch_kernel(const uint4* src, uint4* dst,
                                                          uint32_t words) {
-    for (uint32_t i = threadIdx.x; i < words; i += kThreads) dst[i] = src[i];
+    const uint32_t i = blockIdx.x * kThreads + threadIdx.x;
+    if (i < words) dst[i] = src[i];
 }
 
 }  // namespace
@@ -49,10 +51,10 @@ cudaError_t launch_fetch(const void* mapped_src, void* dst, size_t bytes, cudaSt
     if ((bytes & 15u) || ((reinterpret_cast<uintptr_t>(mapped_src) |
                            reinterpret_cast<uintptr_t>(dst)) & 15u))
         return cudaErrorInvalidValue;
+    const uint32_t words = static_cast<uint32_t>(bytes / 16);
     note_launch();
-    fetch_kernel<<<1, kThreads, 0, stream>>>(static_cast<const uint4*>(mapped_src),
-                                            static_cast<uint4*>(dst),
-                                            static_cast<uint32_t>(bytes / 16));
+    fetch_kernel<<<(words + kThreads - 1) / kThreads, kThreads, 0, stream>>>(
+        static_cast<const uint4*>(mapped_src), static_cast<uint4*>(dst), words);
     return cudaGetLastError();
 }
 

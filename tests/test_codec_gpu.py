@@ -331,7 +331,7 @@ def test_indexed_groups_one_launch(cpp, co):
     before = cpp.kernel_launches()
     ok, sizes, bounds = w.compress_batch_fixed_bf16_indexed_groups(
         inputs, outs, groups, [3, 3], prefix, layers, epl, eps)
-    # one encode kernel for all groups (and its one-CTA descriptor copy)
+    # one encode kernel for all groups (and its descriptor fetch kernel)
     assert ok and cpp.kernel_launches() - before == 2
     for k in range(6):
         sel = high if k < 3 else low
