@@ -241,6 +241,117 @@ def cpu_baseline(host_pages: torch.Tensor, reps: int = 1) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# Same-run comparison points for the page codec: the reference connector's
+# other codecs -- zstd level 1 and LZ4 through the system libraries (as its
+# native_lossless.py binds them) and per-page INT8 absmax quantisation
+# (vllm_v1_compressed_offload.py:711-724) -- on a bounded sample of pages.
+
+
+def _load_c_codecs():
+    import ctypes.util
+    libs = {}
+    zpath, lpath = ctypes.util.find_library("zstd"), ctypes.util.find_library("lz4")
+    if zpath:
+        z = C.CDLL(zpath)
+        z.ZSTD_compressBound.argtypes = [C.c_size_t]
+        z.ZSTD_compressBound.restype = C.c_size_t
+        z.ZSTD_compress.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_int]
+        z.ZSTD_compress.restype = C.c_size_t
+        z.ZSTD_decompress.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]
+        z.ZSTD_decompress.restype = C.c_size_t
+        z.ZSTD_isError.argtypes = [C.c_size_t]
+        z.ZSTD_isError.restype = C.c_uint
+        libs["zstd1"] = (
+            lambda n: int(z.ZSTD_compressBound(n)),
+            lambda dst, cap, src, n: int(z.ZSTD_compress(dst, cap, src, n, 1)),
+            lambda dst, cap, src, n: int(z.ZSTD_decompress(dst, cap, src, n)))
+    if lpath:
+        lz = C.CDLL(lpath)
+        lz.LZ4_compressBound.argtypes = [C.c_int]
+        lz.LZ4_compressBound.restype = C.c_int
+        lz.LZ4_compress_default.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+        lz.LZ4_compress_default.restype = C.c_int
+        lz.LZ4_decompress_safe.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+        lz.LZ4_decompress_safe.restype = C.c_int
+        libs["lz4"] = (
+            lambda n: int(lz.LZ4_compressBound(n)),
+            lambda dst, cap, src, n: int(lz.LZ4_compress_default(src, dst, n, cap)),
+            lambda dst, cap, src, n: int(lz.LZ4_decompress_safe(src, dst, n, cap)))
+    return libs
+
+
+def codec_baselines(host_pages: torch.Tensor, pages_dev: torch.Tensor, sample: int = 32) -> dict:
+    from concurrent.futures import ThreadPoolExecutor
+    out = {"sample": f"{sample} pages x {host_pages.shape[1]} BF16 (lossless and CPU INT8); "
+                     f"all {pages_dev.shape[0]} pages (GPU INT8)"}
+    pages = [np.ascontiguousarray(host_pages[i].view(torch.int16).numpy()) for i in range(sample)]
+    raw = sum(p.nbytes for p in pages)
+    threads = os.cpu_count() or 1
+    for name, (bound, comp, decomp) in _load_c_codecs().items():
+        cap = bound(pages[0].nbytes)
+        bufs = [np.empty(cap, dtype=np.uint8) for _ in pages]
+        back = [np.empty_like(p) for p in pages]
+        sizes = [0] * len(pages)
+
+        def enc(i):
+            sizes[i] = comp(bufs[i].ctypes.data, cap, pages[i].ctypes.data, pages[i].nbytes)
+
+        def dec(i):
+            decomp(back[i].ctypes.data, back[i].nbytes, bufs[i].ctypes.data, sizes[i])
+
+        res = {}
+        for label, workers in (("1_thread", 1), (f"{threads}_threads", threads)):
+            with ThreadPoolExecutor(workers) as pool:
+                t0 = time.perf_counter()
+                list(pool.map(enc, range(len(pages))))
+                t1 = time.perf_counter()
+                list(pool.map(dec, range(len(pages))))
+                t2 = time.perf_counter()
+            res[label] = {"store_gbps": round(raw / (t1 - t0) / 1e9, 3),
+                          "restore_gbps": round(raw / (t2 - t1) / 1e9, 3)}
+        assert all(np.array_equal(a, b) for a, b in zip(pages, back))
+        res["ratio"] = round(raw / sum(sizes), 4)
+        out[name] = res
+
+    def int8_store(x):
+        f = x.float()
+        scale = f.abs().amax(dim=1, keepdim=True) / 127.0
+        scale = torch.where(scale == 0, torch.ones_like(scale), scale)
+        return torch.clamp(torch.round(f / scale), -127, 127).to(torch.int8), scale
+
+    def int8_restore(q, scale):
+        return (q.float() * scale).to(torch.bfloat16)
+
+    cpu = host_pages[:sample]
+    torch.set_num_threads(threads)
+    t0 = time.perf_counter()
+    q, sc = int8_store(cpu)
+    t1 = time.perf_counter()
+    int8_restore(q, sc)
+    t2 = time.perf_counter()
+    out["int8_cpu_torch"] = {"store_gbps": round(raw / (t1 - t0) / 1e9, 3),
+                             "restore_gbps": round(raw / (t2 - t1) / 1e9, 3),
+                             "ratio": round(cpu.numel() * 2 / (cpu.numel() + 4 * sample), 4),
+                             "threads": threads}
+    dev = pages_dev.device
+    for _ in range(2):
+        qg, sg = int8_store(pages_dev)
+        int8_restore(qg, sg)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    e[0].record()
+    qg, sg = int8_store(pages_dev)
+    e[1].record()
+    int8_restore(qg, sg)
+    e[2].record()
+    torch.cuda.synchronize(dev)
+    rawg = pages_dev.numel() * 2
+    out["int8_gpu_torch"] = {"store_gbps": round(rawg / (e[0].elapsed_time(e[1]) / 1e3) / 1e9, 1),
+                             "restore_gbps": round(rawg / (e[1].elapsed_time(e[2]) / 1e3) / 1e9, 1),
+                             "ratio": round(rawg / (pages_dev.numel() + 4 * pages_dev.shape[0]), 4)}
+    return out
+
+
+# ---------------------------------------------------------------------------
 # Our arm: libckv through its C ABI.
 
 
@@ -491,6 +602,21 @@ def raw_pcie(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -
     return 2 * src.numel() / (statistics.mean(times) / 1e3) / 1e9
 
 
+def slowest_rank(seconds: list[float], dist=None, device=None) -> list[float]:
+    """Each timed region's duration on the slowest rank (max over ranks; the
+    identity on one process)."""
+    if dist is None:
+        return list(seconds)
+    t = torch.tensor(seconds, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
+def job_rate(world: int, raw_bytes: int, steps: int, seconds: float) -> float:
+    """Whole-job GB/s: every rank stores and restores its raw_bytes each step."""
+    return world * raw_bytes * 2 * steps / seconds / 1e9
+
+
 def raw_pcie_duplex(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -> float:
     """Raw pinned D2H and H2D of the uncompressed pages at the same time on two
     streams (the link ceiling for a store overlapped with a restore)."""
@@ -624,17 +750,12 @@ def main() -> int:
     ok = ok and codec.verify()
 
     e2e_match = codec.e2e_matches() if pipelined else None
-    t_step = sum(step_ms) / 1e3
-    t_e2e = sum(e2e_ms) / 1e3
-    t_serial = sum(e2e_serial_ms) / 1e3 if e2e_serial_ms else 0.0
-    if dist is not None:
-        t = torch.tensor([t_step, t_e2e, t_serial], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_step, t_e2e, t_serial = float(t[0]), float(t[1]), float(t[2])
-    total_units = world * raw_bytes * 2 * args.steps
-    value = total_units / t_step / 1e9
-    e2e = total_units / t_e2e / 1e9
-    e2e_serial = total_units / t_serial / 1e9 if t_serial else None
+    t_step, t_e2e, t_serial = slowest_rank(
+        [sum(step_ms) / 1e3, sum(e2e_ms) / 1e3, sum(e2e_serial_ms) / 1e3 if e2e_serial_ms else 0.0],
+        dist, device)
+    value = job_rate(world, raw_bytes, args.steps, t_step)
+    e2e = job_rate(world, raw_bytes, args.steps, t_e2e)
+    e2e_serial = job_rate(world, raw_bytes, args.steps, t_serial) if t_serial else None
     pcie = raw_pcie(pages_dev, min(args.steps, 10), flush, device) if rank == 0 else None
     pcie_duplex = raw_pcie_duplex(pages_dev, min(args.steps, 10), flush, device) if rank == 0 else None
 
@@ -718,6 +839,8 @@ def main() -> int:
                                   "built unchanged in oracle/_ref, driven like CuSZpWrapper")
         line["gpu_launches"] = None
     line["cpu_baseline"] = cpu
+    if cpu is not None:
+        line["codec_baselines"] = codec_baselines(host, pages_dev)
     line["clocks"] = clocks.summary()
     print(json.dumps(line))
     if dist is not None:
