@@ -1,0 +1,461 @@
+"""Compressed KV-page offload jobs: GPU blocks -> page-locked host memory -> GPU blocks.
+
+The job layer of the reference's vLLM connector
+(integration/compression_pipeline/vllm_v1_compressed_offload.py), for its
+fixed-mode BF16 path, on top of libckv's store / restore pipeline
+(``ckv_pipe_*``):
+
+* ``BundleComponent`` / ``EncodedSegment`` / ``CompressedBundle`` -- the
+  reference's per-page host metadata (:58-88), same fields;
+* ``CompressedPageStore`` -- host storage shared by both directions
+  (:360-457).  The reference packs each store job with ``torch.cat`` into a
+  freshly allocated pinned slab and synchronises; here a job is written by
+  the pipeline into a pinned slab taken from a reusable pool, and the slab
+  starts with a self-describing header and page table (``JobHeader``), so a
+  stored job can be validated and restored from its bytes alone;
+* ``CompressedOffloadingHandler`` -- ``transfer_async`` / ``get_finished`` /
+  ``wait`` / ``shutdown`` (:2365-2410) over vLLM-style specs (anything with a
+  ``block_ids`` array, e.g. ``GPULoadStoreSpec`` / ``CPULoadStoreSpec``);
+  page addresses come from the block ids in one vector operation (no
+  per-page Python, the reference's ``_compress_fixed_bundles_batched`` loops
+  over pages, :825-1028);
+* ``CompressedCpuGpuOffloadingHandlers`` -- the pair of handlers (:2412-2470),
+  sharing one store and one pipeline, so that a load is ordered after the
+  store that wrote its pages on the device.
+
+A KV cache here is one contiguous tensor ``[num_blocks, *page_shape]`` of
+BF16 pages (the cross-layer page layout the reference compresses as one
+unit, e.g. ``[2, layers, heads, 16, head_dim]``).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import struct
+import threading
+from dataclasses import dataclass, field
+from typing import Any, Iterable, Sequence
+
+import numpy as np
+import torch
+
+import _ckv
+
+# --------------------------------------------------------------------------
+# Host metadata (vllm_v1_compressed_offload.py:58-88)
+
+
+@dataclass
+class BundleComponent:
+    tensor_idx: int
+    original_shape: tuple[int, ...]
+    original_dtype: torch.dtype
+    numel: int
+    layer_axis: int | None = None
+    layer_indices: tuple[int, ...] = ()
+    destination_view_shape: tuple[int, ...] = ()
+
+
+@dataclass
+class EncodedSegment:
+    payload: torch.Tensor            # view of the job's pinned slab
+    compressed_size: int
+    actual_error_bound: float
+    encoding: str
+    components: tuple[BundleComponent, ...]
+    unpadded_numel: int
+    compressed_numel: int
+    original_bytes: int
+    requested_error_bound: float
+    quant_scale: float | None = None
+    cuszp_mode: str | None = None
+
+
+@dataclass
+class CompressedBundle:
+    segments: tuple[EncodedSegment, ...]
+    compressed_size: int
+    original_bytes: int
+
+
+@dataclass
+class TransferResult:
+    """vLLM's ``TransferResult`` fields (vllm.v1.kv_offload.worker.worker)."""
+
+    job_id: int
+    success: bool
+    transfer_size: int | None = None
+    transfer_time: float | None = None
+    transfer_type: Any = None
+
+
+# --------------------------------------------------------------------------
+# On-host job format
+
+
+class JobHeader:
+    """Header and page table at the start of a job's slab.
+
+    Layout (little-endian): magic b"CKVJ", u16 version, u16 element type
+    (0 BF16), u32 page count, u64 elements per page, u64 payload bytes, f32
+    requested bound, u32 flags (bit 0: relative bound), then per page u64
+    offset (from the payload start), u64 size, f32 absolute bound, u32 zero;
+    the payload starts at the next 256-byte boundary.
+    """
+
+    MAGIC = b"CKVJ"
+    VERSION = 1
+    _HEAD = struct.Struct("<4sHHIQQfI")
+    _PAGE = np.dtype([("offset", "<u8"), ("size", "<u8"), ("bound", "<f4"), ("zero", "<u4")])
+
+    @classmethod
+    def bytes_for(cls, count: int) -> int:
+        return (cls._HEAD.size + count * cls._PAGE.itemsize + 255) // 256 * 256
+
+    @classmethod
+    def write(cls, slab: torch.Tensor, n: int, eps: float, relative: bool, offsets, sizes,
+              bounds, payload_bytes: int) -> None:
+        count = len(offsets)
+        buf = slab[: cls.bytes_for(count)].numpy()
+        buf[: cls._HEAD.size] = np.frombuffer(
+            cls._HEAD.pack(cls.MAGIC, cls.VERSION, 0, count, n, payload_bytes, eps,
+                           1 if relative else 0), dtype=np.uint8)
+        table = np.zeros(count, dtype=cls._PAGE)
+        table["offset"] = np.ctypeslib.as_array(offsets)
+        table["size"] = np.ctypeslib.as_array(sizes)
+        table["bound"] = np.ctypeslib.as_array(bounds)
+        start = cls._HEAD.size
+        buf[start:start + table.nbytes] = table.view(np.uint8)
+
+    @classmethod
+    def read(cls, slab: torch.Tensor) -> dict:
+        """The job's description, validated against the slab."""
+        raw = slab[: cls._HEAD.size].numpy().tobytes()
+        if len(raw) < cls._HEAD.size:
+            raise ValueError("slab shorter than a job header")
+        magic, version, etype, count, n, payload, eps, flags = cls._HEAD.unpack(raw)
+        if magic != cls.MAGIC or version != cls.VERSION or etype != 0:
+            raise ValueError("not a compressed KV job (bad magic, version or element type)")
+        hdr = cls.bytes_for(count)
+        if slab.numel() < hdr + payload:
+            raise ValueError("slab shorter than its header says")
+        table = np.frombuffer(slab[cls._HEAD.size:cls._HEAD.size + count * cls._PAGE.itemsize]
+                              .numpy().tobytes(), dtype=cls._PAGE)
+        if np.any(table["offset"] + table["size"] > payload) or np.any(table["size"] == 0):
+            raise ValueError("page table points outside the payload")
+        return {"count": count, "n": n, "eps": eps, "relative": bool(flags & 1),
+                "payload_at": hdr, "payload_bytes": payload,
+                "offsets": table["offset"].astype(np.uint64),
+                "sizes": table["size"].astype(np.uint64),
+                "bounds": table["bound"].astype(np.float32)}
+
+
+# --------------------------------------------------------------------------
+# Host storage (vllm_v1_compressed_offload.py:360-457)
+
+
+@dataclass
+class _Slab:
+    buffer: torch.Tensor             # pinned
+    payload_at: int = 0              # header and page table bytes
+    ticket: int = 0                  # store ticket that fills it
+    readers: int = 0                 # last restore ticket reading it
+    pages: set[int] = field(default_factory=set)
+
+
+@dataclass
+class _PageRecord:
+    slab: int
+    offset: int                      # from the slab's payload start
+    size: int
+    bound: float
+    n: int
+
+
+class CompressedPageStore:
+    """Host storage for compressed pages, shared by both transfer directions.
+
+    ``put_many_packed`` / ``get`` keep the reference's names.  A job's pages
+    live in one pinned slab from a pool; a slab goes back to the pool when
+    none of its pages is referenced any more (overwritten or evicted)."""
+
+    def __init__(self, allocate=None):
+        # page-locked host buffers by default (the pipeline's copies need them)
+        self._allocate = allocate or (
+            lambda n: torch.empty(n, dtype=torch.uint8, pin_memory=True))
+        self._pages: dict[int, _PageRecord] = {}
+        self._bundles: dict[int, CompressedBundle] = {}
+        self._slabs: dict[int, _Slab] = {}
+        self._free: list[tuple[torch.Tensor, int]] = []   # (buffer, last reader ticket)
+        self._next_slab = 0
+        self._lock = threading.Lock()
+
+    # -- slabs
+    def _take_slab(self, nbytes: int, payload_at: int, settle) -> int:
+        """A slab of at least nbytes; `settle(ticket)` waits on the host
+        for the last restore that read a recycled buffer."""
+        with self._lock:
+            best = None
+            for i, (buf, _t) in enumerate(self._free):
+                if buf.numel() >= nbytes and (best is None or
+                                               buf.numel() < self._free[best][0].numel()):
+                    best = i
+            buf, last = self._free.pop(best) if best is not None else (None, 0)
+            sid = self._next_slab
+            self._next_slab += 1
+        if buf is None:
+            buf = self._allocate(nbytes)
+        elif last:
+            settle(last)   # its header is rewritten on the host right away
+        with self._lock:
+            self._slabs[sid] = _Slab(buf, payload_at)
+        return sid
+
+    def slab(self, sid: int) -> _Slab:
+        return self._slabs[sid]
+
+    def _drop(self, cpu_block_id: int) -> None:
+        rec = self._pages.pop(cpu_block_id, None)
+        self._bundles.pop(cpu_block_id, None)
+        if rec is None:
+            return
+        slab = self._slabs[rec.slab]
+        slab.pages.discard(cpu_block_id)
+        if not slab.pages:
+            del self._slabs[rec.slab]
+            self._free.append((slab.buffer, max(slab.readers, slab.ticket)))
+
+    # -- the reference's interface
+    def put_many_packed(self, entries: Iterable[tuple[int, _PageRecord, CompressedBundle]]) -> None:
+        with self._lock:
+            for cpu_block_id, rec, bundle in entries:
+                self._drop(cpu_block_id)
+                self._pages[cpu_block_id] = rec
+                self._bundles[cpu_block_id] = bundle
+                self._slabs[rec.slab].pages.add(cpu_block_id)
+
+    def get(self, cpu_block_id: int) -> CompressedBundle:
+        with self._lock:
+            bundle = self._bundles.get(cpu_block_id)
+        if bundle is None:
+            raise KeyError(f"compressed bundle not found for CPU block {cpu_block_id}")
+        return bundle
+
+    def record(self, cpu_block_id: int) -> _PageRecord:
+        with self._lock:
+            rec = self._pages.get(cpu_block_id)
+        if rec is None:
+            raise KeyError(f"compressed bundle not found for CPU block {cpu_block_id}")
+        return rec
+
+    def evict(self, cpu_block_ids: Iterable[int]) -> None:
+        with self._lock:
+            for b in cpu_block_ids:
+                self._drop(int(b))
+
+    def __len__(self) -> int:
+        return len(self._pages)
+
+
+# --------------------------------------------------------------------------
+# Handlers (vllm_v1_compressed_offload.py:481-2470)
+
+
+def _block_ids(spec: Any) -> np.ndarray:
+    ids = getattr(spec, "block_ids", spec)
+    return np.asarray(ids, dtype=np.int64).reshape(-1)
+
+
+class _Engine:
+    """One libckv context and pipeline per KV cache, shared by both handlers."""
+
+    def __init__(self, kv_cache: torch.Tensor, error_bound: float, device_id: int,
+                 chunk_pages: int):
+        if kv_cache.dtype != torch.bfloat16 or not kv_cache.is_cuda or not kv_cache.is_contiguous():
+            raise ValueError("kv_cache must be a contiguous BF16 CUDA tensor [num_blocks, ...]")
+        self.lib = _ckv.load()
+        self.kv = kv_cache
+        self.device = kv_cache.device
+        self.n = kv_cache[0].numel()
+        self.page_bytes = self.n * 2
+        self.error_bound = float(error_bound)
+        self.ctx = C.c_void_p()
+        cfg = _ckv.Config(self.error_bound, 1, _ckv.DIM_1D, _ckv.MODE_FIXED, _ckv.TYPE_FLOAT)
+        self._check(self.lib.ckv_create(cfg, int(device_id), C.byref(self.ctx)), "ckv_create")
+        self.pipe = C.c_void_p()
+        self._check(self.lib.ckv_pipe_create(self.ctx, int(chunk_pages), C.byref(self.pipe)),
+                    "ckv_pipe_create")
+        self.lock = threading.Lock()
+
+    def _check(self, status: int, what: str) -> None:
+        if status != 0:
+            raise RuntimeError(f"{what}: {_ckv.error_message(self.lib, self.ctx, status)}")
+
+    def page_ptrs(self, block_ids: np.ndarray) -> C.Array:
+        if block_ids.size and (block_ids.min() < 0 or block_ids.max() >= self.kv.shape[0]):
+            raise IndexError("GPU block id out of range")
+        addrs = np.uint64(self.kv.data_ptr()) + block_ids.astype(np.uint64) * np.uint64(self.page_bytes)
+        return (C.c_void_p * len(addrs)).from_buffer_copy(addrs.astype(np.uint64).tobytes())
+
+    def close(self) -> None:
+        if self.pipe:
+            self.lib.ckv_pipe_destroy(self.pipe)
+            self.pipe = C.c_void_p()
+        if self.ctx:
+            self.lib.ckv_destroy(self.ctx)
+            self.ctx = C.c_void_p()
+
+
+class CompressedOffloadingHandler:
+    """One transfer direction.  ``transfer_async(job_id, (src_spec, dst_spec))``
+    with GPU block ids on the GPU side and CPU block ids (keys of the page
+    store) on the CPU side."""
+
+    def __init__(self, engine: _Engine, store: CompressedPageStore, gpu_to_cpu: bool,
+                 error_bound: float | None = None):
+        self.engine = engine
+        self.store = store
+        self.gpu_to_cpu = bool(gpu_to_cpu)
+        self.error_bound = float(engine.error_bound if error_bound is None else error_bound)
+        self.transfer_type = ("GPU", "CPU") if gpu_to_cpu else ("CPU", "GPU")
+        self._pending: dict[int, tuple[list[int], int]] = {}   # job -> (tickets, bytes)
+        self._finished: list[TransferResult] = []
+        self._lock = threading.Lock()
+
+    # -- one job
+    def _store(self, gpu_ids: np.ndarray, cpu_ids: np.ndarray) -> tuple[list[int], int]:
+        e = self.engine
+        count = len(gpu_ids)
+        hdr = JobHeader.bytes_for(count)
+        cap = int(e.lib.ckv_pipe_host_capacity(count, e.n))
+        sid = self.store._take_slab(hdr + cap, hdr,
+                                    lambda t: e._check(e.lib.ckv_pipe_wait(e.pipe, t), "wait"))
+        slab = self.store.slab(sid)
+        offsets = (C.c_size_t * count)()
+        sizes = (C.c_size_t * count)()
+        bounds = (C.c_float * count)()
+        total = C.c_size_t(0)
+        ticket = C.c_uint64(0)
+        eps = (C.c_float * count)(*([self.error_bound] * count))
+        stream = torch.cuda.current_stream(e.device).cuda_stream
+        e._check(e.lib.ckv_pipe_store_bf16(
+            e.pipe, e.page_ptrs(gpu_ids), eps, count, e.n, slab.buffer.data_ptr() + hdr, cap,
+            offsets, sizes, bounds, C.byref(total), slab.readers, C.byref(ticket), stream),
+            "store")
+        slab.ticket = ticket.value
+        JobHeader.write(slab.buffer, e.n, self.error_bound, True, offsets, sizes, bounds,
+                        total.value)
+        entries = []
+        for i in range(count):
+            rec = _PageRecord(sid, int(offsets[i]), int(sizes[i]), float(bounds[i]), e.n)
+            payload = slab.buffer[hdr + rec.offset: hdr + rec.offset + rec.size]
+            comp = BundleComponent(0, tuple(e.kv.shape[1:]), torch.bfloat16, e.n)
+            seg = EncodedSegment(payload, rec.size, rec.bound, "cuszp", (comp,), e.n, e.n,
+                                 e.page_bytes, self.error_bound, cuszp_mode="fixed")
+            entries.append((int(cpu_ids[i]), rec, CompressedBundle((seg,), rec.size, e.page_bytes)))
+        self.store.put_many_packed(entries)
+        return [ticket.value], int(total.value)
+
+    def _load(self, cpu_ids: np.ndarray, gpu_ids: np.ndarray) -> tuple[list[int], int]:
+        e = self.engine
+        recs = [self.store.record(int(c)) for c in cpu_ids]
+        by_slab: dict[int, list[int]] = {}
+        for i, r in enumerate(recs):
+            by_slab.setdefault(r.slab, []).append(i)
+        tickets, nbytes = [], 0
+        stream = torch.cuda.current_stream(e.device).cuda_stream
+        for sid, idx in by_slab.items():
+            slab = self.store.slab(sid)
+            count = len(idx)
+            offsets = (C.c_size_t * count)(*[recs[i].offset for i in idx])
+            sizes = (C.c_size_t * count)(*[recs[i].size for i in idx])
+            bounds = (C.c_float * count)(*[recs[i].bound for i in idx])
+            base = slab.buffer.data_ptr() + slab.payload_at
+            ticket = C.c_uint64(0)
+            e._check(e.lib.ckv_pipe_restore_bf16(
+                e.pipe, base, offsets, sizes, bounds, count, e.n,
+                e.page_ptrs(gpu_ids[np.asarray(idx)]), slab.ticket, C.byref(ticket), stream),
+                "restore")
+            slab.readers = ticket.value
+            tickets.append(ticket.value)
+            nbytes += sum(sizes)
+        return tickets, nbytes
+
+    # -- the OffloadingHandler interface (vLLM)
+    def transfer_async(self, job_id: int, spec: Sequence[Any]) -> bool:
+        src, dst = spec
+        src_ids, dst_ids = _block_ids(src), _block_ids(dst)
+        if len(src_ids) != len(dst_ids):
+            raise ValueError("GPU/CPU block specification length mismatch")
+        with self.engine.lock:
+            if len(src_ids) == 0:
+                tickets, nbytes = [], 0
+            elif self.gpu_to_cpu:
+                tickets, nbytes = self._store(src_ids, dst_ids)
+            else:
+                tickets, nbytes = self._load(src_ids, dst_ids)
+        with self._lock:
+            self._pending[int(job_id)] = (tickets, nbytes)
+        return True
+
+    def get_finished(self) -> list[TransferResult]:
+        """Jobs finished since the last call (a pipeline keeps its last 64
+        tickets: poll at least that often)."""
+        lib, pipe = self.engine.lib, self.engine.pipe
+        with self._lock:
+            done = []
+            for job_id, (tickets, nbytes) in self._pending.items():
+                states = [lib.ckv_pipe_done(pipe, t) for t in tickets]
+                if all(s != 0 for s in states):
+                    done.append((job_id, all(s == 1 for s in states), nbytes))
+            for job_id, ok, nbytes in done:
+                del self._pending[job_id]
+                self._finished.append(TransferResult(job_id, ok, nbytes,
+                                                     transfer_type=self.transfer_type))
+            out, self._finished = self._finished, []
+        return out
+
+    def wait(self, job_ids: set[int]) -> None:
+        lib, pipe = self.engine.lib, self.engine.pipe
+        with self._lock:
+            tickets = [t for j in job_ids for t in self._pending.get(int(j), ([], 0))[0]]
+        for t in tickets:
+            self.engine._check(lib.ckv_pipe_wait(pipe, t), "wait")
+
+    def shutdown(self) -> None:
+        with self._lock:
+            pending = list(self._pending)
+        self.wait(set(pending))
+
+
+class CompressedCpuGpuOffloadingHandlers:
+    """Both directions over one KV cache (vllm_v1_compressed_offload.py:2412-2470)."""
+
+    def __init__(self, kv_cache: torch.Tensor, error_bound: float = 1e-4, device_id: int = 0,
+                 chunk_pages: int = 64):
+        self.engine = _Engine(kv_cache, error_bound, device_id, chunk_pages)
+        self.store = CompressedPageStore()
+        self.gpu_to_cpu_handler = CompressedOffloadingHandler(self.engine, self.store, True)
+        self.cpu_to_gpu_handler = CompressedOffloadingHandler(self.engine, self.store, False)
+
+    def shutdown(self) -> None:
+        self.gpu_to_cpu_handler.shutdown()
+        self.cpu_to_gpu_handler.shutdown()
+        self.engine.close()
+
+
+def restore_job(slab: torch.Tensor, dst_pages: Sequence[torch.Tensor], engine: _Engine) -> int:
+    """Restores every page of a job from its slab bytes alone (the header and
+    page table), e.g. after the slab was written to a file and read back.
+    Returns the pipeline ticket."""
+    job = JobHeader.read(slab)
+    if job["n"] != engine.n or len(dst_pages) != job["count"]:
+        raise ValueError("job does not match the destination pages")
+    count = job["count"]
+    ticket = C.c_uint64(0)
+    engine._check(engine.lib.ckv_pipe_restore_bf16(
+        engine.pipe, slab.data_ptr() + job["payload_at"],
+        (C.c_size_t * count)(*job["offsets"].tolist()), (C.c_size_t * count)(*job["sizes"].tolist()),
+        (C.c_float * count)(*job["bounds"].tolist()), count, engine.n,
+        _ckv.ptr_array([p.data_ptr() for p in dst_pages]), 0, C.byref(ticket),
+        torch.cuda.current_stream(engine.device).cuda_stream), "restore")
+    return ticket.value

@@ -1,0 +1,184 @@
+"""The offload job layer (kv_offload.py): on-host job format and page store on
+CPU; store / load jobs through the handlers against the plain calls on GPU."""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import kv_offload as ko
+
+
+# ---------------------------------------------------------------- CPU
+
+
+def test_job_header_round_trip():
+    count, n = 5, 229376
+    offsets = (C.c_size_t * count)(0, 320, 704, 1024, 4096)
+    sizes = (C.c_size_t * count)(300, 384, 300, 3000, 16)
+    bounds = (C.c_float * count)(1e-4, 2e-4, 3e-4, 4e-4, 5e-4)
+    hdr = ko.JobHeader.bytes_for(count)
+    assert hdr % 256 == 0
+    slab = torch.zeros(hdr + 4112, dtype=torch.uint8)
+    ko.JobHeader.write(slab, n, 1e-5, True, offsets, sizes, bounds, 4112)
+    job = ko.JobHeader.read(slab)
+    assert job["count"] == count and job["n"] == n and job["relative"]
+    assert job["payload_at"] == hdr and job["payload_bytes"] == 4112
+    assert np.float32(job["eps"]) == np.float32(1e-5)
+    assert job["offsets"].tolist() == list(offsets)
+    assert job["sizes"].tolist() == list(sizes)
+    assert job["bounds"].tolist() == [np.float32(b) for b in bounds]
+
+
+def test_job_header_rejects_bad_slabs():
+    count = 2
+    offsets = (C.c_size_t * count)(0, 64)
+    sizes = (C.c_size_t * count)(64, 64)
+    bounds = (C.c_float * count)(1.0, 1.0)
+    hdr = ko.JobHeader.bytes_for(count)
+    slab = torch.zeros(hdr + 128, dtype=torch.uint8)
+    ko.JobHeader.write(slab, 1000, 1e-4, False, offsets, sizes, bounds, 128)
+    ko.JobHeader.read(slab)
+    bad = slab.clone()
+    bad[0] = ord("X")
+    with pytest.raises(ValueError):
+        ko.JobHeader.read(bad)
+    with pytest.raises(ValueError):
+        ko.JobHeader.read(slab[: hdr + 64])          # payload cut short
+    big = (C.c_size_t * count)(64, 200)
+    ko.JobHeader.write(slab, 1000, 1e-4, False, offsets, big, bounds, 128)
+    with pytest.raises(ValueError):
+        ko.JobHeader.read(slab)                       # page past the payload
+
+
+def test_page_store_overwrite_evict_and_recycle():
+    store = ko.CompressedPageStore(allocate=lambda n: torch.empty(n, dtype=torch.uint8))
+    buffers = []
+
+    def slab_with(pages):
+        sid = store._take_slab(1024, 256, lambda t: None)
+        buffers.append(store.slab(sid).buffer)
+        entries = []
+        for k, cpu in enumerate(pages):
+            rec = ko._PageRecord(sid, 64 * k, 64, 0.5, 32)
+            entries.append((cpu, rec, ko.CompressedBundle((), 64, 64)))
+        store.put_many_packed(entries)
+        return sid
+
+    slab_with([1, 2, 3])
+    assert len(store) == 3 and store.record(2).offset == 64
+    s2 = slab_with([3, 4])             # block 3 moves to the new slab
+    assert store.record(3).slab == s2 and len(store) == 4
+    store.evict([1, 2])                # the first slab is unreferenced now
+    assert len(store._free) == 1 and store._free[0][0] is buffers[0]
+    with pytest.raises(KeyError):
+        store.get(1)
+    s3 = slab_with([7])                # reuses the freed buffer
+    assert store.slab(s3).buffer is buffers[0] and not store._free
+
+
+# ---------------------------------------------------------------- GPU
+
+
+def _kv(blocks, page_shape, seed):
+    g = torch.Generator().manual_seed(seed)
+    n = int(np.prod(page_shape))
+    scale = torch.empty(page_shape[-1]).log_normal_(0.0, 0.5, generator=g)
+    x = torch.randn(blocks, n, generator=g) * scale.repeat(n // page_shape[-1])
+    return x.to(torch.bfloat16).view(blocks, *page_shape)
+
+
+@pytest.mark.gpu
+def test_handlers_store_then_load_match_plain_calls():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    import cuszp_wrapper_cpp as cpp
+
+    shape = (2, 28, 2, 16, 128)
+    kv = _kv(64, shape, seed=11).cuda()
+    h = ko.CompressedCpuGpuOffloadingHandlers(kv, error_bound=1e-5, device_id=0, chunk_pages=16)
+    try:
+        gpu_ids = np.array([3, 9, 10, 11, 40, 63, 0, 5, 22, 31], dtype=np.int64)
+        cpu_ids = np.arange(100, 100 + len(gpu_ids), dtype=np.int64)
+        assert h.gpu_to_cpu_handler.transfer_async(1, (gpu_ids, cpu_ids))
+        h.gpu_to_cpu_handler.wait({1})
+        done = h.gpu_to_cpu_handler.get_finished()
+        assert [(r.job_id, r.success) for r in done] == [(1, True)]
+
+        # the same pages through the plain wrapper calls
+        cfg = cpp.CompressionConfig(error_bound=1e-5, use_relative_error=True,
+                                    processing_dim=cpp.CuszpDim.DIM_1D,
+                                    encoding_mode=cpp.CuszpMode.MODE_FIXED,
+                                    data_type=cpp.CuszpType.TYPE_FLOAT)
+        w = cpp.CuSZpWrapper(cfg, 0)
+        n = kv[0].numel()
+        pages = [kv[i].view(-1) for i in gpu_ids]
+        outs = [torch.empty(w.estimate_compressed_buffer_size(n * 4), dtype=torch.uint8,
+                            device="cuda") for _ in pages]
+        ok, sizes, bounds = w.compress_batch_fixed_bf16(pages, outs, [1e-5] * len(pages))
+        assert ok
+        for k, cpu in enumerate(cpu_ids):
+            seg = h.store.get(int(cpu)).segments[0]
+            assert seg.compressed_size == sizes[k]
+            assert np.float32(seg.actual_error_bound) == np.float32(bounds[k])
+            assert torch.equal(seg.payload, outs[k][: sizes[k]].cpu())
+
+        # load into other GPU blocks, in another order
+        dst_gpu = np.array([50, 51, 52, 53, 54, 55, 56, 57, 58, 59], dtype=np.int64)
+        order = np.array([9, 0, 1, 8, 2, 7, 3, 6, 4, 5])
+        assert h.cpu_to_gpu_handler.transfer_async(2, (cpu_ids[order], dst_gpu))
+        h.cpu_to_gpu_handler.wait({2})
+        assert [r.success for r in h.cpu_to_gpu_handler.get_finished()] == [True]
+        restored = torch.zeros(len(pages) * n, dtype=torch.bfloat16, device="cuda")
+        assert w.decompress_batch_fixed_bf16(outs, sizes, restored, n, bounds)
+        torch.cuda.synchronize()
+        ref = restored.view(len(pages), n)
+        for j, k in enumerate(order):
+            assert torch.equal(kv[dst_gpu[j]].view(-1).view(torch.int16), ref[k].view(torch.int16))
+
+        # the job restored from its slab bytes alone
+        slab = h.store.slab(h.store.record(int(cpu_ids[0])).slab).buffer
+        dst = [torch.empty(n, dtype=torch.bfloat16, device="cuda") for _ in pages]
+        t = ko.restore_job(slab, dst, h.engine)
+        assert h.engine.lib.ckv_pipe_wait(h.engine.pipe, t) == 0
+        for k in range(len(pages)):
+            assert torch.equal(dst[k].view(torch.int16), ref[k].view(torch.int16))
+    finally:
+        h.shutdown()
+
+
+@pytest.mark.gpu
+def test_handlers_overlapping_jobs_and_slab_reuse():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    shape = (2, 4, 2, 16, 128)
+    kv = _kv(96, shape, seed=12).cuda()
+    snapshot = kv.clone()
+    h = ko.CompressedCpuGpuOffloadingHandlers(kv, error_bound=1e-4, device_id=0, chunk_pages=8)
+    try:
+        # store blocks 0-31 as job 1, 32-63 as job 2; load job 1's pages into
+        # 64-95 while job 2 is still being stored
+        h.gpu_to_cpu_handler.transfer_async(1, (np.arange(0, 32), np.arange(1000, 1032)))
+        h.gpu_to_cpu_handler.transfer_async(2, (np.arange(32, 64), np.arange(2000, 2032)))
+        h.cpu_to_gpu_handler.transfer_async(3, (np.arange(1000, 1032), np.arange(64, 96)))
+        h.gpu_to_cpu_handler.wait({1, 2})
+        h.cpu_to_gpu_handler.wait({3})
+        torch.cuda.synchronize()
+        first = kv[64:96].clone()
+        # overwrite job 1's CPU blocks (its slab returns to the pool) and
+        # load them again: the decode must match the first load bit for bit
+        h.store.evict(range(1000, 1032))
+        h.gpu_to_cpu_handler.transfer_async(4, (np.arange(0, 32), np.arange(1000, 1032)))
+        h.cpu_to_gpu_handler.transfer_async(5, (np.arange(1000, 1032), np.arange(64, 96)))
+        h.cpu_to_gpu_handler.wait({5})
+        torch.cuda.synchronize()
+        assert torch.equal(kv[64:96].view(torch.int16), first.view(torch.int16))
+        assert torch.equal(kv[:64].view(torch.int16), snapshot[:64].view(torch.int16))
+        err = (kv[64:96].float() - snapshot[:32].float()).abs()
+        assert bool((err <= 1e-4 * 2 * snapshot[:32].float().abs().amax() + 1e-7 +
+                     snapshot[:32].float().abs() * 2 ** -8).all())
+        got = {r.job_id for r in h.gpu_to_cpu_handler.get_finished()}
+        got |= {r.job_id for r in h.cpu_to_gpu_handler.get_finished()}
+        assert got == {1, 2, 3, 4, 5}
+    finally:
+        h.shutdown()
