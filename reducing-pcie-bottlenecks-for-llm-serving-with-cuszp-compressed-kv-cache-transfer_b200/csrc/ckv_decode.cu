@@ -59,6 +59,7 @@ struct DecodeArgs {
     uint32_t uniform_items;   // items per unit when all units are equal, else 0
     uint32_t zero_fill;
     uint32_t* status;
+    ShiftMul mul;
 };
 
 // What the consumers need of the item a slot holds.
@@ -113,27 +114,30 @@ __device__ __forceinline__ void unpack_general(const uint32_t* words, uint32_t r
 }
 
 // Values of one block for rate <= 15 with a "safe" bound: the sign word goes
-// to bit 15 of every row, so row = |q| | sign << 15.
+// to bit 15 of every row, so row = |q| | sign << 15.  Rows k < 16 sit in the
+// low half of A[k], rows k >= 16 in the high half of A[k - 16]; the moves of
+// a row into place are multiplies (FMA pipe), the masks and the sign flip
+// one bit select each.
 __device__ __forceinline__ void unpack_fast(const uint32_t* words, uint32_t rate, float eb2,
-                                            float negc, float (&f)[32]) {
+                                            float negc, const ShiftMul& mul, float (&f)[32]) {
     uint32_t A[16];
 #pragma unroll
     for (int b = 0; b < 15; ++b) A[b] = b < static_cast<int>(rate) ? words[1 + b] : 0u;
     A[15] = words[0];
-    transpose16(A);
+    transpose16_mul(A, mul);
 #pragma unroll
     for (int v = 0; v < 32; ++v) {
         const int k = bitpos(v);
         uint32_t mag, sign;
         if (k < 16) {
-            mag = A[k] & 0x7fffu;
-            sign = (A[k] << 16) & 0x80000000u;
+            mag = A[k];
+            sign = A[k] * mul.r16;             // row bit 15 -> bit 31
         } else {
-            mag = (A[k - 16] >> 16) & 0x7fffu;
-            sign = A[k - 16] & 0x80000000u;
+            mag = __umulhi(A[k - 16], mul.r16);   // high half -> low half
+            sign = A[k - 16];
         }
-        const float x = __fmaf_rn(__uint_as_float(0x4b000000u | mag), eb2, negc);
-        f[v] = __uint_as_float(__float_as_uint(x) ^ sign);
+        const float x = __fmaf_rn(__uint_as_float(0x4b000000u | (mag & 0x7fffu)), eb2, negc);
+        f[v] = __uint_as_float(__float_as_uint(x) ^ (sign & 0x80000000u));
     }
 }
 
@@ -486,7 +490,7 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
                 const bool safe = eb >= 7.8886091e-31f && eb <= 1.2676506e30f;
                 if (rate <= 15 && safe) {
                     const float eb2 = __fmul_rn(eb, 2.0f);
-                    unpack_fast(words, rate, eb2, __fmul_rn(eb2, -8388608.0f), f);
+                    unpack_fast(words, rate, eb2, __fmul_rn(eb2, -8388608.0f), a.mul, f);
                 } else {
                     unpack_general(words, rate, eb, f);
                 }
@@ -523,7 +527,7 @@ cudaError_t launch_decode_t(const DecodeLaunch& l, cudaStream_t stream) {
                                            kSmem);
     if (err != cudaSuccess) return err;
     DecodeArgs args{l.units, l.maps, l.num_units, l.total_items, l.uniform_items,
-                    l.zero_fill ? 1u : 0u, l.status};
+                    l.zero_fill ? 1u : 0u, l.status, shift_mul()};
     const uint32_t ctas = static_cast<uint32_t>(sm_count() * kCtasPerSm);
     const uint32_t grid = l.total_items < ctas ? l.total_items : ctas;
     if (grid == 0) return cudaSuccess;

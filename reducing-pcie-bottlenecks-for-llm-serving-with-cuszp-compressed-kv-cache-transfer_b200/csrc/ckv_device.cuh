@@ -150,6 +150,50 @@ __device__ __forceinline__ void transpose16(uint32_t (&A)[16]) {
         if (!(k & 1)) delta_swap<1>(A[k], A[k + 1], 0x55555555u);
 }
 
+// Multipliers that stand for shifts: x << J == x * 2^J and x >> J ==
+// umulhi(x, 2^(32-J)).  They reach the kernels as launch arguments, so the
+// compiler cannot turn the multiplies back into shifts: an integer
+// multiply-add issues to the FMA pipe, a shift to the integer ALU pipe, and
+// the bit-matrix transposes are otherwise all ALU work.
+struct ShiftMul {
+    uint32_t l4, l2, l1;    // 2^4, 2^2, 2^1
+    uint32_t r4, r2, r1;    // 2^28, 2^30, 2^31
+    uint32_t r16;           // 2^16
+    uint32_t neg3;          // 2^32 - 3: x * neg3 == -3x
+};
+
+inline ShiftMul shift_mul() {
+    return ShiftMul{1u << 4, 1u << 2, 1u << 1, 1u << 28, 1u << 30, 1u << 31, 1u << 16, 0xFFFFFFFDu};
+}
+
+// delta_swap with the two shifts done as multiplies (lmul = 2^J,
+// rmul = 2^(32-J)).
+template <int J>
+__device__ __forceinline__ void delta_swap_mul(uint32_t& a, uint32_t& b, uint32_t mask,
+                                               uint32_t lmul, uint32_t rmul) {
+    const uint32_t hi = mask << J;
+    const uint32_t na = (a & ~hi) | ((b * lmul) & hi);
+    const uint32_t nb = (b & ~mask) | (__umulhi(a, rmul) & mask);
+    a = na;
+    b = nb;
+}
+
+// transpose16 with its 4-, 2- and 1-bit steps split between the integer
+// ALU (bit selects) and the FMA pipe (shifts as multiplies).
+__device__ __forceinline__ void transpose16_mul(uint32_t (&A)[16], const ShiftMul& m) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) swap8(A[k], A[k + 8]);
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+        if (!(k & 4)) delta_swap_mul<4>(A[k], A[k + 4], 0x0F0F0F0Fu, m.l4, m.r4);
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+        if (!(k & 2)) delta_swap_mul<2>(A[k], A[k + 2], 0x33333333u, m.l2, m.r2);
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+        if (!(k & 1)) delta_swap_mul<1>(A[k], A[k + 1], 0x55555555u, m.l1, m.r1);
+}
+
 // Full 32x32 transpose (rows of up to 32 bits).
 __device__ __forceinline__ void transpose32(uint32_t (&A)[32]) {
 #pragma unroll
@@ -250,6 +294,91 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar,
     for (uint32_t i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
+}
+
+// ---- cluster-scope barriers (distributed shared memory exchanges) ----------
+
+// Address of the same shared variable in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+    return r;
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (address from
+// cluster_addr); orders this thread's earlier stores, peer stores included.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar)
+                 : "memory");
+}
+
+// Non-blocking test (acquire at cluster scope) of the phase with the given
+// parity.
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for the phase with the given parity of a barrier that peers of the
+// cluster arrive on, polling without suspending (a suspended try_wait is
+// woken late by remote arrivals); gives up after `limit` polls.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity,
+                                                          uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_test_wait_cluster(bar, parity)) return true;
+    return false;
+}
+
+// Asynchronous store into another CTA's shared memory that completes
+// `bytes` of transaction count on that CTA's mbarrier (both addresses from
+// cluster_addr).  No fence orders it after this thread's earlier writes.
+__device__ __forceinline__ void st_async_f32x2(uint32_t remote, float a, float b,
+                                               uint32_t remote_bar) {
+    asm volatile(
+        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+            remote),
+        "f"(a), "f"(b), "r"(remote_bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void st_async_u32(uint32_t remote, uint32_t v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+                     remote),
+                 "r"(v), "r"(remote_bar)
+                 : "memory");
+}
+
+// Non-blocking test of the phase with the given parity (acquire, CTA scope).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Polls a barrier that completes by transaction count from other CTAs
+// without suspending; gives up after `limit` polls.
+__device__ __forceinline__ bool mbar_spin_bounded(uint64_t* bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_test_wait(bar, parity)) return true;
+    return false;
+}
+
+// Cluster-wide barrier that does not require converged warps.
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 // 1-D bulk copy global -> this CTA's shared memory (16-byte aligned

@@ -1,42 +1,52 @@
-// Single-pass clustered encoder for the fixed-mode codec (sm_100a).
+// Persistent clustered encoder for the fixed-mode codec (sm_100a).
 //
-// One thread-block cluster encodes one unit (a KV page, or the selected
-// layers of one).  Each CTA of the cluster owns a contiguous slice of the
-// unit's 32-element blocks and keeps that slice in shared memory for the
-// whole encode, so HBM is read once and written once:
+// A thread-block cluster of c CTAs (one CTA per SM) walks a list of units
+// (KV pages, or the selected layers of one); every CTA of the cluster owns
+// the same contiguous slice of each unit's 32-element blocks.  A slice is
+// read from HBM once (TMA bulk copies into shared memory) and its compressed
+// bytes are written once.  Each CTA keeps three slices in flight and splits
+// its warps by role so that copies, cluster exchanges and arithmetic of
+// neighbouring units overlap:
 //
-//   1. TMA bulk copies bring the slice into shared memory (one copy per
-//      contiguous run of the element map);
-//   2. per block, min / max / NaN-presence (packed BF16 min/max);
-//   3. the CTAs exchange their slice extremes through distributed shared
-//      memory (each CTA stores into every peer before a cluster barrier and
-//      reads locally after it) -> every CTA resolves the same absolute bound
-//      eb = eps * fmaxf(max - min, 1e-6f) (cuszp_batched_fixed.cu:55-133);
-//   4. per block rate = bit length of max(|q(block min)|, |q(block max)|)
-//      -- the quantiser is monotone, so the extremes give the block's
-//      largest |q| (NaN contributes |q| = 1) -- one CTA scan gives every
-//      block's payload offset, and the CTAs exchange their slice byte totals
-//      -> each CTA knows where its output starts; no look-back chain, no
-//      global scratch;
-//   5. per round of 256 blocks (one per thread): quantise the 32 values,
-//      transpose them into the sign word and bit planes in registers, and
-//      write them IN PLACE over the already consumed input in shared memory
-//      (a block of rate <= 15 packs into at most the 64 bytes it came from);
-//      at the end one TMA bulk store writes the slice's payload.
+//   producer warp    bulk-loads slice j into buffer j % 3 as soon as unit
+//                    j-3 has been packed out of it;
+//   analysis warps   per unit: block min / max / NaN-presence (packed BF16
+//                    min/max); slice extremes pushed into every CTA of the
+//                    cluster (distributed shared memory stores + an arrive on
+//                    the receiver's mbarrier) -> absolute bound
+//                    eb = eps * fmaxf(max - min, 1e-6f)
+//                    (cuszp_batched_fixed.cu:55-133); per block rate = bit
+//                    length of max(|q(block min)|, |q(block max)|) (the
+//                    quantiser is monotone; NaN contributes |q| = 1); a scan
+//                    gives every block's payload offset; slice byte totals
+//                    pushed into every CTA -> this slice's output offset,
+//                    header rate bytes; then the unit is handed to the pack
+//                    warps;
+//   pack warps       32-block chunks, dealt round-robin across units so no
+//                    warp waits for another: quantise, transpose into sign
+//                    word + bit planes in registers, compact the chunk's
+//                    payload in place over its own input (a block of rate
+//                    <= 15 packs into at most the 64 bytes it came from; a
+//                    warp barrier suffices) and copy it out with coalesced
+//                    stores.
 //
 // Rate <= 15 blocks without NaN (every block at REL bounds >= 1e-5 on
 // two-sided data) use a quantiser that truncates with a round-toward-zero
 // add of 2^23 instead of a float->int conversion; it gives the reference's
-// integer for |q| < 2^15.  Other blocks use the reference's exact
-// instruction sequence and are written straight to global memory.
+// integer for |q| < 2^15.  A chunk with any other block uses the reference's
+// exact instruction sequence and is written straight to global memory.
 //
-// The rate found in step 5 from the values themselves is checked against
-// the one from step 4; a mismatch sets kErrRateCheck.
+// The rate found while packing from the values themselves is checked
+// against the one from the extremes; a mismatch sets kErrRateCheck.  Every
+// wait is bounded; a wait that runs out sets kErrTimeout on the cluster's
+// units and every role stops after the copies it issued have landed.
 #include "ckv_launch.h"
 
 #include <cooperative_groups.h>
 
 #include <cfloat>
+#include <map>
+#include <mutex>
 
 namespace cg = cooperative_groups;
 
@@ -44,11 +54,19 @@ namespace ckv {
 namespace {
 
 constexpr uint32_t kSliceBytes = 64 * 1024;
-constexpr uint32_t kGuard = 16;     // in-place output may start up to 15 bytes early
 constexpr uint32_t kMaxCluster = 16;
 constexpr uint32_t kWaitPolls = 1u << 24;
 constexpr uint32_t kMaxPieces = 512;
 constexpr uint8_t kNanFlag = 0x80;
+constexpr uint32_t kBufs = 3;       // slices (and per-unit metadata sets) in flight per CTA
+constexpr uint32_t kXSlots = 2;     // cluster exchange slots (units j and j+1)
+constexpr int kPWarps = 11;         // pack warps
+constexpr int kAWarps = 4;          // analysis warps
+constexpr int kAThreads = kAWarps * 32;
+constexpr int kProducerWarp = kPWarps + kAWarps;
+constexpr int kEncThreads = (kProducerWarp + 1) * 32;
+constexpr uint32_t kMaxRun = 8;     // blocks per analysis thread in the offset scan
+constexpr uint32_t kWaitSpins = 1u << 26;   // polls of a non-suspending wait
 
 template <typename T>
 struct Traits;
@@ -63,14 +81,18 @@ struct Traits<float> {
     static constexpr int kWords = 32;
 };
 
+// Dynamic shared memory: kBufs slices, then kBufs x block extremes (later
+// payload offsets, 4 KB either type), then kBufs x rate bytes.
 template <typename T>
 struct Layout {
     static constexpr uint32_t kBlocks = kSliceBytes / (kBlock * Traits<T>::kBytes);
-    static constexpr uint32_t kRounds = kBlocks / kThreads;
-    static constexpr uint32_t kSlice = kGuard;
-    static constexpr uint32_t kExtremes = kGuard + kSliceBytes;   // 4 KB either type
-    static constexpr uint32_t kRates = kExtremes + 4096;
-    static constexpr uint32_t kTotal = kRates + (kBlocks + 15) / 16 * 16;
+    static constexpr uint32_t kMeta = kBufs * kSliceBytes;
+    static constexpr uint32_t kMetaStride = 4096;
+    static constexpr uint32_t kRates = kMeta + kBufs * kMetaStride;
+    static constexpr uint32_t kRatesStride = (kBlocks + 15) / 16 * 16;
+    static constexpr uint32_t kTotal = kRates + kBufs * kRatesStride;
+    static_assert(kBlocks * 4 <= kMetaStride, "offsets per slice");
+    static_assert(kBlocks <= kAThreads * kMaxRun, "offset scan");
 };
 
 struct EncodeArgs {
@@ -81,21 +103,103 @@ struct EncodeArgs {
     uint64_t* sizes;
     float* bounds;
     uint32_t* status;
+    ShiftMul mul;
 };
 
-// ---- slice load ------------------------------------------------------------
+// This CTA's share of a unit of n elements.
+struct Slice {
+    uint32_t n, nb, b0, nbs, e0, e1, hdr;
+};
 
-// Thread 0: plan the slice load [e0, e1) as bulk copies of 16-byte aligned
-// runs.  Returns false when some run cannot be bulk-copied (then every
-// element is copied by the threads).  *tail is the first element of the
-// sub-16-byte tail that the threads copy.
+__device__ __forceinline__ Slice slice_of(uint32_t n, uint32_t rank, uint32_t csize) {
+    Slice s;
+    s.n = n;
+    s.nb = (n + kBlock - 1) / kBlock;
+    const uint32_t sb = (s.nb + csize - 1) / csize;
+    s.b0 = min(rank * sb, s.nb);
+    const uint32_t b1 = min(s.b0 + sb, s.nb);
+    s.nbs = b1 - s.b0;
+    s.e0 = s.b0 * kBlock;
+    s.e1 = min(b1 * kBlock, n);
+    s.hdr = (n + kGroup - 1) / kGroup * (kGroup / kBlock);
+    return s;
+}
+
+// What the analysis warps hand to the pack warps (and, through them, to
+// the producer) for one unit.
+struct SetInfo {
+    uint8_t* stream;      // the unit's compressed stream
+    uint8_t* out;         // this slice's payload in it
+    uint64_t unit_bytes;  // compressed size of the unit
+    float eb, recip;      // bound, 0.5 / eb
+    uint32_t n, b0, nbs;
+    uint32_t pad_from, pad_to;   // header bytes after the last block (last CTA)
+    uint32_t fits;
+};
+
+// One unit as the producer publishes it with the slice load.
+struct Job {
+    uint8_t* stream;
+    uint64_t capacity;
+    float eps;
+    uint32_t u;
+    Slice s;
+};
+
+// Barriers and exchange slots of one CTA.
+struct Sync {
+    uint64_t full[kBufs];      // producer -> analysis: slice landed
+    uint64_t ready[kBufs];     // analysis -> pack: offsets, bound, output address
+    uint64_t packed[kBufs];    // pack warps -> producer: buffer and metadata free
+    uint64_t ext_bar[kXSlots]; // cluster: slice extremes of every CTA stored here
+    uint64_t tot_bar[kXSlots]; // cluster: slice byte totals of every CTA stored here
+    SetInfo info[kBufs];
+    Job job[kBufs];
+    uint32_t tail[kBufs];
+    uint32_t status[kBufs];
+    // Written by every CTA of the cluster into every CTA (asynchronous
+    // distributed shared memory stores counted on the receiver's barrier).
+    float2 ext[kXSlots][kMaxCluster];
+    uint32_t tot[kXSlots][kMaxCluster];
+    float red_lo[kAWarps], red_hi[kAWarps];
+    uint32_t scan[kAWarps];
+    uint32_t broken;
+};
+
+// Barrier of the analysis warps.
+__device__ __forceinline__ void abar() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kAThreads) : "memory");
+}
+
+// Barrier of the analysis warps that also ORs a predicate over them, so
+// that every analysis thread takes the same branch on a flag that other
+// roles may set at any time.
+__device__ __forceinline__ bool abar_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "n"(kAThreads)
+        : "memory");
+    return r != 0;
+}
+
+// ---- slice load (producer lane) ----------------------------------------------
+
+// Plans the load of elements [e0, e1) as bulk copies of 16-byte aligned runs
+// and issues them on `bar`.  *tail (written before the arrive, so it is
+// visible once the phase completes) is the first element the compute warps
+// copy themselves: the sub-16-byte tail, or e0 when some run cannot be
+// bulk-copied.
 template <typename T>
-__device__ bool plan_and_issue_load(const Unit& unit, const Map& m, uint32_t u, uint32_t e0,
-                                    uint32_t e1, uint8_t* slice, uint64_t* bar, uint32_t* tail) {
+__device__ void issue_load(const Unit& unit, const Map& m, uint32_t u, uint32_t e0, uint32_t e1,
+                           uint8_t* slice, uint64_t* bar, volatile uint32_t* tail) {
     constexpr uint32_t B = Traits<T>::kBytes;
     const uint32_t L = run_len(unit, m);
-    uint32_t total = 0, pieces = 0;
-    *tail = e1;
+    uint32_t total = 0, pieces = 0, t = e1;
     bool ok = true;
     for (uint32_t pos = e0; pos < e1;) {
         const uint32_t r = pos / L, off = pos - r * L;
@@ -109,14 +213,15 @@ __device__ bool plan_and_issue_load(const Unit& unit, const Map& m, uint32_t u, 
             break;
         }
         total += body;
-        if (last) *tail = pos + body / B;
+        if (last) t = pos + body / B;
         pos += len;
     }
     if (!ok) {
         *tail = e0;
         mbar_arrive_expect_tx(bar, 0);
-        return false;
+        return;
     }
+    *tail = t;
     mbar_arrive_expect_tx(bar, total);
     for (uint32_t pos = e0; pos < e1;) {
         const uint32_t r = pos / L, off = pos - r * L;
@@ -126,15 +231,14 @@ __device__ bool plan_and_issue_load(const Unit& unit, const Map& m, uint32_t u, 
         if (body) bulk_load(slice + (pos - e0) * B, src, body, bar);
         pos += len;
     }
-    return true;
 }
 
 template <typename T>
 __device__ void copy_elements(const Unit& unit, const Map& m, uint32_t u, uint32_t from,
-                              uint32_t to, uint32_t e0, uint8_t* slice) {
+                              uint32_t to, uint32_t e0, uint8_t* slice, uint32_t t) {
     const uint32_t L = run_len(unit, m);
     T* dst = reinterpret_cast<T*>(slice);
-    for (uint32_t i = from + threadIdx.x; i < to; i += kThreads) {
+    for (uint32_t i = from + t; i < to; i += kAThreads) {
         const uint32_t r = i / L;
         dst[i - e0] = run_base<const T>(unit, m, u, r)[i - r * L];
     }
@@ -185,15 +289,21 @@ __device__ __forceinline__ bool masked(int e, int rho, uint32_t valid) {
     return static_cast<uint32_t>(8 * (((e >> 3) + rho) & 3) + (e & 7)) >= valid;
 }
 
-// (|q| << 1) | sign for |q| < 2^15 and no NaN: truncation by a
-// round-toward-zero add of 2^23 (exact for |t| < 2^23), the rest as
-// batch_quantization (cuszp_batched_fixed.cu:10-25).
-__device__ __forceinline__ uint32_t narrow_row(float x, float recip) {
+// (|q| << 1) | sign for |q| < 2^15 and no NaN, as batch_quantization
+// (cuszp_batched_fixed.cu:10-25) computes it: r = x * recip and
+// t = r + 0.5, each rounded; trunc(|t|) from a round-toward-zero add of 2^23
+// (exact for |t| < 2^23).  The reference's s = (r < -0.5) is the sign bit of
+// t: r + 0.5 is exact for r in [-1, -0.5) (Sterbenz), so t < 0 exactly when
+// r < -0.5, and t is never -0.  Then |q| = trunc(|t|) + s and the row is
+// 2 * trunc(|t|) + 3 * s, written as integer multiply-adds.
+// The integer steps are multiply-adds with multipliers from `mul` (FMA pipe).
+__device__ __forceinline__ uint32_t narrow_row(float x, float recip, const ShiftMul& mul) {
     const float r = __fmul_rn(x, recip);
     const float t = __fadd_rn(r, 0.5f);
     const float z = __fadd_rz(fabsf(t), 8388608.0f);
-    const uint32_t twice = (__float_as_uint(z) << 1) - 0x96000000u;  // 2 * trunc(|t|)
-    return r >= -0.5f ? twice : twice + 3u;  // |q| = trunc(|t|) + s, sign = s
+    const uint32_t twice = __float_as_uint(z) * mul.l1 - 0x96000000u;   // 2 * trunc(|t|)
+    const uint32_t neg = static_cast<uint32_t>(static_cast<int32_t>(__float_as_uint(t)) >> 31);
+    return twice + neg * mul.neg3;   // + 3 when t < 0
 }
 
 // Rows of the 16x32 bit matrix for a narrow block: A[k] holds rows k and
@@ -203,17 +313,18 @@ __device__ __forceinline__ uint32_t narrow_row(float x, float recip) {
 // OR of all rows.
 template <typename T>
 __device__ __forceinline__ uint32_t narrow_block(const uint32_t (&w)[Traits<T>::kWords],
-                                                 float recip, uint32_t (&A)[16]) {
+                                                 float recip, const ShiftMul& mul,
+                                                 uint32_t (&A)[16]) {
     uint32_t orv = 0;
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
         const int e = bitpos(k);
-        const uint32_t lo = narrow_row(elem<T>(w, e), recip);
-        const uint32_t hi = narrow_row(elem<T>(w, e + 16), recip);
+        const uint32_t lo = narrow_row(elem<T>(w, e), recip, mul);
+        const uint32_t hi = narrow_row(elem<T>(w, e + 16), recip, mul);
         orv |= lo | hi;
         A[k] = __byte_perm(lo, hi, 0x5410);
     }
-    transpose16(A);
+    transpose16_mul(A, mul);
     return orv;
 }
 
@@ -332,78 +443,102 @@ __device__ __forceinline__ float elem_at(const uint8_t* blk, int v) {
         return reinterpret_cast<const float*>(blk)[v];
 }
 
-// ---- the kernel --------------------------------------------------------------
+// ---- producer warp (one lane) -------------------------------------------------
+
+// Loads slice j into buffer j % kBufs once unit j - kBufs has been packed out
+// of it, and publishes each unit's status word after its pack.  Returns once
+// the copies it issued have landed.
+template <typename T>
+__device__ void produce(const EncodeArgs& a, uint32_t count, uint32_t first, uint32_t stride,
+                        uint32_t rank, uint32_t csize, uint8_t* smem, Sync& sy) {
+    uint32_t last[kBufs];
+    for (uint32_t b = 0; b < kBufs; ++b) last[b] = ~0u;
+    for (uint32_t j = 0; j < count + kBufs; ++j) {
+        const uint32_t b = j % kBufs;
+        if (j >= kBufs) {
+            const uint32_t jj = j - kBufs;
+            if (!mbar_wait_bounded(&sy.packed[b], (jj / kBufs) & 1u, kWaitPolls)) {
+                sy.broken = 1;
+                break;
+            }
+            // Results live in mapped host memory.  They are written here, by a
+            // lane that never releases at cluster scope, so that no
+            // exchange waits for a PCIe write.  Status is a plain store (no
+            // atomics over PCIe); any CTA that saw an error leaves a nonzero
+            // word.
+            const uint32_t uj = first + jj * stride;
+            if (rank == 0) {
+                a.sizes[uj] = sy.info[b].unit_bytes;
+                a.bounds[uj] = sy.info[b].eb;
+            }
+            if (sy.status[b]) *reinterpret_cast<volatile uint32_t*>(&a.status[uj]) = sy.status[b];
+            sy.status[b] = 0;
+        }
+        if (j < count) {
+            const uint32_t u = first + j * stride;
+            const Unit unit = a.units[u];
+            const Map map = a.maps[unit.map];
+            const Slice s = slice_of(unit.n, rank, csize);
+            Job& job = sy.job[b];
+            job.stream = unit.stream;
+            job.capacity = unit.capacity;
+            job.eps = unit.eb;
+            job.u = u;
+            job.s = s;
+            // published by the arrive on full[b] inside issue_load
+            issue_load<T>(unit, map, u, s.e0, s.e1, smem + b * kSliceBytes, &sy.full[b],
+                          &sy.tail[b]);
+            last[b] = j;
+        }
+    }
+    for (uint32_t b = 0; b < kBufs; ++b)
+        if (last[b] != ~0u) mbar_wait_bounded(&sy.full[b], (last[b] / kBufs) & 1u, kWaitPolls);
+}
+
+// ---- analysis warps -------------------------------------------------------------
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 3) encode_kernel(EncodeArgs a) {
+__device__ void analyse(const EncodeArgs& a, uint32_t count, uint32_t first, uint32_t stride,
+                        cg::cluster_group& cluster, uint8_t* smem, Sync& sy) {
     using L = Layout<T>;
     constexpr uint32_t BB = kBlock * Traits<T>::kBytes;  // input bytes per block
-    constexpr int R = static_cast<int>(L::kRounds);
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* slice = smem + L::kSlice;
-    float2* ext32 = reinterpret_cast<float2*>(smem + L::kExtremes);
-    uint32_t* ext16 = reinterpret_cast<uint32_t*>(smem + L::kExtremes);
-    uint8_t* rates = smem + L::kRates;
-    uint32_t* offs = reinterpret_cast<uint32_t*>(smem + L::kExtremes);  // after phase 4
-
-    __shared__ uint64_t bar;
-    __shared__ uint32_t wsum[R][kWarps];
-    __shared__ float red_lo[kWarps], red_hi[kWarps];
-    // Written by every CTA of the cluster into every CTA (distributed shared
-    // memory stores before a cluster barrier), read locally after it.
-    __shared__ float2 s_extremes[kMaxCluster];
-    __shared__ uint32_t s_totals[kMaxCluster];
-    __shared__ uint32_t s_base, s_unit_total, s_tail, s_status;
-    __shared__ float s_eb, s_recip;
-
-    cg::cluster_group cluster = cg::this_cluster();
     const uint32_t rank = cluster.block_rank();
     const uint32_t csize = cluster.num_blocks();
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int rho = (sizeof(T) == 2) ? ((tid >> 1) & 3) : (tid & 3);
+    const uint32_t t = threadIdx.x - kPWarps * 32;
+    const int lane = t & 31, awarp = t >> 5;
+    const int rho = (sizeof(T) == 2) ? ((t >> 1) & 3) : (t & 3);
+    for (uint32_t j = 0; j < count; ++j) {
+        const uint32_t b = j % kBufs, x = j % kXSlots;
+        const uint32_t xpar = (j / kXSlots) & 1u;
+        uint8_t* slice = smem + b * kSliceBytes;
+        uint8_t* meta = smem + L::kMeta + b * L::kMetaStride;
+        uint8_t* rates = smem + L::kRates + b * L::kRatesStride;
 
-    if (tid == 0) {
-        mbar_init(&bar, 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
-    uint32_t parity = 0;
-
-    for (uint32_t u = blockIdx.y; u < a.num_units; u += gridDim.y) {
-        const Unit unit = a.units[u];
-        const Map map = a.maps[unit.map];
-        const uint32_t n = unit.n;
-        const uint32_t nb = (n + kBlock - 1) / kBlock;
-        const uint32_t sb = (nb + csize - 1) / csize;
-        const uint32_t b0 = min(rank * sb, nb), b1 = min(b0 + sb, nb);
-        const uint32_t nbs = b1 - b0;
-        const uint32_t e0 = b0 * kBlock, e1 = min(b1 * kBlock, n);
-        const uint32_t hdr = (n + kGroup - 1) / kGroup * (kGroup / kBlock);
-        uint32_t status = 0;
-
-        // 1. the slice on chip
-        if (tid == 0) {
-            s_status = 0;
-            uint32_t tail;
-            plan_and_issue_load<T>(unit, map, u, e0, e1, slice, &bar, &tail);
-            s_tail = tail;
+        // -- slice on chip, block extremes, slice extremes to the cluster
+        const bool landed = mbar_wait_bounded(&sy.full[b], (j / kBufs) & 1u, kWaitPolls);
+        const Job job = sy.job[b];
+        const Slice& s = job.s;
+        const uint32_t u = job.u;
+        if (landed) {
+            const uint32_t tail = sy.tail[b];
+            if (tail < s.e1) {   // runs the bulk copies could not take
+                const Unit unit = a.units[u];
+                copy_elements<T>(unit, a.maps[unit.map], u, tail, s.e1, s.e0, slice, t);
+            }
+            // +0 past the end of the unit (the last block may be partial)
+            if (s.nbs && s.b0 + s.nbs == s.nb && t < s.nb * kBlock - s.e1)
+                reinterpret_cast<T*>(slice)[s.e1 - s.e0 + t] = T(0.0f);
+        } else {
+            sy.broken = 1;
         }
-        __syncthreads();
-        copy_elements<T>(unit, map, u, s_tail, e1, e0, slice);
-        if (!mbar_wait_bounded(&bar, parity, kWaitPolls)) status |= kErrTimeout;
-        parity ^= 1u;
-        // +0 past the end of the unit (the last block may be partial)
-        if (b1 == nb && nbs && tid < static_cast<int>(b1 * kBlock - e1))
-            reinterpret_cast<T*>(slice)[e1 - e0 + tid] = T(0.0f);
-        __syncthreads();
-
-        // 2. block extremes
+        if (abar_or(*reinterpret_cast<volatile uint32_t*>(&sy.broken) != 0)) return;
         float tlo = FLT_MAX, thi = -FLT_MAX;
-        for (uint32_t i = tid; i < nbs; i += kThreads) {
+#pragma unroll 2
+        for (uint32_t i = t; i < s.nbs; i += kAThreads) {
             const uint8_t* blk = slice + i * BB;
             float lo, hi;
             bool nan;
-            const uint32_t valid = min(n - (b0 + i) * kBlock, uint32_t(kBlock));
+            const uint32_t valid = min(s.n - (s.b0 + i) * kBlock, uint32_t(kBlock));
             if (valid == kBlock) {
                 uint32_t w[Traits<T>::kWords];
                 load_block<T>(blk, rho, w);
@@ -413,16 +548,17 @@ __global__ void __launch_bounds__(kThreads, 3) encode_kernel(EncodeArgs a) {
                 hi = lo;
                 nan = false;
                 for (uint32_t v = 0; v < valid; ++v) {
-                    const float x = elem_at<T>(blk, v);
-                    lo = fminf(lo, x);
-                    hi = fmaxf(hi, x);
-                    nan |= x != x;
+                    const float xv = elem_at<T>(blk, v);
+                    lo = fminf(lo, xv);
+                    hi = fmaxf(hi, xv);
+                    nan |= xv != xv;
                 }
             }
             if constexpr (sizeof(T) == 2)
-                ext16[i] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+                reinterpret_cast<uint32_t*>(meta)[i] =
+                    (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
             else
-                ext32[i] = make_float2(lo, hi);
+                reinterpret_cast<float2*>(meta)[i] = make_float2(lo, hi);
             rates[i] = nan ? kNanFlag : 0;
             tlo = fminf(tlo, lo);
             thi = fmaxf(thi, hi);
@@ -433,30 +569,30 @@ __global__ void __launch_bounds__(kThreads, 3) encode_kernel(EncodeArgs a) {
             thi = fmaxf(thi, __shfl_xor_sync(0xffffffffu, thi, d));
         }
         if (lane == 0) {
-            red_lo[warp] = tlo;
-            red_hi[warp] = thi;
+            sy.red_lo[awarp] = tlo;
+            sy.red_hi[awarp] = thi;
         }
-        __syncthreads();
-        // 3. unit extremes through distributed shared memory -> bound: lane r
-        // of warp 0 stores this slice's extremes into CTA r
-        if (warp == 0) {
-            float lo = lane < kWarps ? red_lo[lane] : FLT_MAX;
-            float hi = lane < kWarps ? red_hi[lane] : -FLT_MAX;
+        abar();
+        if (awarp == 0) {
+            float lo = lane < kAWarps ? sy.red_lo[lane] : FLT_MAX;
+            float hi = lane < kAWarps ? sy.red_hi[lane] : -FLT_MAX;
 #pragma unroll
             for (int d = 16; d > 0; d >>= 1) {
                 lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, d));
                 hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, d));
             }
+            if (lane == 0) mbar_arrive_expect_tx(&sy.ext_bar[x], csize * sizeof(float2));
             if (static_cast<uint32_t>(lane) < csize)
-                *cluster.map_shared_rank(&s_extremes[rank], static_cast<uint32_t>(lane)) =
-                    make_float2(lo, hi);
-        }
-        cluster.sync();
-        if (warp == 0) {
-            float lo = FLT_MAX, hi = -FLT_MAX;
+                st_async_f32x2(cluster_addr(&sy.ext[x][rank], lane), lo, hi,
+                               cluster_addr(&sy.ext_bar[x], lane));
+            // -- unit extremes -> bound
+            const bool ok =
+                __all_sync(0xffffffffu, mbar_spin_bounded(&sy.ext_bar[x], xpar, kWaitSpins));
+            lo = FLT_MAX;
+            hi = -FLT_MAX;
             if (static_cast<uint32_t>(lane) < csize) {
-                lo = s_extremes[lane].x;
-                hi = s_extremes[lane].y;
+                lo = sy.ext[x][lane].x;
+                hi = sy.ext[x][lane].y;
             }
 #pragma unroll
             for (int d = 16; d > 0; d >>= 1) {
@@ -464,218 +600,315 @@ __global__ void __launch_bounds__(kThreads, 3) encode_kernel(EncodeArgs a) {
                 hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, d));
             }
             if (lane == 0) {
-                const float eb = resolve_bound(unit.eb, lo, hi, a.relative != 0);
-                s_eb = eb;
-                s_recip = __fdiv_rn(0.5f, eb);
+                if (!ok) sy.broken = 1;
+                const float eb = resolve_bound(job.eps, lo, hi, a.relative != 0);
+                sy.info[b].eb = eb;
+                sy.info[b].recip = __fdiv_rn(0.5f, eb);
             }
         }
-        __syncthreads();
-        const float eb = s_eb;
-        const float recip = s_recip;
+        if (abar_or(*reinterpret_cast<volatile uint32_t*>(&sy.broken) != 0)) return;
 
-        // 4. rates, payload offsets (one scan for all rounds), slice size
-        uint32_t off[R];
-        bool any_wide = !(recip <= FLT_MAX);  // 0.5 / eb must be finite for +0 padding
+        // -- rates and payload offsets: each thread a run of kRun blocks
+        const float recip = sy.info[b].recip;
+        const uint32_t run = (s.nbs + kAThreads - 1) / kAThreads;
+        const uint32_t i0 = t * run;
+        uint32_t local = 0;
 #pragma unroll
-        for (int k = 0; k < R; ++k) {
-            const uint32_t i = k * kThreads + tid;
-            uint32_t sz = 0;
-            if (i < nbs) {
+        for (uint32_t k = 0; k < kMaxRun; ++k) {
+            const uint32_t i = i0 + k;
+            if (k < run && i < s.nbs) {
                 float lo, hi;
                 if constexpr (sizeof(T) == 2) {
-                    const uint32_t p = ext16[i];
+                    const uint32_t p = reinterpret_cast<const uint32_t*>(meta)[i];
                     lo = __uint_as_float(p << 16);
                     hi = __uint_as_float(p & 0xffff0000u);
                 } else {
-                    lo = ext32[i].x;
-                    hi = ext32[i].y;
+                    const float2 p = reinterpret_cast<const float2*>(meta)[i];
+                    lo = p.x;
+                    hi = p.y;
                 }
                 const bool nan = rates[i] & kNanFlag;
-                uint32_t m = 0;
-                if (lo == lo) m = max(uabs(quantize(lo, recip)), uabs(quantize(hi, recip)));
-                if (nan) m = max(m, 1u);
-                const uint32_t r = 32 - __clz(m);
+                uint32_t mq = 0;
+                if (lo == lo) mq = max(uabs(quantize(lo, recip)), uabs(quantize(hi, recip)));
+                if (nan) mq = max(mq, 1u);
+                const uint32_t r = 32 - __clz(mq);
                 rates[i] = static_cast<uint8_t>(r | (nan ? kNanFlag : 0));
-                any_wide |= nan || r > 15;
-                sz = r ? 4 + 4 * r : 0u;
+                local += r ? 4 + 4 * r : 0u;
             }
-            uint32_t x = sz;
-#pragma unroll
-            for (int d = 1; d < 32; d <<= 1) {
-                const uint32_t y = __shfl_up_sync(0xffffffffu, x, d);
-                if (lane >= d) x += y;
-            }
-            if (lane == 31) wsum[k][warp] = x;
-            off[k] = x - sz;
         }
-        const bool inplace = !__syncthreads_or(any_wide);
-        // every extremes word has been read: the region now holds offsets
-        uint32_t slice_total = 0;
+        uint32_t inc = local;
 #pragma unroll
-        for (int k = 0; k < R; ++k) {
-            uint32_t pre = 0, tot = 0;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                const uint32_t s = wsum[k][w];
-                pre += w < warp ? s : 0u;
-                tot += s;
-            }
-            const uint32_t i = k * kThreads + tid;
-            if (i < nbs) offs[i] = slice_total + off[k] + pre;
-            slice_total += tot;
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, inc, d);
+            if (lane >= d) inc += y;
         }
-        if (warp == 0 && static_cast<uint32_t>(lane) < csize)
-            *cluster.map_shared_rank(&s_totals[rank], static_cast<uint32_t>(lane)) = slice_total;
-        cluster.sync();
-        if (warp == 0) {
-            const uint32_t t = static_cast<uint32_t>(lane) < csize ? s_totals[lane] : 0u;
-            uint32_t base = static_cast<uint32_t>(lane) < rank ? t : 0u, all = t;
+        if (lane == 31) sy.scan[awarp] = inc;
+        abar();
+        uint32_t pre = 0, slice_total = 0;
+#pragma unroll
+        for (int w = 0; w < kAWarps; ++w) {
+            const uint32_t v = sy.scan[w];
+            pre += w < awarp ? v : 0u;
+            slice_total += v;
+        }
+        // The extremes of these blocks were read by this thread only: the
+        // words now hold payload offsets.
+        uint32_t off = pre + inc - local;
+#pragma unroll
+        for (uint32_t k = 0; k < kMaxRun; ++k) {
+            const uint32_t i = i0 + k;
+            if (k < run && i < s.nbs) {
+                reinterpret_cast<uint32_t*>(meta)[i] = off;
+                const uint32_t r = rates[i] & 0x3f;
+                off += r ? 4 + 4 * r : 0u;
+            }
+        }
+        if (awarp == 0) {
+            if (lane == 0) mbar_arrive_expect_tx(&sy.tot_bar[x], csize * sizeof(uint32_t));
+            if (static_cast<uint32_t>(lane) < csize)
+                st_async_u32(cluster_addr(&sy.tot[x][rank], lane), slice_total,
+                             cluster_addr(&sy.tot_bar[x], lane));
+            // -- slice totals -> this slice's output offset
+            const bool ok =
+                __all_sync(0xffffffffu, mbar_spin_bounded(&sy.tot_bar[x], xpar, kWaitSpins));
+            const uint32_t tv = static_cast<uint32_t>(lane) < csize ? sy.tot[x][lane] : 0u;
+            uint32_t base = static_cast<uint32_t>(lane) < rank ? tv : 0u, all = tv;
 #pragma unroll
             for (int d = 16; d > 0; d >>= 1) {
                 base += __shfl_xor_sync(0xffffffffu, base, d);
                 all += __shfl_xor_sync(0xffffffffu, all, d);
             }
             if (lane == 0) {
-                s_base = base;
-                s_unit_total = all;
+                if (!ok) sy.broken = 1;
+                const uint64_t unit_bytes = static_cast<uint64_t>(s.hdr) + all;
+                const bool fits = unit_bytes <= job.capacity;
+                if (!fits) sy.status[b] |= kErrCapacity;
+                SetInfo& info = sy.info[b];
+                info.stream = job.stream;
+                info.out = job.stream + s.hdr + base;
+                info.unit_bytes = unit_bytes;
+                info.n = s.n;
+                info.b0 = s.b0;
+                info.nbs = s.nbs;
+                info.pad_from = rank == csize - 1 ? s.nb : 0u;
+                info.pad_to = rank == csize - 1 ? s.hdr : 0u;
+                info.fits = fits ? 1u : 0u;
             }
         }
-        __syncthreads();
-        const uint64_t unit_bytes = static_cast<uint64_t>(hdr) + s_unit_total;
-        const bool fits = unit_bytes <= unit.capacity;
-        if (rank == 0 && tid == 0) {
-            a.sizes[u] = unit_bytes;
-            a.bounds[u] = eb;
+        if (abar_or(*reinterpret_cast<volatile uint32_t*>(&sy.broken) != 0)) return;
+        if (t == 0) mbar_arrive(&sy.ready[b]);   // offsets, bound and address published
+    }
+}
+
+// ---- pack warps ----------------------------------------------------------------
+
+template <typename T>
+__device__ void pack(uint32_t count, const ShiftMul& mul, uint8_t* smem, Sync& sy) {
+    using L = Layout<T>;
+    constexpr uint32_t BB = kBlock * Traits<T>::kBytes;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int rho = (sizeof(T) == 2) ? ((lane >> 1) & 3) : (lane & 3);
+    const uint32_t sh = 8u * rho;
+    uint32_t rot = 0;   // chunk c of this unit goes to pack warp (c + rot) % kPWarps
+    for (uint32_t j = 0; j < count; ++j) {
+        const uint32_t b = j % kBufs;
+        const bool ok = mbar_wait_bounded(&sy.ready[b], (j / kBufs) & 1u, kWaitPolls);
+        if (!__all_sync(0xffffffffu, ok)) {
+            sy.broken = 1;
+            return;
         }
-        if (!fits) status |= kErrCapacity;
-
-        if (fits) {
-            uint8_t* stream = unit.stream;
-            for (uint32_t i = tid; i < nbs; i += kThreads) stream[b0 + i] = rates[i] & 0x3f;
-            if (rank == csize - 1)
-                for (uint32_t j = nb + tid; j < hdr; j += kThreads) stream[j] = 0;
-
-            // 5. pack round by round
-            const uint64_t start = static_cast<uint64_t>(hdr) + s_base;
-            const uint32_t shift =
-                static_cast<uint32_t>((reinterpret_cast<uintptr_t>(stream) + start) & 15u);
-            uint8_t* out_smem = smem + shift;   // slice payload byte 0 (in place)
-            const uint32_t sh = 8u * rho;
-            const uint32_t rounds = (nbs + kThreads - 1) / kThreads;
-#pragma unroll 1
-            for (uint32_t k = 0; k < rounds; ++k) {
-                const uint32_t i = k * kThreads + tid;
-                const bool active = i < nbs;
+        const SetInfo info = sy.info[b];
+        uint8_t* slice = smem + b * kSliceBytes;
+        const uint32_t* offs = reinterpret_cast<const uint32_t*>(smem + L::kMeta + b * L::kMetaStride);
+        const uint8_t* rates = smem + L::kRates + b * L::kRatesStride;
+        const uint32_t chunks = (info.nbs + 31) / 32;
+        uint32_t status = 0;
+        if (info.fits) {
+            const float recip = info.recip;
+            // header bytes past the last block (zero) by the warp of chunk 0
+            if (static_cast<uint32_t>(warp) == rot)
+                for (uint32_t k = info.pad_from + lane; k < info.pad_to; k += 32) info.stream[k] = 0;
+            for (uint32_t c = (warp + kPWarps - rot) % kPWarps; c < chunks; c += kPWarps) {
+                const uint32_t i = c * 32 + lane;
+                const bool active = i < info.nbs;
                 const uint32_t rb = active ? rates[i] : 0u;
                 const uint32_t r = rb & 0x3f;
-                const uint32_t valid =
-                    active ? min(n - (b0 + i) * kBlock, uint32_t(kBlock)) : uint32_t(kBlock);
+                if (active) info.stream[info.b0 + i] = static_cast<uint8_t>(r);
                 const uint32_t pos = active ? offs[i] : 0u;
+                uint8_t* chunk = slice + c * 32 * BB;
                 uint32_t w[Traits<T>::kWords];
-                if (active) load_block<T>(slice + i * BB, rho, w);
-                if (inplace) {
+                if (active) load_block<T>(chunk + lane * BB, rho, w);
+                const bool narrow_ok = !(rb & kNanFlag) && r <= 15;
+                // +0 padding quantises to 0 only for a finite 0.5 / eb
+                const bool wide = __any_sync(0xffffffffu, active && !narrow_ok) || !(recip <= FLT_MAX);
+                if (!wide) {
                     uint32_t A[16];
                     if (active) {
-                        const uint32_t orv = narrow_block<T>(w, recip, A);
+                        const uint32_t orv = narrow_block<T>(w, recip, mul, A);
                         if (32u - __clz(orv >> 1) != r) status |= kErrRateCheck;
                     }
-                    __syncthreads();  // every input of this round is in registers
+                    // Every input of the chunk is in registers: its payload is
+                    // compacted over the chunk's own input, then copied out.
+                    __syncwarp();
+                    const uint32_t p0 = __shfl_sync(0xffffffffu, pos, 0);
                     if (active && r) {
-                        uint32_t* out = reinterpret_cast<uint32_t*>(out_smem + pos);
+                        uint32_t* out = reinterpret_cast<uint32_t*>(chunk + (pos - p0));
 #pragma unroll
-                        for (int t = 0; t < 16; ++t)
-                            if (t <= static_cast<int>(r)) out[t] = __funnelshift_l(A[t], A[t], sh);
+                        for (int k = 0; k < 16; ++k)
+                            if (k <= static_cast<int>(r)) out[k] = __funnelshift_l(A[k], A[k], sh);
                     }
-                } else {
-                    const bool narrow_ok = !(rb & kNanFlag) && r <= 15;
-                    const bool wide = __any_sync(0xffffffffu, active && !narrow_ok);
-                    if (active) {
-                        uint32_t* out = reinterpret_cast<uint32_t*>(stream + start + pos);
-                        uint32_t orv;
-                        if (!wide) {
-                            uint32_t A[16];
-                            orv = narrow_block<T>(w, recip, A) >> 1;
-#pragma unroll
-                            for (int t = 0; t < 16; ++t)
-                                if (r && t <= static_cast<int>(r))
-                                    out[t] = __funnelshift_l(A[t], A[t], sh);
-                        } else {
-                            orv = wide_block<T>(w, rho, recip, valid, r, out);
-                        }
-                        if (32u - __clz(orv) != r) status |= kErrRateCheck;
-                    }
+                    const uint32_t end = __reduce_max_sync(0xffffffffu, active && r ? pos + 4 + 4 * r : 0u);
+                    __syncwarp();
+                    const uint32_t words = end > p0 ? (end - p0) >> 2 : 0u;
+                    const uint32_t* src = reinterpret_cast<const uint32_t*>(chunk);
+                    uint32_t* dst = reinterpret_cast<uint32_t*>(info.out + p0);
+                    for (uint32_t k = lane; k < words; k += 32) dst[k] = src[k];
+                } else if (active) {
+                    const uint32_t valid = min(info.n - (info.b0 + i) * kBlock, uint32_t(kBlock));
+                    uint32_t* out = reinterpret_cast<uint32_t*>(info.out + pos);
+                    const uint32_t orv = wide_block<T>(w, rho, recip, valid, r, out);
+                    if (32u - __clz(orv) != r) status |= kErrRateCheck;
                 }
-            }
-            if (inplace) {
-                fence_proxy_async_smem();
-                __syncthreads();
-                const uint64_t g_end = start + slice_total;
-                const uint64_t a0 = (reinterpret_cast<uintptr_t>(stream) + start + 15u) & ~uint64_t(15);
-                const uint64_t a1 = (reinterpret_cast<uintptr_t>(stream) + g_end) & ~uint64_t(15);
-                const uint64_t s0 = reinterpret_cast<uintptr_t>(stream) + start;
-                const uint64_t s1 = reinterpret_cast<uintptr_t>(stream) + g_end;
-                const bool body = a1 > a0;
-                const uint64_t head_end = body ? a0 : s1;
-                if (body && tid == 0) {
-                    bulk_store(reinterpret_cast<void*>(a0), out_smem + (a0 - s0),
-                               static_cast<uint32_t>(a1 - a0));
-                    bulk_commit();
-                }
-                const uint32_t head_words = static_cast<uint32_t>(head_end - s0) >> 2;
-                const uint32_t tail_words = body ? static_cast<uint32_t>(s1 - a1) >> 2 : 0u;
-                if (static_cast<uint32_t>(tid) < head_words) {
-                    reinterpret_cast<uint32_t*>(s0)[tid] =
-                        reinterpret_cast<const uint32_t*>(out_smem)[tid];
-                } else if (tid >= 32 && static_cast<uint32_t>(tid - 32) < tail_words) {
-                    const uint32_t t = tid - 32;
-                    reinterpret_cast<uint32_t*>(a1)[t] =
-                        reinterpret_cast<const uint32_t*>(out_smem + (a1 - s0))[t];
-                }
-                if (tid == 0) bulk_wait<0>();
             }
         }
-        if (status) atomicOr(&s_status, status);
-        __syncthreads();
-        // Status lives in mapped host memory: a plain store (no atomics over
-        // PCIe); any CTA that saw an error leaves a nonzero word.
-        if (tid == 0 && s_status) *reinterpret_cast<volatile uint32_t*>(&a.status[u]) = s_status;
-        // No CTA reads another's shared memory after the second cluster
-        // barrier, and the next unit's stores into s_extremes / s_totals come
-        // after barriers this CTA only reaches once it has read them.
+        rot = (rot + chunks) % kPWarps;
+        status = __reduce_or_sync(0xffffffffu, status);
+        // Every lane's reads of this buffer are done before lane 0 releases it.
+        __syncwarp();
+        if (lane == 0) {
+            if (status) atomicOr(&sy.status[b], status);
+            mbar_arrive(&sy.packed[b]);
+        }
     }
+}
+
+// ---- the kernel --------------------------------------------------------------
+
+template <typename T>
+__global__ void __launch_bounds__(kEncThreads, 1) encode_kernel(EncodeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ Sync sy;
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t rank = cluster.block_rank();
+    const uint32_t csize = cluster.num_blocks();
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const uint32_t first = blockIdx.y, stride = gridDim.y;
+    const uint32_t count =
+        first < a.num_units ? (a.num_units - first + stride - 1) / stride : 0u;
+
+    if (tid == 0) {
+        for (uint32_t b = 0; b < kBufs; ++b) {
+            mbar_init(&sy.full[b], 1);
+            mbar_init(&sy.ready[b], 1);
+            mbar_init(&sy.packed[b], kPWarps);
+            sy.status[b] = 0;
+        }
+        for (uint32_t x = 0; x < kXSlots; ++x) {
+            mbar_init(&sy.ext_bar[x], 1);   // armed locally, completed by peers' bytes
+            mbar_init(&sy.tot_bar[x], 1);
+        }
+        sy.broken = 0;
+        fence_mbar_init();
+    }
+    cluster_barrier();   // every barrier of the cluster initialised before any arrive
+
+    if (warp == kProducerWarp) {
+        if ((tid & 31) == 0) produce<T>(a, count, first, stride, rank, csize, smem, sy);
+    } else if (warp >= kPWarps) {
+        analyse<T>(a, count, first, stride, cluster, smem, sy);
+    } else {
+        pack<T>(count, a.mul, smem, sy);
+    }
+    // No peer touches this CTA's shared memory once every CTA is here.
+    cluster_barrier();
+    if (tid == 0 && sy.broken)
+        for (uint32_t j = 0; j < count; ++j)
+            *reinterpret_cast<volatile uint32_t*>(&a.status[first + j * stride]) = kErrTimeout;
+}
+
+// Cluster size for units of at least c_min slices: the size in
+// [c_min, kMaxCluster] whose co-resident clusters cover the most SMs (one
+// CTA per SM), and how many clusters that is.  Cached per device.
+struct ClusterShape {
+    uint32_t c;
+    uint32_t clusters;
+};
+
+template <typename T>
+cudaError_t cluster_shape(uint32_t c_min, ClusterShape* out) {
+    static std::mutex mu;
+    static std::map<uint64_t, ClusterShape> cache;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    const uint64_t key = (static_cast<uint64_t>(dev) << 8) | c_min;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return cudaSuccess;
+    }
+    auto kernel = encode_kernel<T>;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Layout<T>::kTotal);
+    if (err != cudaSuccess) return err;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (err != cudaSuccess) return err;
+    ClusterShape best{0, 0};
+    for (uint32_t c = c_min; c <= kMaxCluster; ++c) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(c, 1, 1);
+        cfg.blockDim = dim3(kEncThreads, 1, 1);
+        cfg.dynamicSmemBytes = Layout<T>::kTotal;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = c;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        if (clusters > 0 && static_cast<uint64_t>(clusters) * c > static_cast<uint64_t>(best.clusters) * best.c)
+            best = ClusterShape{c, static_cast<uint32_t>(clusters)};
+    }
+    if (best.c == 0) return cudaErrorInvalidConfiguration;
+    cache[key] = best;
+    *out = best;
+    return cudaSuccess;
 }
 
 template <typename T>
 cudaError_t launch_encode_t(const EncodeLaunch& l, cudaStream_t stream) {
     using L = Layout<T>;
     const uint32_t nb_max = (l.max_n + kBlock - 1) / kBlock;
-    uint32_t c = (nb_max + L::kBlocks - 1) / L::kBlocks;
-    if (c == 0) c = 1;
-    if (c > kMaxCluster || l.num_units == 0) return cudaErrorInvalidValue;
-    auto kernel = encode_kernel<T>;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           L::kTotal);
+    uint32_t c_min = (nb_max + L::kBlocks - 1) / L::kBlocks;
+    if (c_min == 0) c_min = 1;
+    if (c_min > kMaxCluster || l.num_units == 0) return cudaErrorInvalidValue;
+    ClusterShape shape;
+    cudaError_t err = cluster_shape<T>(c_min, &shape);
     if (err != cudaSuccess) return err;
-    if (c > 8) {
-        err = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (err != cudaSuccess) return err;
-    }
     EncodeArgs args{l.units, l.maps, l.num_units, l.relative ? 1u : 0u,
-                    l.sizes, l.bounds, l.status};
+                    l.sizes, l.bounds, l.status, shift_mul()};
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(c, l.num_units < 65535u ? l.num_units : 65535u, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    const uint32_t clusters = min(min(l.num_units, shape.clusters), 65535u);
+    cfg.gridDim = dim3(shape.c, clusters, 1);
+    cfg.blockDim = dim3(kEncThreads, 1, 1);
     cfg.dynamicSmemBytes = L::kTotal;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = c;
+    attr[0].val.clusterDim.x = shape.c;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     note_launch();
-    return cudaLaunchKernelEx(&cfg, kernel, args);
+    return cudaLaunchKernelEx(&cfg, encode_kernel<T>, args);
 }
 
 }  // namespace
