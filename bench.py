@@ -585,6 +585,98 @@ def timed_steps(fn, steps: int, flush: torch.Tensor, device, after=None):
     return times, results
 
 
+def pipeline_codecs(codec, steps: int, flush: torch.Tensor, device) -> dict:
+    """The reference's INT8 and raw encodings (vllm_v1_compressed_offload.py:
+    711-724 / :2090-2116 and :1578-1615) through the same store / restore
+    pipeline, timed like the fixed-mode e2e: step k stores the pages into one
+    page-locked slab while step k-1's slab is restored, both on the device
+    clock.  Restores are checked against the reference's torch expression
+    (INT8) or the pages themselves (raw)."""
+    lib, ck = codec.lib, codec.ckv
+    count, n = codec.count, codec.n
+    page_bytes = n * 2
+    raw_bytes = count * page_bytes
+    x = codec.pages.float()
+    scale = x.abs().amax(dim=1, keepdim=True) / 127.0
+    scale = torch.where(scale == 0, torch.ones_like(scale), scale)
+    q = torch.clamp(torch.round(x / scale), -127, 127).to(torch.int8)   # -0 becomes 0 here
+    want_int8 = (q.to(torch.float32) * scale).to(torch.bfloat16)
+    del q
+    del x
+    out = {}
+    for name in ("int8", "raw"):
+        cap = int(lib.ckv_pipe_host_capacity_int8(count, n) if name == "int8"
+                  else lib.ckv_pipe_host_capacity_raw(count, page_bytes))
+        slabs = [torch.empty(cap, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        meta = [{"o": (C.c_size_t * count)(), "s": (C.c_size_t * count)(), "t": C.c_size_t(0)}
+                for _ in range(2)]
+        dst = torch.empty_like(codec.pages)
+        dptr = ck.ptr_array([dst[i].data_ptr() for i in range(count)])
+        side = torch.cuda.Stream(device)
+        state = {"k": 0, "ts": 0, "tr": 0}
+
+        def step():
+            k = state["k"]
+            state["k"] += 1
+            main = torch.cuda.current_stream(device)
+            a, b = meta[k % 2], meta[(k + 1) % 2]
+            prev_restore = state["tr"]
+            restored = 0
+            if k > 0:
+                side.wait_stream(main)
+                tr = C.c_uint64(0)
+                slab = slabs[(k + 1) % 2].data_ptr()
+                if name == "int8":
+                    st = lib.ckv_pipe_restore_int8(codec.pipe, slab, b["o"], count, n, dptr,
+                                                   state["ts"], C.byref(tr), side.cuda_stream)
+                else:
+                    st = lib.ckv_pipe_restore_raw(codec.pipe, slab, b["o"], count, page_bytes, dptr,
+                                                  state["ts"], C.byref(tr), side.cuda_stream)
+                codec._check(st, f"{name} pipe restore")
+                state["tr"] = tr.value
+                restored = b["t"].value
+            ts = C.c_uint64(0)
+            slab = slabs[k % 2].data_ptr()
+            if name == "int8":
+                st = lib.ckv_pipe_store_int8(codec.pipe, codec.in_ptrs, count, n, slab, cap, a["o"],
+                                             a["s"], C.byref(a["t"]), prev_restore, C.byref(ts),
+                                             main.cuda_stream)
+            else:
+                st = lib.ckv_pipe_store_raw(codec.pipe, codec.in_ptrs, count, page_bytes, slab, cap,
+                                            a["o"], C.byref(a["t"]), prev_restore, C.byref(ts),
+                                            main.cuda_stream)
+            codec._check(st, f"{name} pipe store")
+            state["ts"] = ts.value
+            codec._check(lib.ckv_pipe_join(codec.pipe, state["ts"], main.cuda_stream), "pipe join")
+            main.wait_stream(side)
+            return a["t"].value, restored
+
+        for _ in range(3):
+            step()
+        times, totals = timed_steps(step, steps, flush, device)
+        torch.cuda.synchronize(device)
+        ok = bool(torch.equal(dst.view(torch.int16),
+                              (want_int8 if name == "int8" else codec.pages).view(torch.int16)))
+        stored = totals[-1][0]
+        ms = [C.c_float(0.0) for _ in range(2)]
+        kinds = (3, 4) if name == "int8" else (5, 5)
+        for m, kind in zip(ms, kinds):
+            codec._check(lib.ckv_kernel_time(codec.ctx, kind, C.byref(m)), "kernel time")
+        t = sum(times) / 1e3
+        out[name] = {
+            "e2e_gbps": round(job_rate(1, raw_bytes, steps, t), 3),
+            "ms_per_step": round(t * 1e3 / steps, 4),
+            "compression_ratio": round(raw_bytes / stored, 4),
+            "d2h_bytes_per_step": int(stored), "h2d_bytes_per_step": int(totals[-1][1]),
+            "restore_ok": ok,
+            "store_kernel_ms": round(ms[0].value, 4),
+            "restore_kernel_ms": round(ms[1].value, 4) if name == "int8" else None,
+            "path": f"ckv_pipe_store_{name} overlapped with ckv_pipe_restore_{name} of the "
+                    "previous step's slab, one chunk per job",
+        }
+    return out
+
+
 def raw_pcie(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -> float:
     """Raw pinned D2H + H2D of the uncompressed pages (the PCIe reference point)."""
     pinned = torch.empty(pages_dev.numel() * 2, dtype=torch.uint8, pin_memory=True)
@@ -748,6 +840,8 @@ def main() -> int:
         pack_ms.append(codec.kernel_ms(2))
     compressed = codec.compressed_bytes()
     ok = ok and codec.verify()
+    piped = (pipeline_codecs(codec, min(args.steps, 10), flush, device)
+             if impl == "ours" and pipelined and rank == 0 else None)
 
     e2e_match = codec.e2e_matches() if pipelined else None
     t_step, t_e2e, t_serial = slowest_rank(
@@ -830,6 +924,7 @@ def main() -> int:
             "algorithmic_bytes_per_launch": int(dom_b),
         }
         line["kernels"] = kernels
+        line["pipeline_codecs"] = piped
         line["gpu_launches"] = launches_total
         line["gpu_launches_value_region"] = launches_value
     else:

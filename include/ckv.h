@@ -189,8 +189,9 @@ CKV_API ckv_status ckv_pack(ckv_ctx* ctx, const uint8_t* const* srcs, const size
 
 /* Record CUDA events immediately around every kernel this context launches
  * (on the launch stream).  ckv_kernel_time returns the device duration of
- * the last launch of the given kind (0 encode, 1 decode, 2 pack), in
- * milliseconds, waiting for it to finish. */
+ * the last launch of the given kind (0 encode, 1 decode, 2 pack, 3 INT8
+ * encode, 4 INT8 decode, 5 raw page copy), in milliseconds, waiting for it to
+ * finish. */
 CKV_API ckv_status ckv_set_kernel_timing(ckv_ctx* ctx, int enable);
 CKV_API ckv_status ckv_kernel_time(ckv_ctx* ctx, int kind, float* ms);
 
@@ -244,6 +245,43 @@ CKV_API int ckv_pipe_done(ckv_pipe* pipe, uint64_t ticket);
 
 /* Host bytes that always hold `count` compressed pages of n elements. */
 CKV_API size_t ckv_pipe_host_capacity(size_t count, size_t n);
+
+/* The reference's comparison codecs through the same pipeline (its INT8
+ * encoding, vllm_v1_compressed_offload.py:711-724 store and :2090-2116
+ * restore, and its raw encoding, :1578-1615), so that they are timed on the
+ * same streams, staging and copies as the fixed-mode codec.
+ *
+ * INT8: per page scale = max|x| / 127 (FP32; 1 for an all-zero page),
+ * q = clamp(round_half_even(x / scale), -127, 127); restore writes
+ * bf16_rn((float)q * scale).  A stored page is its n int8 values followed by
+ * the FP32 scale at byte align4(n): sizes[i] = align4(n) + 4 (the
+ * reference's numel + 4).  Offsets are 16-byte aligned.  Neither call
+ * synchronises the host: every stored size is known in advance.  The host
+ * buffer needs ckv_pipe_host_capacity_int8(count, n) bytes.
+ *
+ * Raw: the pages' bytes, page_bytes each, at 16-byte aligned offsets; the
+ * host buffer needs ckv_pipe_host_capacity_raw(count, page_bytes) bytes.
+ *
+ * Ordering (after / ticket / stream) is as for ckv_pipe_store_bf16 and
+ * ckv_pipe_restore_bf16. */
+CKV_API ckv_status ckv_pipe_store_int8(ckv_pipe* pipe, const void* const* pages, size_t count,
+                                       size_t n, uint8_t* host, size_t capacity, size_t* offsets,
+                                       size_t* sizes, size_t* total, uint64_t after,
+                                       uint64_t* ticket, void* stream);
+CKV_API ckv_status ckv_pipe_restore_int8(ckv_pipe* pipe, const uint8_t* host,
+                                         const size_t* offsets, size_t count, size_t n,
+                                         void* const* pages, uint64_t after, uint64_t* ticket,
+                                         void* stream);
+CKV_API ckv_status ckv_pipe_store_raw(ckv_pipe* pipe, const void* const* pages, size_t count,
+                                      size_t page_bytes, uint8_t* host, size_t capacity,
+                                      size_t* offsets, size_t* total, uint64_t after,
+                                      uint64_t* ticket, void* stream);
+CKV_API ckv_status ckv_pipe_restore_raw(ckv_pipe* pipe, const uint8_t* host,
+                                        const size_t* offsets, size_t count, size_t page_bytes,
+                                        void* const* pages, uint64_t after, uint64_t* ticket,
+                                        void* stream);
+CKV_API size_t ckv_pipe_host_capacity_int8(size_t count, size_t n);
+CKV_API size_t ckv_pipe_host_capacity_raw(size_t count, size_t page_bytes);
 
 /* ckv_compress_batch_fixed_bf16 for callers that cannot allocate memory.
  * No counterpart in the reference.  Some callers cannot call cudaMalloc when

@@ -45,6 +45,8 @@ EXPORTS = (
     "ckv_set_kernel_timing", "ckv_kernel_time", "ckv_compress_batch_fixed_bf16_noalloc",
     "ckv_pipe_create", "ckv_pipe_destroy", "ckv_pipe_store_bf16", "ckv_pipe_restore_bf16",
     "ckv_pipe_join", "ckv_pipe_wait", "ckv_pipe_done", "ckv_pipe_host_capacity",
+    "ckv_pipe_store_int8", "ckv_pipe_restore_int8", "ckv_pipe_store_raw", "ckv_pipe_restore_raw",
+    "ckv_pipe_host_capacity_int8", "ckv_pipe_host_capacity_raw",
 )
 
 
@@ -109,6 +111,14 @@ def _declare(lib: C.CDLL) -> None:
         "ckv_pipe_wait": (c_status, [P, C.c_uint64]),
         "ckv_pipe_done": (c_int, [P, C.c_uint64]),
         "ckv_pipe_host_capacity": (c_size, [c_size, c_size]),
+        "ckv_pipe_store_int8": (c_status, [P, P, c_size, c_size, P, c_size, P, P, P, C.c_uint64,
+                                           P, P]),
+        "ckv_pipe_restore_int8": (c_status, [P, P, P, c_size, c_size, P, C.c_uint64, P, P]),
+        "ckv_pipe_store_raw": (c_status, [P, P, c_size, c_size, P, c_size, P, P, C.c_uint64, P,
+                                          P]),
+        "ckv_pipe_restore_raw": (c_status, [P, P, P, c_size, c_size, P, C.c_uint64, P, P]),
+        "ckv_pipe_host_capacity_int8": (c_size, [c_size, c_size]),
+        "ckv_pipe_host_capacity_raw": (c_size, [c_size, c_size]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

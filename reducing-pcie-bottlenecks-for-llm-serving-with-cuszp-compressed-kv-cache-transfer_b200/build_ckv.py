@@ -16,7 +16,8 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 CSRC = HERE / "csrc"
 LIB = HERE / "lib" / "libckv.so"
-SOURCES = ["ckv_api.cu", "ckv_encode.cu", "ckv_decode.cu", "ckv_pack.cu", "ckv_noalloc.cu"]
+SOURCES = ["ckv_api.cu", "ckv_encode.cu", "ckv_decode.cu", "ckv_pack.cu", "ckv_noalloc.cu",
+           "ckv_int8.cu"]
 HEADERS = ["ckv_device.cuh", "ckv_launch.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -70,11 +70,13 @@ struct ckv_ctx {
     // decode status words (device), accumulated until read
     uint32_t* dec_status = nullptr;
     size_t dec_status_cap = 0;
-    // optional kernel timing (encode, decode, pack)
+    // optional kernel timing (encode, decode, pack, INT8 encode, INT8 decode,
+    // raw page copy)
+    static constexpr int kTimedKinds = 6;
     bool timing = false;
-    cudaEvent_t t_start[3] = {nullptr, nullptr, nullptr};
-    cudaEvent_t t_stop[3] = {nullptr, nullptr, nullptr};
-    bool t_valid[3] = {false, false, false};
+    cudaEvent_t t_start[kTimedKinds] = {};
+    cudaEvent_t t_stop[kTimedKinds] = {};
+    bool t_valid[kTimedKinds] = {};
 };
 
 namespace {
@@ -806,7 +808,7 @@ ckv_status ckv_set_kernel_timing(ckv_ctx* ctx, int enable) {
 }
 
 ckv_status ckv_kernel_time(ckv_ctx* ctx, int kind, float* ms) {
-    if (!ctx || !ms || kind < 0 || kind > 2) return CKV_ERR_ARGUMENT;
+    if (!ctx || !ms || kind < 0 || kind >= ckv_ctx::kTimedKinds) return CKV_ERR_ARGUMENT;
     if (!ctx->t_valid[kind]) return fail(ctx, CKV_ERR_ARGUMENT, "no timed launch of kind %d", kind);
     DeviceGuard guard(ctx->device);
     cudaError_t e = cudaEventSynchronize(ctx->t_stop[kind]);
@@ -858,8 +860,10 @@ size_t worst_page(size_t n) {
     return align16(hdr + nb * (4 + 4 * 32));
 }
 
-ckv_status pipe_staging(ckv_pipe* p, size_t n) {
-    const size_t need = worst_page(n);
+// Staging for chunks of pages of at most `need` bytes each (compressed or
+// stored form).
+ckv_status pipe_staging(ckv_pipe* p, size_t need) {
+    need = align16(need);
     if (need <= p->page_cap) return CKV_OK;
     for (int k = 0; k < 2; ++k) {
         cudaFree(p->enc[k]);
@@ -974,7 +978,7 @@ ckv_status ckv_pipe_store_bf16(ckv_pipe* p, const void* const* pages, const floa
     *total = 0;
     if (count == 0) return pipe_issue(p, static_cast<cudaStream_t>(stream_ptr), ticket);
     DeviceGuard guard(ctx->device);
-    if (ckv_status st = pipe_staging(p, n)) return st;
+    if (ckv_status st = pipe_staging(p, worst_page(n))) return st;
     cudaStream_t caller = static_cast<cudaStream_t>(stream_ptr);
     cudaError_t e = cudaEventRecord(p->ev_in, caller);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_enc, p->ev_in, 0);
@@ -1100,6 +1104,277 @@ ckv_status ckv_pipe_restore_bf16(ckv_pipe* p, const uint8_t* host, const size_t*
     if (e != cudaSuccess) return cuda_fail(ctx, "joining the pipeline restore", e);
     if (ticket) *ticket = t;
     return CKV_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Store whose per-chunk device step needs no host synchronisation (every
+// page has the same stored size `stride`, a multiple of 16): stage(k, c0,
+// cnt, dst) enqueues on p->s_enc the writing of pages c0..c0+cnt-1 into dst,
+// one every `stride` bytes.  Chunks are copied out as they are staged.
+template <typename Stage>
+ckv_status pipe_store_fixed(ckv_pipe* p, size_t count, size_t stride, uint8_t* host,
+                            size_t capacity, size_t* offsets, size_t* total, uint64_t after,
+                            uint64_t* ticket, cudaStream_t caller, Stage stage) {
+    ckv_ctx* ctx = p->ctx;
+    *total = 0;
+    if (count == 0) return pipe_issue(p, caller, ticket);
+    if (count * stride > capacity)
+        return fail(ctx, CKV_ERR_CAPACITY, "host buffer of %zu bytes too small (%zu needed)", capacity,
+                    count * stride);
+    if (ckv_status st = pipe_staging(p, stride)) return st;
+    cudaError_t e = cudaEventRecord(p->ev_in, caller);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_enc, p->ev_in, 0);
+    if (e != cudaSuccess) return cuda_fail(ctx, "ordering the pipeline store", e);
+    if (ckv_status st = pipe_after(p, after, p->s_d2h)) return st;
+    size_t pos = 0;
+    for (size_t c0 = 0, c = 0; c0 < count; c0 += p->chunk, ++c) {
+        const int k = static_cast<int>(c & 1);
+        const size_t cnt = std::min(p->chunk, count - c0);
+        if (p->copied_used[k] && (e = cudaStreamWaitEvent(p->s_enc, p->ev_copied[k], 0)))
+            return cuda_fail(ctx, "ordering the pipeline store", e);
+        if (ckv_status st = stage(k, c0, cnt, p->packed[k])) return st;
+        e = cudaEventRecord(p->ev_packed[k], p->s_enc);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_d2h, p->ev_packed[k], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(host + pos, p->packed[k], cnt * stride, cudaMemcpyDeviceToHost,
+                                p->s_d2h);
+        if (e == cudaSuccess) e = cudaEventRecord(p->ev_copied[k], p->s_d2h);
+        if (e != cudaSuccess) return cuda_fail(ctx, "pipeline store copy", e);
+        p->copied_used[k] = true;
+        for (size_t i = 0; i < cnt; ++i) offsets[c0 + i] = pos + i * stride;
+        pos += cnt * stride;
+    }
+    *total = pos;
+    return pipe_issue(p, p->s_d2h, ticket);
+}
+
+// Restore of pages stored `bytes` each at offsets[] of the host buffer:
+// each chunk's span is copied into a landing buffer, then unstage(k, c0, cnt,
+// land, lo) enqueues on p->s_dec the writing of its pages (page i's bytes sit
+// at land + offsets[i] - lo).
+template <typename Unstage>
+ckv_status pipe_restore_fixed(ckv_pipe* p, const uint8_t* host, const size_t* offsets,
+                              size_t count, size_t bytes, void* const* dst, uint64_t after,
+                              uint64_t* ticket, cudaStream_t caller, Unstage unstage) {
+    ckv_ctx* ctx = p->ctx;
+    if (count == 0) return pipe_issue(p, caller, ticket);
+    size_t span_max = 0;
+    for (size_t c0 = 0; c0 < count; c0 += p->chunk) {
+        const size_t cnt = std::min(p->chunk, count - c0);
+        size_t lo = SIZE_MAX, hi = 0;
+        for (size_t i = c0; i < c0 + cnt; ++i) {
+            if ((offsets[i] & 3u) || !dst[i] || (reinterpret_cast<uintptr_t>(dst[i]) & 1u))
+                return fail(ctx, CKV_ERR_ARGUMENT, "invalid restored page %zu", i);
+            lo = std::min(lo, offsets[i]);
+            hi = std::max(hi, offsets[i] + bytes);
+        }
+        span_max = std::max(span_max, hi - (lo & ~size_t(15)));
+    }
+    if (ckv_status st = pipe_landing(p, span_max)) return st;
+    cudaError_t e = cudaEventRecord(p->ev_in, caller);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_dec, p->ev_in, 0);
+    if (e != cudaSuccess) return cuda_fail(ctx, "ordering the pipeline restore", e);
+    if (ckv_status st = pipe_after(p, after, p->s_h2d)) return st;
+    for (size_t c0 = 0, c = 0; c0 < count; c0 += p->chunk, ++c) {
+        const int k = static_cast<int>(c & 1);
+        const size_t cnt = std::min(p->chunk, count - c0);
+        size_t lo = SIZE_MAX, hi = 0;
+        for (size_t i = c0; i < c0 + cnt; ++i) {
+            lo = std::min(lo, offsets[i]);
+            hi = std::max(hi, offsets[i] + bytes);
+        }
+        lo &= ~size_t(15);
+        if (p->decoded_used[k] && (e = cudaStreamWaitEvent(p->s_h2d, p->ev_decoded[k], 0)))
+            return cuda_fail(ctx, "ordering the pipeline restore", e);
+        e = cudaMemcpyAsync(p->land[k], host + lo, hi - lo, cudaMemcpyHostToDevice, p->s_h2d);
+        if (e == cudaSuccess) e = cudaEventRecord(p->ev_landed[k], p->s_h2d);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_dec, p->ev_landed[k], 0);
+        if (e != cudaSuccess) return cuda_fail(ctx, "pipeline restore copy", e);
+        if (ckv_status st = unstage(k, c0, cnt, p->land[k], lo)) return st;
+        if ((e = cudaEventRecord(p->ev_decoded[k], p->s_dec)))
+            return cuda_fail(ctx, "pipeline restore", e);
+        p->decoded_used[k] = true;
+    }
+    uint64_t t = 0;
+    if (ckv_status st = pipe_issue(p, p->s_dec, &t)) return st;
+    e = cudaStreamWaitEvent(caller, pipe_ticket_event(p, t), 0);
+    if (e != cudaSuccess) return cuda_fail(ctx, "joining the pipeline restore", e);
+    if (ticket) *ticket = t;
+    return CKV_OK;
+}
+
+// Descriptors of one launch in the next staging slot, copied to the device
+// on `stream` by the fetch kernel; `extra` zeroed bytes follow them.
+template <typename D>
+ckv_status stage_descriptors(ckv_ctx* ctx, size_t count, size_t extra, cudaStream_t stream,
+                             Slot** slot, D** host, D** dev, uint8_t** extra_dev) {
+    const size_t body = align16(count * sizeof(D));
+    const size_t need = body + align16(extra);
+    if (ckv_status st = acquire_slot(ctx, need, slot)) return st;
+    *host = reinterpret_cast<D*>((*slot)->host);
+    *dev = reinterpret_cast<D*>((*slot)->dev);
+    if (extra_dev) *extra_dev = (*slot)->dev + body;
+    memset((*slot)->host + body, 0, align16(extra));
+    (void)stream;
+    return CKV_OK;
+}
+
+ckv_status fetch_descriptors(ckv_ctx* ctx, Slot* slot, size_t bytes, cudaStream_t stream) {
+    cudaError_t e = ckv::launch_fetch(slot->host_dev, slot->dev, align16(bytes), stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, "uploading descriptors", e);
+    return CKV_OK;
+}
+
+size_t int8_stride(size_t n) { return align16(ckv::align4(static_cast<uint32_t>(n)) + 4); }
+
+}  // namespace
+
+extern "C" {
+
+ckv_status ckv_pipe_store_int8(ckv_pipe* p, const void* const* pages, size_t count, size_t n,
+                               uint8_t* host, size_t capacity, size_t* offsets, size_t* sizes,
+                               size_t* total, uint64_t after, uint64_t* ticket, void* stream_ptr) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    ckv_ctx* ctx = p->ctx;
+    ctx->err.clear();
+    if (!pages || !host || !offsets || !sizes || !total || !fits_u32(n) || n == 0 ||
+        n > 0xfffffff0u)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid INT8 store arguments");
+    DeviceGuard guard(ctx->device);
+    const size_t stride = int8_stride(n);
+    const uint32_t n32 = static_cast<uint32_t>(n);
+    auto stage = [&](int, size_t c0, size_t cnt, uint8_t* dst) -> ckv_status {
+        Slot* slot = nullptr;
+        ckv::Int8Unit *units = nullptr, *dunits = nullptr;
+        uint8_t* amax = nullptr;
+        if (ckv_status st = stage_descriptors(ctx, cnt, cnt * 4, p->s_enc, &slot, &units, &dunits, &amax))
+            return st;
+        for (size_t i = 0; i < cnt; ++i) {
+            const void* page = pages[c0 + i];
+            if (!page || (reinterpret_cast<uintptr_t>(page) & 1u))
+                return fail(ctx, CKV_ERR_ARGUMENT, "invalid page %zu", c0 + i);
+            units[i] = ckv::Int8Unit{page, dst + i * stride,
+                                     reinterpret_cast<uint32_t*>(amax) + i, n32, 0u};
+        }
+        if (ckv_status st = fetch_descriptors(ctx, slot, align16(cnt * sizeof(ckv::Int8Unit)) + align16(cnt * 4), p->s_enc))
+            return st;
+        timing_begin(ctx, 3, p->s_enc);
+        cudaError_t e = ckv::launch_int8_encode(dunits, static_cast<uint32_t>(cnt), n32, p->s_enc);
+        timing_end(ctx, 3, p->s_enc);
+        release(slot, p->s_enc);
+        if (e != cudaSuccess) return cuda_fail(ctx, "INT8 encode launch", e);
+        return CKV_OK;
+    };
+    ckv_status st = pipe_store_fixed(p, count, stride, host, capacity, offsets, total, after, ticket,
+                                     static_cast<cudaStream_t>(stream_ptr), stage);
+    if (st == CKV_OK)
+        for (size_t i = 0; i < count; ++i) sizes[i] = ckv::align4(n32) + 4;
+    return st;
+}
+
+ckv_status ckv_pipe_restore_int8(ckv_pipe* p, const uint8_t* host, const size_t* offsets,
+                                 size_t count, size_t n, void* const* dst, uint64_t after,
+                                 uint64_t* ticket, void* stream_ptr) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    ckv_ctx* ctx = p->ctx;
+    ctx->err.clear();
+    if (!host || !offsets || !dst || !fits_u32(n) || n == 0 || n > 0xfffffff0u)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid INT8 restore arguments");
+    DeviceGuard guard(ctx->device);
+    const uint32_t n32 = static_cast<uint32_t>(n);
+    auto unstage = [&](int, size_t c0, size_t cnt, uint8_t* land, size_t lo) -> ckv_status {
+        Slot* slot = nullptr;
+        ckv::Int8Unit *units = nullptr, *dunits = nullptr;
+        if (ckv_status st = stage_descriptors<ckv::Int8Unit>(ctx, cnt, 0, p->s_dec, &slot, &units,
+                                                             &dunits, nullptr))
+            return st;
+        for (size_t i = 0; i < cnt; ++i)
+            units[i] = ckv::Int8Unit{dst[c0 + i], land + (offsets[c0 + i] - lo), nullptr, n32, 0u};
+        if (ckv_status st = fetch_descriptors(ctx, slot, cnt * sizeof(ckv::Int8Unit), p->s_dec))
+            return st;
+        timing_begin(ctx, 4, p->s_dec);
+        cudaError_t e = ckv::launch_int8_decode(dunits, static_cast<uint32_t>(cnt), n32, p->s_dec);
+        timing_end(ctx, 4, p->s_dec);
+        release(slot, p->s_dec);
+        if (e != cudaSuccess) return cuda_fail(ctx, "INT8 decode launch", e);
+        return CKV_OK;
+    };
+    return pipe_restore_fixed(p, host, offsets, count, ckv::align4(n32) + 4, dst, after, ticket,
+                              static_cast<cudaStream_t>(stream_ptr), unstage);
+}
+
+ckv_status ckv_pipe_store_raw(ckv_pipe* p, const void* const* pages, size_t count,
+                              size_t page_bytes, uint8_t* host, size_t capacity, size_t* offsets,
+                              size_t* total, uint64_t after, uint64_t* ticket, void* stream_ptr) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    ckv_ctx* ctx = p->ctx;
+    ctx->err.clear();
+    if (!pages || !host || !offsets || !total || page_bytes == 0)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid raw store arguments");
+    DeviceGuard guard(ctx->device);
+    const size_t stride = align16(page_bytes);
+    auto stage = [&](int, size_t c0, size_t cnt, uint8_t* dst) -> ckv_status {
+        Slot* slot = nullptr;
+        ckv::CopyUnit *units = nullptr, *dunits = nullptr;
+        if (ckv_status st = stage_descriptors<ckv::CopyUnit>(ctx, cnt, 0, p->s_enc, &slot, &units,
+                                                             &dunits, nullptr))
+            return st;
+        for (size_t i = 0; i < cnt; ++i) {
+            if (!pages[c0 + i]) return fail(ctx, CKV_ERR_ARGUMENT, "null page %zu", c0 + i);
+            units[i] = ckv::CopyUnit{static_cast<const uint8_t*>(pages[c0 + i]), dst + i * stride,
+                                     page_bytes};
+        }
+        if (ckv_status st = fetch_descriptors(ctx, slot, cnt * sizeof(ckv::CopyUnit), p->s_enc))
+            return st;
+        timing_begin(ctx, 5, p->s_enc);
+        cudaError_t e = ckv::launch_copy(dunits, static_cast<uint32_t>(cnt), page_bytes, p->s_enc);
+        timing_end(ctx, 5, p->s_enc);
+        release(slot, p->s_enc);
+        if (e != cudaSuccess) return cuda_fail(ctx, "raw gather launch", e);
+        return CKV_OK;
+    };
+    return pipe_store_fixed(p, count, stride, host, capacity, offsets, total, after, ticket,
+                            static_cast<cudaStream_t>(stream_ptr), stage);
+}
+
+ckv_status ckv_pipe_restore_raw(ckv_pipe* p, const uint8_t* host, const size_t* offsets,
+                                size_t count, size_t page_bytes, void* const* dst, uint64_t after,
+                                uint64_t* ticket, void* stream_ptr) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    ckv_ctx* ctx = p->ctx;
+    ctx->err.clear();
+    if (!host || !offsets || !dst || page_bytes == 0)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid raw restore arguments");
+    DeviceGuard guard(ctx->device);
+    auto unstage = [&](int, size_t c0, size_t cnt, uint8_t* land, size_t lo) -> ckv_status {
+        Slot* slot = nullptr;
+        ckv::CopyUnit *units = nullptr, *dunits = nullptr;
+        if (ckv_status st = stage_descriptors<ckv::CopyUnit>(ctx, cnt, 0, p->s_dec, &slot, &units,
+                                                             &dunits, nullptr))
+            return st;
+        for (size_t i = 0; i < cnt; ++i)
+            units[i] = ckv::CopyUnit{land + (offsets[c0 + i] - lo),
+                                     static_cast<uint8_t*>(dst[c0 + i]), page_bytes};
+        if (ckv_status st = fetch_descriptors(ctx, slot, cnt * sizeof(ckv::CopyUnit), p->s_dec))
+            return st;
+        timing_begin(ctx, 5, p->s_dec);
+        cudaError_t e = ckv::launch_copy(dunits, static_cast<uint32_t>(cnt), page_bytes, p->s_dec);
+        timing_end(ctx, 5, p->s_dec);
+        release(slot, p->s_dec);
+        if (e != cudaSuccess) return cuda_fail(ctx, "raw scatter launch", e);
+        return CKV_OK;
+    };
+    return pipe_restore_fixed(p, host, offsets, count, page_bytes, dst, after, ticket,
+                              static_cast<cudaStream_t>(stream_ptr), unstage);
+}
+
+size_t ckv_pipe_host_capacity_int8(size_t count, size_t n) { return count * int8_stride(n); }
+
+size_t ckv_pipe_host_capacity_raw(size_t count, size_t page_bytes) {
+    return count * align16(page_bytes);
 }
 
 ckv_status ckv_pipe_join(ckv_pipe* p, uint64_t ticket, void* stream) {

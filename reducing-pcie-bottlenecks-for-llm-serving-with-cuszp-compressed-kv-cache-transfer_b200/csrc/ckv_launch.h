@@ -40,6 +40,26 @@ struct PackUnit {
     uint64_t offset;           // byte offset in the destination slab
 };
 
+// One page of the INT8 codec: the page (BF16, n elements) and its stored
+// form (n int8 values, FP32 scale at byte align4(n)).  amax is a zeroed
+// device word the encoder folds the page's max |x| into.
+struct Int8Unit {
+    const void* page;
+    uint8_t* q;
+    uint32_t* amax;
+    uint32_t n;
+    uint32_t pad;
+};
+
+// One byte copy.
+struct CopyUnit {
+    const uint8_t* src;
+    uint8_t* dst;
+    uint64_t bytes;
+};
+
+__host__ __device__ constexpr uint32_t align4(uint32_t x) { return (x + 3u) & ~3u; }
+
 // Work items (256 blocks each) of a unit of n elements in the decoder.
 uint32_t decode_items(uint32_t n);
 
@@ -51,6 +71,14 @@ cudaError_t launch_encode(const EncodeLaunch& l, cudaStream_t stream);
 cudaError_t launch_decode(const DecodeLaunch& l, cudaStream_t stream);
 cudaError_t launch_pack(const PackUnit* units, uint32_t count, uint64_t max_size,
                         uint8_t* dst, cudaStream_t stream);
+// INT8 codec: page max then quantise (two launches), or dequantise.
+cudaError_t launch_int8_encode(const Int8Unit* units, uint32_t count, uint32_t max_n,
+                               cudaStream_t stream);
+cudaError_t launch_int8_decode(const Int8Unit* units, uint32_t count, uint32_t max_n,
+                               cudaStream_t stream);
+// Byte copies (raw page gather / scatter).
+cudaError_t launch_copy(const CopyUnit* units, uint32_t count, uint64_t max_bytes,
+                        cudaStream_t stream);
 // Copies `bytes` (a multiple of 16, both addresses 16-byte aligned) from
 // mapped page-locked host memory to device memory with a kernel.
 cudaError_t launch_fetch(const void* mapped_src, void* dst, size_t bytes, cudaStream_t stream);
