@@ -356,7 +356,7 @@ def codec_baselines(host_pages: torch.Tensor, pages_dev: torch.Tensor, sample: i
 
 
 class OurCodec:
-    def __init__(self, device: torch.device, pages_dev: torch.Tensor):
+    def __init__(self, device: torch.device, pages_dev: torch.Tensor, chunk_pages: int = 0):
         import _ckv
         self.ckv = _ckv
         self.lib = _ckv.load()
@@ -388,7 +388,8 @@ class OurCodec:
         # store and a restore in flight together keep both directions busy
         # without splitting the job (smaller chunks bound the staging memory)
         self.pipe = C.c_void_p()
-        self._check(self.lib.ckv_pipe_create(self.ctx, count, C.byref(self.pipe)), "pipe")
+        self.chunk = chunk_pages if chunk_pages > 0 else count
+        self._check(self.lib.ckv_pipe_create(self.ctx, self.chunk, C.byref(self.pipe)), "pipe")
         host_cap = int(self.lib.ckv_pipe_host_capacity(count, n))
         self.hslab = [torch.empty(host_cap, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
         self.hmeta = [{"offsets": (C.c_size_t * count)(), "sizes": (C.c_size_t * count)(),
@@ -678,7 +679,8 @@ def pipeline_codecs(codec, steps: int, flush: torch.Tensor, device) -> dict:
 
 
 def raw_pcie(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -> float:
-    """Raw pinned D2H + H2D of the uncompressed pages (the PCIe reference point)."""
+    """Raw pinned D2H + H2D of the uncompressed pages, one after the other (the
+    PCIe reference point): seconds for `steps` steps of 2 x the pages' bytes."""
     pinned = torch.empty(pages_dev.numel() * 2, dtype=torch.uint8, pin_memory=True)
     src = pages_dev.view(-1).view(torch.uint8)
     back = torch.empty_like(src)
@@ -691,7 +693,7 @@ def raw_pcie(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -
         step()
     torch.cuda.synchronize(device)
     times, _ = timed_steps(step, steps, flush, device)
-    return 2 * src.numel() / (statistics.mean(times) / 1e3) / 1e9
+    return sum(times) / 1e3
 
 
 def slowest_rank(seconds: list[float], dist=None, device=None) -> list[float]:
@@ -711,7 +713,8 @@ def job_rate(world: int, raw_bytes: int, steps: int, seconds: float) -> float:
 
 def raw_pcie_duplex(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -> float:
     """Raw pinned D2H and H2D of the uncompressed pages at the same time on two
-    streams (the link ceiling for a store overlapped with a restore)."""
+    streams (the link ceiling for a store overlapped with a restore): seconds
+    for `steps` steps of 2 x the pages' bytes."""
     src = pages_dev.view(-1).view(torch.uint8)
     pinned_out = torch.empty(src.numel(), dtype=torch.uint8, pin_memory=True)
     pinned_in = torch.empty(src.numel(), dtype=torch.uint8, pin_memory=True)
@@ -734,7 +737,7 @@ def raw_pcie_duplex(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, de
         step()
     torch.cuda.synchronize(device)
     times, _ = timed_steps(step, steps, flush, device)
-    return 2 * src.numel() / (statistics.mean(times) / 1e3) / 1e9
+    return sum(times) / 1e3
 
 
 def main() -> int:
@@ -745,6 +748,8 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--pages", type=int, default=PAGES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--chunk-pages", type=int, default=0,
+                    help="pages per pipeline chunk (0: the whole job in one chunk)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -792,7 +797,8 @@ def main() -> int:
             print(json.dumps(line))
         return 0
 
-    codec = OurCodec(device, pages_dev) if impl == "ours" else RefCodec(device, pages_dev)
+    codec = (OurCodec(device, pages_dev, args.chunk_pages) if impl == "ours"
+             else RefCodec(device, pages_dev))
     pipelined = impl == "ours"
     for _ in range(args.warmup):
         codec.step()
@@ -850,8 +856,17 @@ def main() -> int:
     value = job_rate(world, raw_bytes, args.steps, t_step)
     e2e = job_rate(world, raw_bytes, args.steps, t_e2e)
     e2e_serial = job_rate(world, raw_bytes, args.steps, t_serial) if t_serial else None
-    pcie = raw_pcie(pages_dev, min(args.steps, 10), flush, device) if rank == 0 else None
-    pcie_duplex = raw_pcie_duplex(pages_dev, min(args.steps, 10), flush, device) if rank == 0 else None
+    # the link ceilings at the same GPU count: every rank copies at once (GPUs
+    # may share a PCIe switch and the host's memory), slowest rank's time
+    raw_steps = min(args.steps, 10)
+    barrier()
+    t_raw = raw_pcie(pages_dev, raw_steps, flush, device)
+    barrier()
+    t_dup = raw_pcie_duplex(pages_dev, raw_steps, flush, device)
+    barrier()
+    t_raw, t_dup = slowest_rank([t_raw, t_dup], dist, device)
+    pcie = world * 2 * pages_dev.numel() * 2 * raw_steps / t_raw / 1e9
+    pcie_duplex = world * 2 * pages_dev.numel() * 2 * raw_steps / t_dup / 1e9
 
     if rank != 0:
         if dist is not None:
@@ -889,8 +904,8 @@ def main() -> int:
                 if totals else compressed,
                 "ms_per_step": round(t_e2e * 1e3 / args.steps, 4),
                 "path": ("ckv_pipe_store_bf16 of step k's pages into one pinned slab, "
-                         "overlapped with ckv_pipe_restore_bf16 of step k-1's slab; one chunk per "
-                         "job") if pipelined else
+                         "overlapped with ckv_pipe_restore_bf16 of step k-1's slab; "
+                         f"{codec.chunk} pages per chunk") if pipelined else
                         "compress, torch.cat pack, one D2H, one H2D, decompress (in order)",
                 "serial_value": round(e2e_serial, 3) if e2e_serial else None,
                 "restore_matches_kernel_path": e2e_match,
