@@ -42,7 +42,7 @@ namespace {
 constexpr uint32_t kItemBlocks = kThreads;               // 256, one per consumer thread
 constexpr int kConsumerWarps = kThreads / 32;            // 8
 constexpr int kCtaThreads = kThreads + 32;               // + the producer warp
-constexpr int kSlots = 4;
+constexpr int kSlots = 3;
 constexpr uint32_t kPayloadCap = kItemBlocks * 64 + 32;  // every block of rate <= 15
 constexpr uint32_t kOffsAt = kPayloadCap;
 constexpr uint32_t kRatesAt = kOffsAt + kItemBlocks * 4;

@@ -533,8 +533,32 @@ __device__ void analyse(const EncodeArgs& a, uint32_t count, uint32_t first, uin
         }
         if (abar_or(*reinterpret_cast<volatile uint32_t*>(&sy.broken) != 0)) return;
         float tlo = FLT_MAX, thi = -FLT_MAX;
-#pragma unroll 2
-        for (uint32_t i = t; i < s.nbs; i += kAThreads) {
+        // Full blocks four at a time: every load of a group is issued before
+        // its stores (which the compiler cannot move across later loads).
+        const uint32_t nfull = min(s.nbs, (s.n - s.e0) / kBlock);
+        uint32_t i = t;
+        for (; i + 3 * kAThreads < nfull; i += 4 * kAThreads) {
+            uint32_t w[4][Traits<T>::kWords];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) load_block<T>(slice + (i + g * kAThreads) * BB, rho, w[g]);
+            float lo[4], hi[4];
+            bool nan[4];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) block_extremes<T>(w[g], lo[g], hi[g], nan[g]);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const uint32_t ig = i + g * kAThreads;
+                if constexpr (sizeof(T) == 2)
+                    reinterpret_cast<uint32_t*>(meta)[ig] =
+                        (__float_as_uint(lo[g]) >> 16) | (__float_as_uint(hi[g]) & 0xffff0000u);
+                else
+                    reinterpret_cast<float2*>(meta)[ig] = make_float2(lo[g], hi[g]);
+                rates[ig] = nan[g] ? kNanFlag : 0;
+                tlo = fminf(tlo, lo[g]);
+                thi = fmaxf(thi, hi[g]);
+            }
+        }
+        for (; i < s.nbs; i += kAThreads) {
             const uint8_t* blk = slice + i * BB;
             float lo, hi;
             bool nan;
@@ -612,30 +636,42 @@ __device__ void analyse(const EncodeArgs& a, uint32_t count, uint32_t first, uin
         const float recip = sy.info[b].recip;
         const uint32_t run = (s.nbs + kAThreads - 1) / kAThreads;
         const uint32_t i0 = t * run;
+        // every load of the run first, then the arithmetic, then the stores
+        float lo[kMaxRun], hi[kMaxRun];
+        uint32_t flag[kMaxRun], sz[kMaxRun];
+#pragma unroll
+        for (uint32_t k = 0; k < kMaxRun; ++k) {
+            lo[k] = hi[k] = 0.0f;
+            flag[k] = 0;
+            const uint32_t ik = i0 + k;
+            if (k < run && ik < s.nbs) {
+                if constexpr (sizeof(T) == 2) {
+                    const uint32_t p = reinterpret_cast<const uint32_t*>(meta)[ik];
+                    lo[k] = __uint_as_float(p << 16);
+                    hi[k] = __uint_as_float(p & 0xffff0000u);
+                } else {
+                    const float2 p = reinterpret_cast<const float2*>(meta)[ik];
+                    lo[k] = p.x;
+                    hi[k] = p.y;
+                }
+                flag[k] = rates[ik] & kNanFlag;
+            }
+        }
         uint32_t local = 0;
 #pragma unroll
         for (uint32_t k = 0; k < kMaxRun; ++k) {
-            const uint32_t i = i0 + k;
-            if (k < run && i < s.nbs) {
-                float lo, hi;
-                if constexpr (sizeof(T) == 2) {
-                    const uint32_t p = reinterpret_cast<const uint32_t*>(meta)[i];
-                    lo = __uint_as_float(p << 16);
-                    hi = __uint_as_float(p & 0xffff0000u);
-                } else {
-                    const float2 p = reinterpret_cast<const float2*>(meta)[i];
-                    lo = p.x;
-                    hi = p.y;
-                }
-                const bool nan = rates[i] & kNanFlag;
-                uint32_t mq = 0;
-                if (lo == lo) mq = max(uabs(quantize(lo, recip)), uabs(quantize(hi, recip)));
-                if (nan) mq = max(mq, 1u);
-                const uint32_t r = 32 - __clz(mq);
-                rates[i] = static_cast<uint8_t>(r | (nan ? kNanFlag : 0));
-                local += r ? 4 + 4 * r : 0u;
-            }
+            uint32_t mq = 0;
+            if (lo[k] == lo[k]) mq = max(uabs(quantize(lo[k], recip)), uabs(quantize(hi[k], recip)));
+            if (flag[k]) mq = max(mq, 1u);
+            const uint32_t r = 32 - __clz(mq);
+            const bool in = k < run && i0 + k < s.nbs;
+            sz[k] = in && r ? 4 + 4 * r : 0u;
+            flag[k] |= r;
+            local += sz[k];
         }
+#pragma unroll
+        for (uint32_t k = 0; k < kMaxRun; ++k)
+            if (k < run && i0 + k < s.nbs) rates[i0 + k] = static_cast<uint8_t>(flag[k]);
         uint32_t inc = local;
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
@@ -656,12 +692,8 @@ __device__ void analyse(const EncodeArgs& a, uint32_t count, uint32_t first, uin
         uint32_t off = pre + inc - local;
 #pragma unroll
         for (uint32_t k = 0; k < kMaxRun; ++k) {
-            const uint32_t i = i0 + k;
-            if (k < run && i < s.nbs) {
-                reinterpret_cast<uint32_t*>(meta)[i] = off;
-                const uint32_t r = rates[i] & 0x3f;
-                off += r ? 4 + 4 * r : 0u;
-            }
+            if (k < run && i0 + k < s.nbs) reinterpret_cast<uint32_t*>(meta)[i0 + k] = off;
+            off += sz[k];
         }
         if (awarp == 0) {
             if (lane == 0) mbar_arrive_expect_tx(&sy.tot_bar[x], csize * sizeof(uint32_t));
@@ -701,6 +733,20 @@ __device__ void analyse(const EncodeArgs& a, uint32_t count, uint32_t first, uin
 }
 
 // ---- pack warps ----------------------------------------------------------------
+
+// A warp copies `words` words from shared to global memory, four loads in
+// flight per lane before their stores.
+__device__ __forceinline__ void copy_out(const uint32_t* src, uint32_t* dst, uint32_t words,
+                                         int lane) {
+    for (uint32_t k = lane; k < words; k += 128) {
+        uint32_t v[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) v[t] = k + 32 * t < words ? src[k + 32 * t] : 0u;
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+            if (k + 32 * t < words) dst[k + 32 * t] = v[t];
+    }
+}
 
 template <typename T>
 __device__ void pack(uint32_t count, const ShiftMul& mul, uint8_t* smem, Sync& sy) {
@@ -759,10 +805,9 @@ __device__ void pack(uint32_t count, const ShiftMul& mul, uint8_t* smem, Sync& s
                     }
                     const uint32_t end = __reduce_max_sync(0xffffffffu, active && r ? pos + 4 + 4 * r : 0u);
                     __syncwarp();
-                    const uint32_t words = end > p0 ? (end - p0) >> 2 : 0u;
-                    const uint32_t* src = reinterpret_cast<const uint32_t*>(chunk);
-                    uint32_t* dst = reinterpret_cast<uint32_t*>(info.out + p0);
-                    for (uint32_t k = lane; k < words; k += 32) dst[k] = src[k];
+                    copy_out(reinterpret_cast<const uint32_t*>(chunk),
+                             reinterpret_cast<uint32_t*>(info.out + p0),
+                             end > p0 ? (end - p0) >> 2 : 0u, lane);
                 } else if (active) {
                     const uint32_t valid = min(info.n - (info.b0 + i) * kBlock, uint32_t(kBlock));
                     uint32_t* out = reinterpret_cast<uint32_t*>(info.out + pos);
