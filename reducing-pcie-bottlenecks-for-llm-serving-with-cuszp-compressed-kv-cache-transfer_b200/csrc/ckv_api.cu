@@ -314,6 +314,19 @@ ckv_status run_decode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, void* stream_p
                                  [](const Unit& u) { return u.n == 0; }),
                   b.units.end());
     if (b.units.empty()) return CKV_OK;
+    // The decoder reads every unit's header (its rate bytes) before it can
+    // check the payload against the size: a size below the header is refused
+    // here, so that no read passes the caller's buffer.
+    for (size_t i = 0; i < b.units.size(); ++i) {
+        const Unit& u = b.units[i];
+        const uint64_t hdr = (static_cast<uint64_t>(u.n) + ckv::kGroup - 1) / ckv::kGroup *
+                             (ckv::kGroup / ckv::kBlock);
+        if (u.capacity < hdr)
+            return fail(ctx, CKV_ERR_ARGUMENT,
+                        "compressed unit %zu of %llu bytes is shorter than its %llu-byte header", i,
+                        static_cast<unsigned long long>(u.capacity),
+                        static_cast<unsigned long long>(hdr));
+    }
     const size_t count = b.units.size();
     uint32_t items = 0;
     bool uniform = true;

@@ -50,6 +50,8 @@ constexpr uint32_t kSlotBytes = (kRatesAt + kItemBlocks + 127) / 128 * 128;
 constexpr uint32_t kSmem = kSlots * kSlotBytes;
 constexpr uint32_t kWaitPolls = 1u << 22;
 constexpr int kCtasPerSm = 3;
+constexpr int kAhead = 3;                 // items whose rate bytes the producer has in flight
+constexpr int kRing = kAhead + 1;
 
 struct DecodeArgs {
     const Unit* units;
@@ -118,12 +120,18 @@ __device__ __forceinline__ void unpack_general(const uint32_t* words, uint32_t r
 // low half of A[k], rows k >= 16 in the high half of A[k - 16]; the moves of
 // a row into place are multiplies (FMA pipe), the masks and the sign flip
 // one bit select each.
+//
+// `whole`: the 15 words after the sign word may be read whatever the rate (a
+// block in a shared-memory slot); planes at and above the rate are then
+// removed by masking the rows' magnitudes instead of zeroing the words.
+template <bool whole>
 __device__ __forceinline__ void unpack_fast(const uint32_t* words, uint32_t rate, float eb2,
                                             float negc, const ShiftMul& mul, float (&f)[32]) {
     uint32_t A[16];
 #pragma unroll
-    for (int b = 0; b < 15; ++b) A[b] = b < static_cast<int>(rate) ? words[1 + b] : 0u;
+    for (int b = 0; b < 15; ++b) A[b] = whole || b < static_cast<int>(rate) ? words[1 + b] : 0u;
     A[15] = words[0];
+    const uint32_t keep = whole ? (1u << rate) - 1u : 0x7fffu;
     transpose16_mul(A, mul);
 #pragma unroll
     for (int v = 0; v < 32; ++v) {
@@ -136,7 +144,7 @@ __device__ __forceinline__ void unpack_fast(const uint32_t* words, uint32_t rate
             mag = __umulhi(A[k - 16], mul.r16);   // high half -> low half
             sign = A[k - 16];
         }
-        const float x = __fmaf_rn(__uint_as_float(0x4b000000u | (mag & 0x7fffu)), eb2, negc);
+        const float x = __fmaf_rn(__uint_as_float(0x4b000000u | (mag & keep)), eb2, negc);
         f[v] = __uint_as_float(__float_as_uint(x) ^ (sign & 0x80000000u));
     }
 }
@@ -225,7 +233,7 @@ __device__ __forceinline__ void locate(const DecodeArgs& a, uint32_t item, uint3
 }
 
 // The producer's view of an item: the unit's fields and this lane's 8 rate
-// bytes (blocks 8*lane .. 8*lane+7 of the item).
+// bytes (blocks 8*lane .. 8*lane+7 of the item, read from the rate ring).
 struct PItem {
     const uint8_t* stream;
     const void* elems;
@@ -234,29 +242,6 @@ struct PItem {
     float eb;
     uint32_t r_lo, r_hi;
 };
-
-__device__ __forceinline__ void p_rates(PItem& it) {
-    const uint32_t first = 8 * (threadIdx.x & 31);
-    const uint8_t* p = it.stream + it.b0 + first;
-    it.r_lo = 0;
-    it.r_hi = 0;
-    if (first + 8 <= it.nbs) {
-        // b0 is a multiple of 256 and streams are 4-byte aligned
-        it.r_lo = __ldg(reinterpret_cast<const uint32_t*>(p));
-        it.r_hi = __ldg(reinterpret_cast<const uint32_t*>(p) + 1);
-    } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            if (first + j < it.nbs) {
-                const uint32_t byte = __ldg(p + j);
-                if (j < 4)
-                    it.r_lo |= byte << (8 * j);
-                else
-                    it.r_hi |= byte << (8 * (j - 4));
-            }
-        }
-    }
-}
 
 __device__ __forceinline__ void p_open(const DecodeArgs& a, uint32_t u, uint32_t s, PItem& it) {
     const Unit unit = a.units[u];
@@ -273,20 +258,65 @@ __device__ __forceinline__ void p_open(const DecodeArgs& a, uint32_t u, uint32_t
     it.s = s;
     it.b0 = s * kItemBlocks;
     it.nbs = min(kItemBlocks, (unit.n + kBlock - 1) / kBlock - it.b0);
-    p_rates(it);
 }
 
-// The item after `it` in item order; within a unit only the rate bytes load.
+// The item after `it` in item order (its unit record loads only when the
+// unit changes).
 __device__ __forceinline__ void p_next(const DecodeArgs& a, const PItem& it, PItem& nx) {
     if (it.s + 1 < it.items) {
         nx = it;
         nx.s = it.s + 1;
         nx.b0 = nx.s * kItemBlocks;
         nx.nbs = min(kItemBlocks, (it.n + kBlock - 1) / kBlock - nx.b0);
-        p_rates(nx);
     } else {
         p_open(a, it.u + 1, 0, nx);
     }
+}
+
+// Where the producer fetches rate bytes next, kAhead items ahead of the item
+// it sets up.
+struct RateCursor {
+    const uint8_t* stream;
+    uint32_t u, s, items, nb;
+};
+
+__device__ __forceinline__ void rc_open(const DecodeArgs& a, uint32_t u, uint32_t s,
+                                        RateCursor& c) {
+    const Unit unit = a.units[u];
+    c.stream = unit.stream;
+    c.u = u;
+    c.s = s;
+    c.items = items_of(unit.n);
+    c.nb = (unit.n + kBlock - 1) / kBlock;
+}
+
+// Starts the copy of the cursor's item's rate bytes into `ring` (64 words,
+// lane l copies words 2l and 2l+1; words past the unit's blocks are not
+// copied and are masked where they are read), then steps the cursor.
+__device__ __forceinline__ void rc_fetch(const DecodeArgs& a, RateCursor& c, uint32_t* ring) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t b0 = c.s * kItemBlocks;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t first = b0 + 8 * lane + 4 * h;
+        // inside the header: nb <= header bytes, both multiples of 4 apart
+        if (first < c.nb) cp_async4(ring + 2 * lane + h, c.stream + first);
+    }
+    if (c.s + 1 < c.items)
+        ++c.s;
+    else
+        rc_open(a, c.u + 1, 0, c);
+}
+
+// This lane's 8 rate bytes of an item from the ring (blocks 8l .. 8l+7; zero
+// past the item's nbs blocks).
+__device__ __forceinline__ void rc_read(const uint32_t* ring, uint32_t nbs, uint32_t& lo,
+                                        uint32_t& hi) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t first = 8 * lane;
+    const uint2 w = *reinterpret_cast<const uint2*>(ring + 2 * lane);
+    lo = first >= nbs ? 0u : first + 4 <= nbs ? w.x : w.x & ((1u << (8 * (nbs - first))) - 1u);
+    hi = first + 4 >= nbs ? 0u : first + 8 <= nbs ? w.y : w.y & ((1u << (8 * (nbs - first - 4))) - 1u);
 }
 
 template <typename T>
@@ -295,6 +325,7 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
     __shared__ uint64_t full[kSlots], empty[kSlots];
     __shared__ SlotMeta meta[kSlots];
     __shared__ uint32_t red[kCtaThreads / 32][2];
+    __shared__ __align__(16) uint32_t rring[kRing][kItemBlocks / 4];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     const uint32_t begin = static_cast<uint32_t>(
@@ -352,6 +383,12 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
         uint32_t status = 0;
         PItem cur, nxt;
         p_open(a, u0, s0, cur);
+        RateCursor rc;
+        rc_open(a, u0, s0, rc);
+        for (int i = 0; i < kAhead; ++i) {
+            if (begin + i < end) rc_fetch(a, rc, rring[i]);
+            cp_async_commit();
+        }
         uint64_t start = first_start;
         bool unit_ok = first_ok;
         if (!first_ok && lane == 0) atomicOr(&a.status[cur.u], kErrBadStream);
@@ -359,8 +396,11 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
         for (uint32_t item = begin; item < end; ++item, ++k) {
             const int slot = static_cast<int>(k % kSlots);
             const uint32_t use = k / kSlots;
-            // the next item's rate bytes load while this one is set up and
-            // while the producer waits for a free slot
+            // rate bytes kAhead items ahead; this item's have landed
+            if (item + kAhead < end) rc_fetch(a, rc, rring[(k + kAhead) % kRing]);
+            cp_async_commit();
+            cp_async_wait<kAhead>();
+            rc_read(rring[k % kRing], cur.nbs, cur.r_lo, cur.r_hi);
             if (item + 1 < end) p_next(a, cur, nxt);
 
             // block sizes of this lane's 8 blocks, then a warp scan
@@ -490,7 +530,12 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
                 const bool safe = eb >= 7.8886091e-31f && eb <= 1.2676506e30f;
                 if (rate <= 15 && safe) {
                     const float eb2 = __fmul_rn(eb, 2.0f);
-                    unpack_fast(words, rate, eb2, __fmul_rn(eb2, -8388608.0f), a.mul, f);
+                    // in a slot the words past the block stay inside the slot
+                    // (payload cap + offsets + rates follow the payload)
+                    if (m.flags & kInSlot)
+                        unpack_fast<true>(words, rate, eb2, __fmul_rn(eb2, -8388608.0f), a.mul, f);
+                    else
+                        unpack_fast<false>(words, rate, eb2, __fmul_rn(eb2, -8388608.0f), a.mul, f);
                 } else {
                     unpack_general(words, rate, eb, f);
                 }

@@ -376,6 +376,23 @@ __device__ __forceinline__ bool mbar_spin_bounded(uint64_t* bar, uint32_t parity
     return false;
 }
 
+// Asynchronous 4-byte copy global -> shared memory: no register holds the
+// value, so a warp can keep several of them in flight across iterations.
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem_dst)), "l"(src)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Waits until at most N of this thread's committed groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Cluster-wide barrier that does not require converged warps.
 __device__ __forceinline__ void cluster_barrier() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");

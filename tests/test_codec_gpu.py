@@ -391,6 +391,8 @@ def test_error_behaviour(cpp):
     assert w.decompress_batch_fixed_bf16([good], [sizes[0] - 4], out, 8192, bounds)
     assert w.device_status() & 4
     assert w.device_status() == 0
+    # a size below the header (1024 rate bytes here) is refused before launch
+    assert w.decompress_batch_fixed_bf16([good], [1020], out, 8192, bounds) is False
     # tiny units: the header alone exceeds 8 * n bytes -> capacity error
     tiny = torch.randn(16, device="cuda").to(torch.bfloat16)
     assert w.compress_batch_fixed_bf16([tiny], [torch.empty(128, dtype=torch.uint8,
