@@ -289,21 +289,36 @@ __device__ __forceinline__ bool masked(int e, int rho, uint32_t valid) {
     return static_cast<uint32_t>(8 * (((e >> 3) + rho) & 3) + (e & 7)) >= valid;
 }
 
-// (|q| << 1) | sign for |q| < 2^15 and no NaN, as batch_quantization
-// (cuszp_batched_fixed.cu:10-25) computes it: r = x * recip and
-// t = r + 0.5, each rounded; trunc(|t|) from a round-toward-zero add of 2^23
-// (exact for |t| < 2^23).  The reference's s = (r < -0.5) is the sign bit of
-// t: r + 0.5 is exact for r in [-1, -0.5) (Sterbenz), so t < 0 exactly when
-// r < -0.5, and t is never -0.  Then |q| = trunc(|t|) + s and the row is
-// 2 * trunc(|t|) + 3 * s, written as integer multiply-adds.
-// The integer steps are multiply-adds with multipliers from `mul` (FMA pipe).
-__device__ __forceinline__ uint32_t narrow_row(float x, float recip, const ShiftMul& mul) {
-    const float r = __fmul_rn(x, recip);
-    const float t = __fadd_rn(r, 0.5f);
-    const float z = __fadd_rz(fabsf(t), 8388608.0f);
-    const uint32_t twice = __float_as_uint(z) * mul.l1 - 0x96000000u;   // 2 * trunc(|t|)
-    const uint32_t neg = static_cast<uint32_t>(static_cast<int32_t>(__float_as_uint(t)) >> 31);
-    return twice + neg * mul.neg3;   // + 3 when t < 0
+// Two rows (|q| << 1) | sign, for |q| < 2^15 and no NaN, packed as the low
+// and high halves of one word, as batch_quantization
+// (cuszp_batched_fixed.cu:10-25) computes q: r = x * recip and t = r + 0.5,
+// each rounded; trunc(|t|) from a round-toward-zero add of 2^23 (exact for
+// |t| < 2^23; the float's low 16 bits are then trunc(|t|)).  The reference's
+// s = (r < -0.5) is the sign bit of t: r + 0.5 is exact for r in [-1, -0.5)
+// (Sterbenz), so t < 0 exactly when r < -0.5, and t is never -0.  Then
+// |q| = trunc(|t|) + s and the row is 2 * trunc(|t|) + 3 * s (< 2^16, so the
+// halves never carry into each other): one byte permute gathers both
+// truncations, one sign-replicating byte permute both signs, and one
+// multiply-add forms both rows.
+// prmt.b32 in its default mode, where a selector nibble of 8-15 replicates
+// the sign bit of byte (nibble & 7) over the result byte (the __byte_perm
+// intrinsic uses only the low 3 bits of each nibble).
+__device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t narrow_pair(float x_lo, float x_hi, float recip,
+                                                const ShiftMul& mul) {
+    const float t_lo = __fadd_rn(__fmul_rn(x_lo, recip), 0.5f);
+    const float t_hi = __fadd_rn(__fmul_rn(x_hi, recip), 0.5f);
+    const float z_lo = __fadd_rz(fabsf(t_lo), 8388608.0f);
+    const float z_hi = __fadd_rz(fabsf(t_hi), 8388608.0f);
+    const uint32_t trunc2 = __byte_perm(__float_as_uint(z_lo), __float_as_uint(z_hi), 0x5410);
+    // 0xffff in each half whose t is negative
+    const uint32_t neg2 = prmt_sign(__float_as_uint(t_lo), __float_as_uint(t_hi), 0xffbbu);
+    return trunc2 * mul.l1 + (neg2 & 0x00030003u);
 }
 
 // Rows of the 16x32 bit matrix for a narrow block: A[k] holds rows k and
@@ -319,13 +334,11 @@ __device__ __forceinline__ uint32_t narrow_block(const uint32_t (&w)[Traits<T>::
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
         const int e = bitpos(k);
-        const uint32_t lo = narrow_row(elem<T>(w, e), recip, mul);
-        const uint32_t hi = narrow_row(elem<T>(w, e + 16), recip, mul);
-        orv |= lo | hi;
-        A[k] = __byte_perm(lo, hi, 0x5410);
+        A[k] = narrow_pair(elem<T>(w, e), elem<T>(w, e + 16), recip, mul);
+        orv |= A[k];
     }
     transpose16_mul(A, mul);
-    return orv;
+    return (orv | (orv >> 16)) & 0xffffu;
 }
 
 // Exact quantiser (the reference's instruction sequence) for one element.
