@@ -12,23 +12,22 @@
 //                    j-3 has been packed out of it;
 //   analysis warps   per unit: block min / max / NaN-presence (packed BF16
 //                    min/max); slice extremes pushed into every CTA of the
-//                    cluster (distributed shared memory stores + an arrive on
-//                    the receiver's mbarrier) -> absolute bound
-//                    eb = eps * fmaxf(max - min, 1e-6f)
+//                    cluster (asynchronous distributed-shared-memory stores
+//                    counted in bytes on the receiver's mbarrier) -> absolute
+//                    bound eb = eps * fmaxf(max - min, 1e-6f)
 //                    (cuszp_batched_fixed.cu:55-133); per block rate = bit
 //                    length of max(|q(block min)|, |q(block max)|) (the
 //                    quantiser is monotone; NaN contributes |q| = 1); a scan
 //                    gives every block's payload offset; slice byte totals
-//                    pushed into every CTA -> this slice's output offset,
-//                    header rate bytes; then the unit is handed to the pack
-//                    warps;
+//                    pushed into every CTA -> this slice's output offset;
+//                    then the unit is handed to the pack warps;
 //   pack warps       32-block chunks, dealt round-robin across units so no
-//                    warp waits for another: quantise, transpose into sign
-//                    word + bit planes in registers, compact the chunk's
-//                    payload in place over its own input (a block of rate
-//                    <= 15 packs into at most the 64 bytes it came from; a
-//                    warp barrier suffices) and copy it out with coalesced
-//                    stores.
+//                    warp waits for another: header rate bytes; quantise,
+//                    transpose into sign word + bit planes in registers,
+//                    compact the chunk's payload in place over its own input
+//                    (a block of rate <= 15 packs into at most the 64 bytes it
+//                    came from; a warp barrier suffices) and copy it out with
+//                    coalesced stores.
 //
 // Rate <= 15 blocks without NaN (every block at REL bounds >= 1e-5 on
 // two-sided data) use a quantiser that truncates with a round-toward-zero
