@@ -7,11 +7,12 @@
 // sums the rate bytes before it.
 //
 // Each CTA is one producer warp and eight consumer warps around a ring of
-// four slots in shared memory, with a "full" and an "empty" mbarrier per
+// three slots in shared memory, with a "full" and an "empty" mbarrier per
 // slot and no CTA-wide barrier in the loop:
 //
-//   producer warp, per item: its 256 rate bytes (loaded one item ahead) ->
-//     block sizes -> per-block payload offsets (warp scan); once the slot is
+//   producer warp, per item: its 256 rate bytes (copied into a small shared
+//     ring by cp.async three items ahead) -> block sizes -> per-block
+//     payload offsets (warp scan); once the slot is
 //     empty it stores offsets, rates and the item's description in the slot
 //     and starts one TMA bulk copy of the item's payload into it, completing
 //     on the slot's full barrier;
