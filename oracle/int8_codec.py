@@ -35,7 +35,9 @@ def encode(page_bits: np.ndarray) -> tuple[np.ndarray, np.float32]:
         scale = np.float32(np.abs(x).max()) * (np.float32(1.0) / np.float32(127.0))
         if scale == np.float32(0.0):
             scale = np.float32(1.0)
-        q = np.clip(np.rint(x / scale), -127, 127).astype(np.int8)
+        v = np.rint(x / scale)
+        # clamp keeps NaN; the int8 cast on the GPU turns it into 0
+        q = np.where(np.isnan(v), 0, np.clip(v, -127, 127)).astype(np.int8)
     return q, np.float32(scale)
 
 

@@ -32,8 +32,11 @@ __device__ __forceinline__ float page_scale(uint32_t amax_bits) {
     return scale == 0.0f ? 1.0f : scale;
 }
 
+// torch.clamp keeps a NaN quotient and the int8 cast turns it into 0 (a
+// page with a NaN has a NaN scale, so every value of it is stored as 0).
 __device__ __forceinline__ uint32_t quantise(float x, float scale) {
-    const float q = fminf(fmaxf(rintf(__fdiv_rn(x, scale)), -127.0f), 127.0f);
+    const float v = rintf(__fdiv_rn(x, scale));
+    const float q = v != v ? 0.0f : fminf(fmaxf(v, -127.0f), 127.0f);
     return static_cast<uint32_t>(static_cast<int32_t>(q)) & 0xffu;
 }
 

@@ -122,6 +122,47 @@ def test_raw_pipe_round_trip(env, count, page_bytes, chunk):
         lib.ckv_pipe_destroy(pipe)
 
 
+def test_int8_pipe_special_values(env):
+    """Pages with NaN, with Inf, and with subnormal-scale values: stored bytes
+    and restores equal the reference's expression on CUDA tensors."""
+    _ckv, lib, ctx = env
+    count, n = 4, 4096
+    pages = _pages(count, n, seed=77)
+    pages[0, 17] = float("nan")
+    pages[1, 5] = float("inf")
+    pages[1, 9] = float("-inf")
+    pages[2] = pages[2] * 1e-38
+    dev = pages.cuda()
+    pipe = C.c_void_p()
+    assert lib.ckv_pipe_create(ctx, 2, C.byref(pipe)) == 0
+    try:
+        cap = int(lib.ckv_pipe_host_capacity_int8(count, n))
+        host = torch.empty(cap, dtype=torch.uint8, pin_memory=True)
+        offsets = (C.c_size_t * count)()
+        sizes = (C.c_size_t * count)()
+        total = C.c_size_t(0)
+        t1, t2 = C.c_uint64(0), C.c_uint64(0)
+        s = torch.cuda.current_stream().cuda_stream
+        assert lib.ckv_pipe_store_int8(pipe, _ckv.ptr_array([dev[i].data_ptr() for i in range(count)]),
+                                       count, n, host.data_ptr(), cap, offsets, sizes,
+                                       C.byref(total), 0, C.byref(t1), s) == 0
+        restored = torch.zeros_like(dev)
+        assert lib.ckv_pipe_restore_int8(pipe, host.data_ptr(), offsets, count, n,
+                                         _ckv.ptr_array([restored[i].data_ptr() for i in range(count)]),
+                                         t1.value, C.byref(t2), s) == 0
+        torch.cuda.synchronize()
+        for i in range(count):
+            tq, tscale, tout = _torch_reference(dev[i])
+            q = torch.frombuffer(bytearray(bytes(host[offsets[i]:offsets[i] + n].numpy())),
+                                 dtype=torch.int8)
+            assert torch.equal(q, tq.cpu()), f"page {i}"
+            assert torch.equal(restored[i].view(torch.int16), tout.view(torch.int16)), f"page {i}"
+            oq, oscale = oc.encode(pages[i].view(torch.int16).numpy().view(np.uint16))
+            assert np.array_equal(oq, q.numpy())
+    finally:
+        lib.ckv_pipe_destroy(pipe)
+
+
 def test_int8_pipe_overlapped_jobs(env):
     """Step k stores into slab k % 2 while step k-1's slab is restored."""
     _ckv, lib, ctx = env
