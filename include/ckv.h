@@ -246,6 +246,37 @@ CKV_API int ckv_pipe_done(ckv_pipe* pipe, uint64_t ticket);
 /* Host bytes that always hold `count` compressed pages of n elements. */
 CKV_API size_t ckv_pipe_host_capacity(size_t count, size_t n);
 
+/* Layer-grouped store and restore (the connector's per-layer bound profile:
+ * _compress_adaptive_fixed_bundles_indexed, vllm_v1_compressed_offload.py:
+ * 1286-1569, which compresses each page as one segment per layer group with
+ * compress_batch_fixed_bf16_indexed_groups, and restores each group with
+ * decompress_batch_fixed_bf16_indexed_scatter).  Each page
+ * [prefix_count][source_layers][elements_per_layer] is stored as `groups`
+ * segments: segment g holds layers layer_indices[g][0..selected[g]) (device
+ * int64 arrays) of every prefix, compressed at eps[g] (NULL or <= 0: the
+ * context's bound).  Segment g of page i is entry i * groups + g of
+ * offsets / sizes / bounds.  The restore writes every group back into its
+ * layers of pages[i], all groups of a chunk in one decode launch.  The host
+ * buffer needs ckv_pipe_host_capacity_groups(...) bytes. */
+CKV_API ckv_status ckv_pipe_store_bf16_groups(ckv_pipe* pipe, const void* const* pages,
+                                              size_t count, const int64_t* const* layer_indices,
+                                              const size_t* selected, size_t groups,
+                                              size_t prefix_count, size_t source_layers,
+                                              size_t elements_per_layer, const float* eps,
+                                              uint8_t* host, size_t capacity, size_t* offsets,
+                                              size_t* sizes, float* bounds, size_t* total,
+                                              uint64_t after, uint64_t* ticket, void* stream);
+CKV_API ckv_status ckv_pipe_restore_bf16_groups(ckv_pipe* pipe, const uint8_t* host,
+                                                const size_t* offsets, const size_t* sizes,
+                                                const float* bounds, size_t count,
+                                                const int64_t* const* layer_indices,
+                                                const size_t* selected, size_t groups,
+                                                size_t prefix_count, size_t source_layers,
+                                                size_t elements_per_layer, void* const* pages,
+                                                uint64_t after, uint64_t* ticket, void* stream);
+CKV_API size_t ckv_pipe_host_capacity_groups(size_t count, const size_t* selected, size_t groups,
+                                             size_t prefix_count, size_t elements_per_layer);
+
 /* The reference's comparison codecs through the same pipeline (its INT8
  * encoding, vllm_v1_compressed_offload.py:711-724 store and :2090-2116
  * restore, and its raw encoding, :1578-1615), so that they are timed on the

@@ -47,6 +47,7 @@ EXPORTS = (
     "ckv_pipe_join", "ckv_pipe_wait", "ckv_pipe_done", "ckv_pipe_host_capacity",
     "ckv_pipe_store_int8", "ckv_pipe_restore_int8", "ckv_pipe_store_raw", "ckv_pipe_restore_raw",
     "ckv_pipe_host_capacity_int8", "ckv_pipe_host_capacity_raw",
+    "ckv_pipe_store_bf16_groups", "ckv_pipe_restore_bf16_groups", "ckv_pipe_host_capacity_groups",
 )
 
 
@@ -119,6 +120,11 @@ def _declare(lib: C.CDLL) -> None:
         "ckv_pipe_restore_raw": (c_status, [P, P, P, c_size, c_size, P, C.c_uint64, P, P]),
         "ckv_pipe_host_capacity_int8": (c_size, [c_size, c_size]),
         "ckv_pipe_host_capacity_raw": (c_size, [c_size, c_size]),
+        "ckv_pipe_store_bf16_groups": (c_status, [P, P, c_size, P, P, c_size, c_size, c_size, c_size,
+                                                  P, P, c_size, P, P, P, P, C.c_uint64, P, P]),
+        "ckv_pipe_restore_bf16_groups": (c_status, [P, P, P, P, P, c_size, P, P, c_size, c_size,
+                                                    c_size, c_size, P, C.c_uint64, P, P]),
+        "ckv_pipe_host_capacity_groups": (c_size, [c_size, P, c_size, c_size, c_size]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -978,21 +978,27 @@ void ckv_pipe_destroy(ckv_pipe* p) {
     delete p;
 }
 
-ckv_status ckv_pipe_store_bf16(ckv_pipe* p, const void* const* pages, const float* eps,
-                               size_t count, size_t n, uint8_t* host, size_t capacity,
-                               size_t* offsets, size_t* sizes, float* bounds, size_t* total,
-                               uint64_t after, uint64_t* ticket, void* stream_ptr) {
-    if (!p) return CKV_ERR_ARGUMENT;
+}  // extern "C"
+
+namespace {
+
+// The fixed-mode store of `count` pages, each compressed as `per_page` units
+// (unit g of page i is entry i * per_page + g of offsets / sizes / bounds):
+// `add(b, i, g, stream, capacity)` appends that unit to the batch, whose map
+// table is `maps`.  Chunks of pages are compressed (sizes on the host),
+// packed and copied into the host buffer one after another on the
+// pipeline's streams.
+template <typename Add>
+ckv_status pipe_store_units(ckv_pipe* p, size_t count, size_t per_page,
+                            const std::vector<Map>& maps, uint32_t max_n, uint8_t* host,
+                            size_t capacity, size_t* offsets, size_t* sizes, float* bounds,
+                            size_t* total, uint64_t after, uint64_t* ticket, cudaStream_t caller,
+                            Add add) {
     ckv_ctx* ctx = p->ctx;
-    ctx->err.clear();
-    if (!pages || !host || !offsets || !sizes || !bounds || !total || !fits_u32(n) || n == 0)
-        return fail(ctx, CKV_ERR_ARGUMENT, "invalid pipeline store arguments");
-    if (ckv_status s = check_fixed(ctx, "pipeline store")) return s;
     *total = 0;
-    if (count == 0) return pipe_issue(p, static_cast<cudaStream_t>(stream_ptr), ticket);
-    DeviceGuard guard(ctx->device);
-    if (ckv_status st = pipe_staging(p, worst_page(n))) return st;
-    cudaStream_t caller = static_cast<cudaStream_t>(stream_ptr);
+    if (count == 0) return pipe_issue(p, caller, ticket);
+    if (ckv_status st = pipe_staging(p, per_page * worst_page(max_n))) return st;
+    const size_t unit_cap = p->page_cap / per_page & ~size_t(15);
     cudaError_t e = cudaEventRecord(p->ev_in, caller);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_enc, p->ev_in, 0);
     if (e != cudaSuccess) return cuda_fail(ctx, "ordering the pipeline store", e);
@@ -1001,32 +1007,26 @@ ckv_status ckv_pipe_store_bf16(ckv_pipe* p, const void* const* pages, const floa
     for (size_t c0 = 0, c = 0; c0 < count; c0 += p->chunk, ++c) {
         const int k = static_cast<int>(c & 1);
         const size_t cnt = std::min(p->chunk, count - c0);
+        const size_t units = cnt * per_page, u0 = c0 * per_page;
         // the staging of chunk c - 2 has been copied out
         if (p->copied_used[k] && (e = cudaStreamWaitEvent(p->s_enc, p->ev_copied[k], 0)))
             return cuda_fail(ctx, "ordering the pipeline store", e);
         Batch b;
-        b.maps.push_back(identity_map());
-        b.max_n = static_cast<uint32_t>(n);
-        p->srcs.resize(cnt);
-        for (size_t i = 0; i < cnt; ++i) {
-            const void* page = pages[c0 + i];
-            if (!page || (reinterpret_cast<uintptr_t>(page) & 1u))
-                return fail(ctx, CKV_ERR_ARGUMENT, "invalid page %zu", c0 + i);
-            Unit u{};
-            u.elems = page;
-            u.stream = p->enc[k] + i * p->page_cap;
-            u.capacity = p->page_cap;
-            u.n = static_cast<uint32_t>(n);
-            u.eb = eps_of(ctx, eps, c0 + i);
-            b.units.push_back(u);
-            p->srcs[i] = u.stream;
-        }
+        b.maps = maps;
+        b.max_n = max_n;
+        p->srcs.resize(units);
+        for (size_t i = 0; i < cnt; ++i)
+            for (size_t g = 0; g < per_page; ++g) {
+                uint8_t* stream = p->enc[k] + (i * per_page + g) * unit_cap;
+                if (ckv_status st = add(b, c0 + i, g, stream, unit_cap)) return st;
+                p->srcs[i * per_page + g] = stream;
+            }
         // compress (returns once the sizes are on the host), then pack
-        if (ckv_status st = run_encode(ctx, b, ckv::ElemType::kBF16, sizes + c0, bounds + c0, p->s_enc))
+        if (ckv_status st = run_encode(ctx, b, ckv::ElemType::kBF16, sizes + u0, bounds + u0, p->s_enc))
             return st;
-        p->local.resize(cnt);
+        p->local.resize(units);
         size_t ctotal = 0;
-        if (ckv_status st = ckv_pack(ctx, p->srcs.data(), sizes + c0, cnt, p->packed[k],
+        if (ckv_status st = ckv_pack(ctx, p->srcs.data(), sizes + u0, units, p->packed[k],
                                      p->page_cap * p->chunk, 16, p->local.data(), &ctotal, p->s_enc))
             return st;
         if (pos + ctotal > capacity)
@@ -1038,35 +1038,32 @@ ckv_status ckv_pipe_store_bf16(ckv_pipe* p, const void* const* pages, const floa
         if (e == cudaSuccess) e = cudaEventRecord(p->ev_copied[k], p->s_d2h);
         if (e != cudaSuccess) return cuda_fail(ctx, "pipeline store copy", e);
         p->copied_used[k] = true;
-        for (size_t i = 0; i < cnt; ++i) offsets[c0 + i] = pos + p->local[i];
+        for (size_t i = 0; i < units; ++i) offsets[u0 + i] = pos + p->local[i];
         pos = align16(pos + ctotal);
     }
     *total = pos;
     return pipe_issue(p, p->s_d2h, ticket);
 }
 
-ckv_status ckv_pipe_restore_bf16(ckv_pipe* p, const uint8_t* host, const size_t* offsets,
-                                 const size_t* sizes, const float* bounds, size_t count, size_t n,
-                                 void* const* dst, uint64_t after, uint64_t* ticket,
-                                 void* stream_ptr) {
-    if (!p) return CKV_ERR_ARGUMENT;
+// The fixed-mode restore of `count` pages stored by pipe_store_units: each
+// chunk's span of the host buffer is copied into a landing buffer and its
+// units decoded into the pages; `add(b, i, g, stream, size)` appends unit g
+// of page i (its bytes at `stream`) to the decode batch.
+template <typename Add>
+ckv_status pipe_restore_units(ckv_pipe* p, const uint8_t* host, const size_t* offsets,
+                              const size_t* sizes, size_t count, size_t per_page,
+                              const std::vector<Map>& maps, uint32_t max_n, uint64_t after,
+                              uint64_t* ticket, cudaStream_t caller, Add add) {
     ckv_ctx* ctx = p->ctx;
-    ctx->err.clear();
-    if (!host || !offsets || !sizes || !bounds || !dst || !fits_u32(n) || n == 0)
-        return fail(ctx, CKV_ERR_ARGUMENT, "invalid pipeline restore arguments");
-    if (ckv_status s = check_fixed(ctx, "pipeline restore")) return s;
-    cudaStream_t caller = static_cast<cudaStream_t>(stream_ptr);
     if (count == 0) return pipe_issue(p, caller, ticket);
-    DeviceGuard guard(ctx->device);
-    // each chunk's pages are copied as one span of the host buffer
+    // each chunk's units are copied as one span of the host buffer
     size_t span_max = 0;
     for (size_t c0 = 0; c0 < count; c0 += p->chunk) {
-        const size_t cnt = std::min(p->chunk, count - c0);
+        const size_t units = std::min(p->chunk, count - c0) * per_page, u0 = c0 * per_page;
         size_t lo = SIZE_MAX, hi = 0;
-        for (size_t i = c0; i < c0 + cnt; ++i) {
-            if (sizes[i] == 0 || (offsets[i] & 3u) || !dst[i] ||
-                (reinterpret_cast<uintptr_t>(dst[i]) & 1u))
-                return fail(ctx, CKV_ERR_ARGUMENT, "invalid restored page %zu", i);
+        for (size_t i = u0; i < u0 + units; ++i) {
+            if (sizes[i] == 0 || (offsets[i] & 3u))
+                return fail(ctx, CKV_ERR_ARGUMENT, "invalid stored unit %zu", i);
             lo = std::min(lo, offsets[i]);
             hi = std::max(hi, offsets[i] + sizes[i]);
         }
@@ -1080,8 +1077,9 @@ ckv_status ckv_pipe_restore_bf16(ckv_pipe* p, const uint8_t* host, const size_t*
     for (size_t c0 = 0, c = 0; c0 < count; c0 += p->chunk, ++c) {
         const int k = static_cast<int>(c & 1);
         const size_t cnt = std::min(p->chunk, count - c0);
+        const size_t units = cnt * per_page, u0 = c0 * per_page;
         size_t lo = SIZE_MAX, hi = 0;
-        for (size_t i = c0; i < c0 + cnt; ++i) {
+        for (size_t i = u0; i < u0 + units; ++i) {
             lo = std::min(lo, offsets[i]);
             hi = std::max(hi, offsets[i] + sizes[i]);
         }
@@ -1094,17 +1092,14 @@ ckv_status ckv_pipe_restore_bf16(ckv_pipe* p, const uint8_t* host, const size_t*
         if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_dec, p->ev_landed[k], 0);
         if (e != cudaSuccess) return cuda_fail(ctx, "pipeline restore copy", e);
         Batch b;
-        b.maps.push_back(identity_map());
-        b.max_n = static_cast<uint32_t>(n);
-        for (size_t i = c0; i < c0 + cnt; ++i) {
-            Unit u{};
-            u.elems = dst[i];
-            u.stream = p->land[k] + (offsets[i] - lo);
-            u.capacity = sizes[i];
-            u.n = static_cast<uint32_t>(n);
-            u.eb = bounds[i];
-            b.units.push_back(u);
-        }
+        b.maps = maps;
+        b.max_n = max_n;
+        for (size_t i = 0; i < cnt; ++i)
+            for (size_t g = 0; g < per_page; ++g) {
+                const size_t j = (c0 + i) * per_page + g;
+                if (ckv_status st = add(b, c0 + i, g, p->land[k] + (offsets[j] - lo), sizes[j]))
+                    return st;
+            }
         if (ckv_status st = run_decode(ctx, b, ckv::ElemType::kBF16, p->s_dec)) return st;
         if ((e = cudaEventRecord(p->ev_decoded[k], p->s_dec)))
             return cuda_fail(ctx, "pipeline restore", e);
@@ -1117,6 +1112,170 @@ ckv_status ckv_pipe_restore_bf16(ckv_pipe* p, const uint8_t* host, const size_t*
     if (e != cudaSuccess) return cuda_fail(ctx, "joining the pipeline restore", e);
     if (ticket) *ticket = t;
     return CKV_OK;
+}
+
+// Checks a layer-group description; the largest group's element count.
+ckv_status check_groups(ckv_ctx* ctx, const int64_t* const* layer_indices, const size_t* selected,
+                        size_t groups, size_t prefix_count, size_t source_layers,
+                        size_t elements_per_layer, std::vector<Map>& maps, uint32_t* max_n) {
+    if (groups == 0 || !layer_indices || !selected || prefix_count == 0 || source_layers == 0 ||
+        elements_per_layer == 0)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid layer groups");
+    maps.clear();
+    *max_n = 0;
+    for (size_t g = 0; g < groups; ++g) {
+        if (!layer_indices[g] || selected[g] == 0 || selected[g] > source_layers)
+            return fail(ctx, CKV_ERR_ARGUMENT, "invalid layer group %zu", g);
+        const size_t n = prefix_count * selected[g] * elements_per_layer;
+        if (!fits_u32(n)) return fail(ctx, CKV_ERR_ARGUMENT, "layer group %zu too large", g);
+        maps.push_back(layers_map(layer_indices[g], selected[g], source_layers, elements_per_layer));
+        *max_n = std::max<uint32_t>(*max_n, static_cast<uint32_t>(n));
+    }
+    return CKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+ckv_status ckv_pipe_store_bf16(ckv_pipe* p, const void* const* pages, const float* eps,
+                               size_t count, size_t n, uint8_t* host, size_t capacity,
+                               size_t* offsets, size_t* sizes, float* bounds, size_t* total,
+                               uint64_t after, uint64_t* ticket, void* stream_ptr) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    ckv_ctx* ctx = p->ctx;
+    ctx->err.clear();
+    if (!pages || !host || !offsets || !sizes || !bounds || !total || !fits_u32(n) || n == 0)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid pipeline store arguments");
+    if (ckv_status s = check_fixed(ctx, "pipeline store")) return s;
+    DeviceGuard guard(ctx->device);
+    auto add = [&](Batch& b, size_t i, size_t, uint8_t* stream, size_t cap) -> ckv_status {
+        const void* page = pages[i];
+        if (!page || (reinterpret_cast<uintptr_t>(page) & 1u))
+            return fail(ctx, CKV_ERR_ARGUMENT, "invalid page %zu", i);
+        Unit u{};
+        u.elems = page;
+        u.stream = stream;
+        u.capacity = cap;
+        u.n = static_cast<uint32_t>(n);
+        u.eb = eps_of(ctx, eps, i);
+        b.units.push_back(u);
+        return CKV_OK;
+    };
+    return pipe_store_units(p, count, 1, {identity_map()}, static_cast<uint32_t>(n), host,
+                            capacity, offsets, sizes, bounds, total, after, ticket,
+                            static_cast<cudaStream_t>(stream_ptr), add);
+}
+
+ckv_status ckv_pipe_restore_bf16(ckv_pipe* p, const uint8_t* host, const size_t* offsets,
+                                 const size_t* sizes, const float* bounds, size_t count, size_t n,
+                                 void* const* dst, uint64_t after, uint64_t* ticket,
+                                 void* stream_ptr) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    ckv_ctx* ctx = p->ctx;
+    ctx->err.clear();
+    if (!host || !offsets || !sizes || !bounds || !dst || !fits_u32(n) || n == 0)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid pipeline restore arguments");
+    if (ckv_status s = check_fixed(ctx, "pipeline restore")) return s;
+    DeviceGuard guard(ctx->device);
+    for (size_t i = 0; i < count; ++i)
+        if (!dst[i] || (reinterpret_cast<uintptr_t>(dst[i]) & 1u))
+            return fail(ctx, CKV_ERR_ARGUMENT, "invalid restored page %zu", i);
+    auto add = [&](Batch& b, size_t i, size_t, uint8_t* stream, size_t size) -> ckv_status {
+        Unit u{};
+        u.elems = dst[i];
+        u.stream = stream;
+        u.capacity = size;
+        u.n = static_cast<uint32_t>(n);
+        u.eb = bounds[i];
+        b.units.push_back(u);
+        return CKV_OK;
+    };
+    return pipe_restore_units(p, host, offsets, sizes, count, 1, {identity_map()},
+                              static_cast<uint32_t>(n), after, ticket,
+                              static_cast<cudaStream_t>(stream_ptr), add);
+}
+
+ckv_status ckv_pipe_store_bf16_groups(ckv_pipe* p, const void* const* pages, size_t count,
+                                      const int64_t* const* layer_indices, const size_t* selected,
+                                      size_t groups, size_t prefix_count, size_t source_layers,
+                                      size_t elements_per_layer, const float* eps, uint8_t* host,
+                                      size_t capacity, size_t* offsets, size_t* sizes,
+                                      float* bounds, size_t* total, uint64_t after,
+                                      uint64_t* ticket, void* stream_ptr) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    ckv_ctx* ctx = p->ctx;
+    ctx->err.clear();
+    if (!pages || !host || !offsets || !sizes || !bounds || !total)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid grouped store arguments");
+    if (ckv_status s = check_fixed(ctx, "grouped store")) return s;
+    std::vector<Map> maps;
+    uint32_t max_n = 0;
+    if (ckv_status s = check_groups(ctx, layer_indices, selected, groups, prefix_count,
+                                    source_layers, elements_per_layer, maps, &max_n))
+        return s;
+    DeviceGuard guard(ctx->device);
+    auto add = [&](Batch& b, size_t i, size_t g, uint8_t* stream, size_t cap) -> ckv_status {
+        const void* page = pages[i];
+        if (!page || (reinterpret_cast<uintptr_t>(page) & 1u))
+            return fail(ctx, CKV_ERR_ARGUMENT, "invalid page %zu", i);
+        Unit u{};
+        u.elems = page;
+        u.stream = stream;
+        u.capacity = cap;
+        u.n = static_cast<uint32_t>(prefix_count * selected[g] * elements_per_layer);
+        u.map = static_cast<uint32_t>(g);
+        u.eb = eps_of(ctx, eps, g);
+        b.units.push_back(u);
+        return CKV_OK;
+    };
+    return pipe_store_units(p, count, groups, maps, max_n, host, capacity, offsets, sizes, bounds,
+                            total, after, ticket, static_cast<cudaStream_t>(stream_ptr), add);
+}
+
+ckv_status ckv_pipe_restore_bf16_groups(ckv_pipe* p, const uint8_t* host, const size_t* offsets,
+                                        const size_t* sizes, const float* bounds, size_t count,
+                                        const int64_t* const* layer_indices,
+                                        const size_t* selected, size_t groups,
+                                        size_t prefix_count, size_t source_layers,
+                                        size_t elements_per_layer, void* const* pages,
+                                        uint64_t after, uint64_t* ticket, void* stream_ptr) {
+    if (!p) return CKV_ERR_ARGUMENT;
+    ckv_ctx* ctx = p->ctx;
+    ctx->err.clear();
+    if (!host || !offsets || !sizes || !bounds || !pages)
+        return fail(ctx, CKV_ERR_ARGUMENT, "invalid grouped restore arguments");
+    if (ckv_status s = check_fixed(ctx, "grouped restore")) return s;
+    std::vector<Map> maps;
+    uint32_t max_n = 0;
+    if (ckv_status s = check_groups(ctx, layer_indices, selected, groups, prefix_count,
+                                    source_layers, elements_per_layer, maps, &max_n))
+        return s;
+    DeviceGuard guard(ctx->device);
+    for (size_t i = 0; i < count; ++i)
+        if (!pages[i] || (reinterpret_cast<uintptr_t>(pages[i]) & 1u))
+            return fail(ctx, CKV_ERR_ARGUMENT, "invalid restored page %zu", i);
+    auto add = [&](Batch& b, size_t i, size_t g, uint8_t* stream, size_t size) -> ckv_status {
+        Unit u{};
+        u.elems = pages[i];
+        u.stream = stream;
+        u.capacity = size;
+        u.n = static_cast<uint32_t>(prefix_count * selected[g] * elements_per_layer);
+        u.map = static_cast<uint32_t>(g);
+        u.eb = bounds[i * groups + g];
+        b.units.push_back(u);
+        return CKV_OK;
+    };
+    return pipe_restore_units(p, host, offsets, sizes, count, groups, maps, max_n, after, ticket,
+                              static_cast<cudaStream_t>(stream_ptr), add);
+}
+
+size_t ckv_pipe_host_capacity_groups(size_t count, const size_t* selected, size_t groups,
+                                     size_t prefix_count, size_t elements_per_layer) {
+    size_t per_page = 0;
+    for (size_t g = 0; g < groups; ++g)
+        per_page += worst_page(prefix_count * selected[g] * elements_per_layer) + 16;
+    return count * per_page;
 }
 
 }  // extern "C"

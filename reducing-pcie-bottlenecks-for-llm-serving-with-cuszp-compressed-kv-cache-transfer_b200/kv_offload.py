@@ -97,33 +97,58 @@ class JobHeader:
 
     Layout (little-endian): magic b"CKVJ", u16 version, u16 element type
     (0 BF16), u32 page count, u64 elements per page, u64 payload bytes, f32
-    requested bound, u32 flags (bit 0: relative bound), then per page u64
-    offset (from the payload start), u64 size, f32 absolute bound, u32 zero;
-    the payload starts at the next 256-byte boundary.
+    requested bound, u32 flags (bit 0: relative bound), u32 segments per
+    page (G), u32 layer prefix count, u32 source layers (L; 0 when G = 1).
+    When G > 1 a layer table follows: L u8 segment indices (the segment that
+    holds each layer, padded to 4 bytes) and G f32 requested bounds.  Then
+    per page and segment (entry i*G + g) u64 offset (from the payload
+    start), u64 size, f32 absolute bound, u32 zero; the payload starts at
+    the next 256-byte boundary.  A segment of G > 1 holds the page's layers
+    of that segment, in ascending layer order, as
+    compress_batch_fixed_bf16_indexed encodes them.
     """
 
     MAGIC = b"CKVJ"
-    VERSION = 1
-    _HEAD = struct.Struct("<4sHHIQQfI")
+    VERSION = 2
+    _HEAD = struct.Struct("<4sHHIQQfIIII")
     _PAGE = np.dtype([("offset", "<u8"), ("size", "<u8"), ("bound", "<f4"), ("zero", "<u4")])
 
+    @staticmethod
+    def _layer_table_bytes(segments: int, layers: int) -> int:
+        return 0 if segments <= 1 else (layers + 3) // 4 * 4 + 4 * segments
+
     @classmethod
-    def bytes_for(cls, count: int) -> int:
-        return (cls._HEAD.size + count * cls._PAGE.itemsize + 255) // 256 * 256
+    def bytes_for(cls, count: int, segments: int = 1, layers: int = 0) -> int:
+        return (cls._HEAD.size + cls._layer_table_bytes(segments, layers) +
+                count * segments * cls._PAGE.itemsize + 255) // 256 * 256
 
     @classmethod
     def write(cls, slab: torch.Tensor, n: int, eps: float, relative: bool, offsets, sizes,
-              bounds, payload_bytes: int) -> None:
-        count = len(offsets)
-        buf = slab[: cls.bytes_for(count)].numpy()
+              bounds, payload_bytes: int, groups=None, prefix: int = 0,
+              layers: int = 0) -> None:
+        """`groups`: None for whole pages, else [(requested bound, layer
+        indices)] per segment, the pages viewed as [prefix, layers, n /
+        (prefix * layers)]."""
+        segs = 1 if not groups else len(groups)
+        count = len(offsets) // segs
+        buf = slab[: cls.bytes_for(count, segs, layers)].numpy()
         buf[: cls._HEAD.size] = np.frombuffer(
             cls._HEAD.pack(cls.MAGIC, cls.VERSION, 0, count, n, payload_bytes, eps,
-                           1 if relative else 0), dtype=np.uint8)
-        table = np.zeros(count, dtype=cls._PAGE)
+                           1 if relative else 0, segs, prefix if segs > 1 else 0,
+                           layers if segs > 1 else 0), dtype=np.uint8)
+        start = cls._HEAD.size
+        if segs > 1:
+            owner = np.zeros((layers + 3) // 4 * 4, dtype=np.uint8)
+            for g, (_b, sel) in enumerate(groups):
+                owner[list(sel)] = g
+            req = np.array([b for b, _sel in groups], dtype="<f4")
+            buf[start:start + owner.size] = owner
+            buf[start + owner.size:start + owner.size + req.nbytes] = req.view(np.uint8)
+            start += owner.size + req.nbytes
+        table = np.zeros(count * segs, dtype=cls._PAGE)
         table["offset"] = np.ctypeslib.as_array(offsets)
         table["size"] = np.ctypeslib.as_array(sizes)
         table["bound"] = np.ctypeslib.as_array(bounds)
-        start = cls._HEAD.size
         buf[start:start + table.nbytes] = table.view(np.uint8)
 
     @classmethod
@@ -132,17 +157,35 @@ class JobHeader:
         raw = slab[: cls._HEAD.size].numpy().tobytes()
         if len(raw) < cls._HEAD.size:
             raise ValueError("slab shorter than a job header")
-        magic, version, etype, count, n, payload, eps, flags = cls._HEAD.unpack(raw)
+        (magic, version, etype, count, n, payload, eps, flags, segs, prefix,
+         layers) = cls._HEAD.unpack(raw)
         if magic != cls.MAGIC or version != cls.VERSION or etype != 0:
             raise ValueError("not a compressed KV job (bad magic, version or element type)")
-        hdr = cls.bytes_for(count)
+        if segs == 0 or (segs > 1 and (prefix == 0 or layers < segs or
+                                       n % (prefix * layers))):
+            raise ValueError("bad segment description")
+        hdr = cls.bytes_for(count, segs, layers)
         if slab.numel() < hdr + payload:
             raise ValueError("slab shorter than its header says")
-        table = np.frombuffer(slab[cls._HEAD.size:cls._HEAD.size + count * cls._PAGE.itemsize]
+        start = cls._HEAD.size
+        groups = None
+        if segs > 1:
+            owner = slab[start:start + layers].numpy().copy()
+            start += (layers + 3) // 4 * 4
+            req = np.frombuffer(slab[start:start + 4 * segs].numpy().tobytes(), dtype="<f4")
+            start += 4 * segs
+            if np.any(owner >= segs):
+                raise ValueError("layer table names a missing segment")
+            groups = [(float(req[g]), tuple(int(x) for x in np.flatnonzero(owner == g)))
+                      for g in range(segs)]
+            if any(not sel for _b, sel in groups):
+                raise ValueError("empty segment in the layer table")
+        table = np.frombuffer(slab[start:start + count * segs * cls._PAGE.itemsize]
                               .numpy().tobytes(), dtype=cls._PAGE)
         if np.any(table["offset"] + table["size"] > payload) or np.any(table["size"] == 0):
             raise ValueError("page table points outside the payload")
         return {"count": count, "n": n, "eps": eps, "relative": bool(flags & 1),
+                "segments": segs, "prefix": prefix, "layers": layers, "groups": groups,
                 "payload_at": hdr, "payload_bytes": payload,
                 "offsets": table["offset"].astype(np.uint64),
                 "sizes": table["size"].astype(np.uint64),
@@ -165,9 +208,9 @@ class _Slab:
 @dataclass
 class _PageRecord:
     slab: int
-    offset: int                      # from the slab's payload start
-    size: int
-    bound: float
+    offsets: tuple[int, ...]         # per segment, from the slab's payload start
+    sizes: tuple[int, ...]
+    bounds: tuple[float, ...]
     n: int
 
 
@@ -266,10 +309,18 @@ def _block_ids(spec: Any) -> np.ndarray:
 
 
 class _Engine:
-    """One libckv context and pipeline per KV cache, shared by both handlers."""
+    """One libckv context and pipeline per KV cache, shared by both handlers.
+
+    With `layer_bounds` (layer -> requested bound, the reference's
+    ``active_bounds`` of ``_compress_adaptive_fixed_bundles_indexed``,
+    vllm_v1_compressed_offload.py:1286-1569) a page is viewed as
+    ``[layer_prefix, len(layer_bounds), n / (layer_prefix * layers)]`` and
+    stored as one segment per distinct bound, in ascending bound order (the
+    reference's ``sorted(grouped.items())``); layers missing from the mapping
+    take `error_bound`.  One distinct bound leaves whole pages."""
 
     def __init__(self, kv_cache: torch.Tensor, error_bound: float, device_id: int,
-                 chunk_pages: int):
+                 chunk_pages: int, layer_bounds=None, layer_prefix: int = 2):
         if kv_cache.dtype != torch.bfloat16 or not kv_cache.is_cuda or not kv_cache.is_contiguous():
             raise ValueError("kv_cache must be a contiguous BF16 CUDA tensor [num_blocks, ...]")
         self.lib = _ckv.load()
@@ -278,6 +329,7 @@ class _Engine:
         self.n = kv_cache[0].numel()
         self.page_bytes = self.n * 2
         self.error_bound = float(error_bound)
+        self._set_groups(layer_bounds, int(layer_prefix))
         self.ctx = C.c_void_p()
         cfg = _ckv.Config(self.error_bound, 1, _ckv.DIM_1D, _ckv.MODE_FIXED, _ckv.TYPE_FLOAT)
         self._check(self.lib.ckv_create(cfg, int(device_id), C.byref(self.ctx)), "ckv_create")
@@ -285,6 +337,41 @@ class _Engine:
         self._check(self.lib.ckv_pipe_create(self.ctx, int(chunk_pages), C.byref(self.pipe)),
                     "ckv_pipe_create")
         self.lock = threading.Lock()
+
+    def _set_groups(self, layer_bounds, prefix: int) -> None:
+        self.groups = None          # [(requested bound, layer indices)] per segment
+        self.segments = 1
+        self.prefix = self.layers = self.epl = 0
+        if layer_bounds is None:
+            return
+        if isinstance(layer_bounds, dict):
+            layers = len(layer_bounds)
+            bound_of = [float(layer_bounds.get(i, self.error_bound)) for i in range(layers)]
+        else:
+            bound_of = [float(b) for b in layer_bounds]
+            layers = len(bound_of)
+        if layers == 0 or prefix <= 0 or self.n % (prefix * layers):
+            raise ValueError("page does not split into [layer_prefix, layers, elements] rows")
+        grouped: dict[float, list[int]] = {}
+        for layer, bound in enumerate(bound_of):
+            grouped.setdefault(bound, []).append(layer)
+        if any(b <= 0 for b in grouped):
+            raise ValueError("layer bounds must be positive (raw layer segments are not stored)")
+        if len(grouped) == 1:
+            self.error_bound = next(iter(grouped))
+            return
+        self.groups = [(b, tuple(sel)) for b, sel in sorted(grouped.items())]
+        self.segments = len(self.groups)
+        self.prefix, self.layers, self.epl = prefix, layers, self.n // (prefix * layers)
+        self._index = [torch.tensor(sel, dtype=torch.int64, device=self.device)
+                       for _b, sel in self.groups]
+        G = self.segments
+        self.sel = (C.c_size_t * G)(*[len(sel) for _b, sel in self.groups])
+        self.idx = (C.c_void_p * G)(*[t.data_ptr() for t in self._index])
+        self.eps = (C.c_float * G)(*[b for b, _sel in self.groups])
+
+    def segment_numel(self, g: int) -> int:
+        return self.n if self.groups is None else self.prefix * len(self.groups[g][1]) * self.epl
 
     def _check(self, status: int, what: str) -> None:
         if status != 0:
@@ -295,6 +382,36 @@ class _Engine:
             raise IndexError("GPU block id out of range")
         addrs = np.uint64(self.kv.data_ptr()) + block_ids.astype(np.uint64) * np.uint64(self.page_bytes)
         return (C.c_void_p * len(addrs)).from_buffer_copy(addrs.astype(np.uint64).tobytes())
+
+    def host_capacity(self, count: int) -> int:
+        if self.groups is None:
+            return int(self.lib.ckv_pipe_host_capacity(count, self.n))
+        return int(self.lib.ckv_pipe_host_capacity_groups(count, self.sel, self.segments,
+                                                          self.prefix, self.epl))
+
+    def store(self, pages: C.Array, count: int, eps: float, host: int, cap: int, offsets,
+              sizes, bounds, total, after: int, ticket, stream: int) -> None:
+        if self.groups is None:
+            self._check(self.lib.ckv_pipe_store_bf16(
+                self.pipe, pages, (C.c_float * count)(*([eps] * count)), count, self.n, host,
+                cap, offsets, sizes, bounds, total, after, ticket, stream), "store")
+        else:
+            self._check(self.lib.ckv_pipe_store_bf16_groups(
+                self.pipe, pages, count, self.idx, self.sel, self.segments, self.prefix,
+                self.layers, self.epl, self.eps, host, cap, offsets, sizes, bounds, total,
+                after, ticket, stream), "store")
+
+    def restore(self, host: int, offsets, sizes, bounds, count: int, pages: C.Array,
+                after: int, ticket, stream: int) -> None:
+        if self.groups is None:
+            self._check(self.lib.ckv_pipe_restore_bf16(
+                self.pipe, host, offsets, sizes, bounds, count, self.n, pages, after, ticket,
+                stream), "restore")
+        else:
+            self._check(self.lib.ckv_pipe_restore_bf16_groups(
+                self.pipe, host, offsets, sizes, bounds, count, self.idx, self.sel,
+                self.segments, self.prefix, self.layers, self.epl, pages, after, ticket,
+                stream), "restore")
 
     def close(self) -> None:
         if self.pipe:
@@ -321,43 +438,60 @@ class CompressedOffloadingHandler:
         self._finished: list[TransferResult] = []
         self._lock = threading.Lock()
 
+    def _components(self, g: int) -> tuple[BundleComponent, ...]:
+        e = self.engine
+        if e.groups is None:
+            return (BundleComponent(0, tuple(e.kv.shape[1:]), torch.bfloat16, e.n),)
+        sel = e.groups[g][1]
+        return (BundleComponent(0, (e.prefix, len(sel), e.epl), torch.bfloat16,
+                                e.segment_numel(g), layer_axis=1, layer_indices=sel,
+                                destination_view_shape=(e.prefix, e.layers, e.epl)),)
+
     # -- one job
     def _store(self, gpu_ids: np.ndarray, cpu_ids: np.ndarray) -> tuple[list[int], int]:
         e = self.engine
-        count = len(gpu_ids)
-        hdr = JobHeader.bytes_for(count)
-        cap = int(e.lib.ckv_pipe_host_capacity(count, e.n))
+        count, G = len(gpu_ids), e.segments
+        hdr = JobHeader.bytes_for(count, G, e.layers)
+        cap = e.host_capacity(count)
         sid = self.store._take_slab(hdr + cap, hdr,
                                     lambda t: e._check(e.lib.ckv_pipe_wait(e.pipe, t), "wait"))
         slab = self.store.slab(sid)
-        offsets = (C.c_size_t * count)()
-        sizes = (C.c_size_t * count)()
-        bounds = (C.c_float * count)()
+        offsets = (C.c_size_t * (count * G))()
+        sizes = (C.c_size_t * (count * G))()
+        bounds = (C.c_float * (count * G))()
         total = C.c_size_t(0)
         ticket = C.c_uint64(0)
-        eps = (C.c_float * count)(*([self.error_bound] * count))
         stream = torch.cuda.current_stream(e.device).cuda_stream
-        e._check(e.lib.ckv_pipe_store_bf16(
-            e.pipe, e.page_ptrs(gpu_ids), eps, count, e.n, slab.buffer.data_ptr() + hdr, cap,
-            offsets, sizes, bounds, C.byref(total), slab.readers, C.byref(ticket), stream),
-            "store")
+        e.store(e.page_ptrs(gpu_ids), count, self.error_bound, slab.buffer.data_ptr() + hdr, cap,
+                offsets, sizes, bounds, C.byref(total), slab.readers, C.byref(ticket), stream)
         slab.ticket = ticket.value
         JobHeader.write(slab.buffer, e.n, self.error_bound, True, offsets, sizes, bounds,
-                        total.value)
+                        total.value, e.groups, e.prefix, e.layers)
+        comps = [self._components(g) for g in range(G)]
+        req = [self.error_bound] if e.groups is None else [b for b, _sel in e.groups]
         entries = []
         for i in range(count):
-            rec = _PageRecord(sid, int(offsets[i]), int(sizes[i]), float(bounds[i]), e.n)
-            payload = slab.buffer[hdr + rec.offset: hdr + rec.offset + rec.size]
-            comp = BundleComponent(0, tuple(e.kv.shape[1:]), torch.bfloat16, e.n)
-            seg = EncodedSegment(payload, rec.size, rec.bound, "cuszp", (comp,), e.n, e.n,
-                                 e.page_bytes, self.error_bound, cuszp_mode="fixed")
-            entries.append((int(cpu_ids[i]), rec, CompressedBundle((seg,), rec.size, e.page_bytes)))
+            span = range(i * G, i * G + G)
+            rec = _PageRecord(sid, tuple(int(offsets[j]) for j in span),
+                              tuple(int(sizes[j]) for j in span),
+                              tuple(float(bounds[j]) for j in span), e.n)
+            segs = []
+            for g in range(G):
+                numel = e.segment_numel(g)
+                payload = slab.buffer[hdr + rec.offsets[g]: hdr + rec.offsets[g] + rec.sizes[g]]
+                segs.append(EncodedSegment(payload, rec.sizes[g], rec.bounds[g], "cuszp",
+                                           comps[g], numel, numel, numel * 2, req[g],
+                                           cuszp_mode="fixed"))
+            entries.append((int(cpu_ids[i]),
+                            rec, CompressedBundle(tuple(segs), sum(rec.sizes), e.page_bytes)))
         self.store.put_many_packed(entries)
         return [ticket.value], int(total.value)
 
     def _load(self, cpu_ids: np.ndarray, gpu_ids: np.ndarray) -> tuple[list[int], int]:
         e = self.engine
         recs = [self.store.record(int(c)) for c in cpu_ids]
+        if any(len(r.sizes) != e.segments or r.n != e.n for r in recs):
+            raise ValueError("stored page does not match the KV cache layout")
         by_slab: dict[int, list[int]] = {}
         for i, r in enumerate(recs):
             by_slab.setdefault(r.slab, []).append(i)
@@ -366,15 +500,13 @@ class CompressedOffloadingHandler:
         for sid, idx in by_slab.items():
             slab = self.store.slab(sid)
             count = len(idx)
-            offsets = (C.c_size_t * count)(*[recs[i].offset for i in idx])
-            sizes = (C.c_size_t * count)(*[recs[i].size for i in idx])
-            bounds = (C.c_float * count)(*[recs[i].bound for i in idx])
+            offsets = (C.c_size_t * (count * e.segments))(*[o for i in idx for o in recs[i].offsets])
+            sizes = (C.c_size_t * (count * e.segments))(*[z for i in idx for z in recs[i].sizes])
+            bounds = (C.c_float * (count * e.segments))(*[b for i in idx for b in recs[i].bounds])
             base = slab.buffer.data_ptr() + slab.payload_at
             ticket = C.c_uint64(0)
-            e._check(e.lib.ckv_pipe_restore_bf16(
-                e.pipe, base, offsets, sizes, bounds, count, e.n,
-                e.page_ptrs(gpu_ids[np.asarray(idx)]), slab.ticket, C.byref(ticket), stream),
-                "restore")
+            e.restore(base, offsets, sizes, bounds, count, e.page_ptrs(gpu_ids[np.asarray(idx)]),
+                      slab.ticket, C.byref(ticket), stream)
             slab.readers = ticket.value
             tickets.append(ticket.value)
             nbytes += sum(sizes)
@@ -428,11 +560,17 @@ class CompressedOffloadingHandler:
 
 
 class CompressedCpuGpuOffloadingHandlers:
-    """Both directions over one KV cache (vllm_v1_compressed_offload.py:2412-2470)."""
+    """Both directions over one KV cache (vllm_v1_compressed_offload.py:2412-2470).
+
+    `layer_bounds` / `layer_prefix`: a fixed per-layer bound assignment (the
+    reference's calibrated mixed profiles, e.g. 1e-5 on a few sensitive
+    layers and 1e-4 on the rest), stored as one segment per distinct bound
+    (see ``_Engine``)."""
 
     def __init__(self, kv_cache: torch.Tensor, error_bound: float = 1e-4, device_id: int = 0,
-                 chunk_pages: int = 64):
-        self.engine = _Engine(kv_cache, error_bound, device_id, chunk_pages)
+                 chunk_pages: int = 64, layer_bounds=None, layer_prefix: int = 2):
+        self.engine = _Engine(kv_cache, error_bound, device_id, chunk_pages, layer_bounds,
+                              layer_prefix)
         self.store = CompressedPageStore()
         self.gpu_to_cpu_handler = CompressedOffloadingHandler(self.engine, self.store, True)
         self.cpu_to_gpu_handler = CompressedOffloadingHandler(self.engine, self.store, False)
@@ -446,16 +584,22 @@ class CompressedCpuGpuOffloadingHandlers:
 def restore_job(slab: torch.Tensor, dst_pages: Sequence[torch.Tensor], engine: _Engine) -> int:
     """Restores every page of a job from its slab bytes alone (the header and
     page table), e.g. after the slab was written to a file and read back.
-    Returns the pipeline ticket."""
+    The job's segments must be the engine's.  Returns the pipeline ticket."""
     job = JobHeader.read(slab)
     if job["n"] != engine.n or len(dst_pages) != job["count"]:
         raise ValueError("job does not match the destination pages")
-    count = job["count"]
+    same = job["segments"] == engine.segments and (
+        engine.groups is None or
+        ([sel for _b, sel in job["groups"]] == [sel for _b, sel in engine.groups] and
+         job["prefix"] == engine.prefix and job["layers"] == engine.layers))
+    if not same:
+        raise ValueError("job segments do not match the engine's layer groups")
+    count, G = job["count"], job["segments"]
     ticket = C.c_uint64(0)
-    engine._check(engine.lib.ckv_pipe_restore_bf16(
-        engine.pipe, slab.data_ptr() + job["payload_at"],
-        (C.c_size_t * count)(*job["offsets"].tolist()), (C.c_size_t * count)(*job["sizes"].tolist()),
-        (C.c_float * count)(*job["bounds"].tolist()), count, engine.n,
-        _ckv.ptr_array([p.data_ptr() for p in dst_pages]), 0, C.byref(ticket),
-        torch.cuda.current_stream(engine.device).cuda_stream), "restore")
+    engine.restore(slab.data_ptr() + job["payload_at"],
+                   (C.c_size_t * (count * G))(*job["offsets"].tolist()),
+                   (C.c_size_t * (count * G))(*job["sizes"].tolist()),
+                   (C.c_float * (count * G))(*job["bounds"].tolist()), count,
+                   _ckv.ptr_array([p.data_ptr() for p in dst_pages]), 0, C.byref(ticket),
+                   torch.cuda.current_stream(engine.device).cuda_stream)
     return ticket.value

@@ -51,6 +51,51 @@ def test_job_header_rejects_bad_slabs():
         ko.JobHeader.read(slab)                       # page past the payload
 
 
+def test_job_header_layer_groups_round_trip():
+    count, layers, prefix = 3, 28, 2
+    low = (0, 1, 2, 5, 19, 20, 21)
+    high = tuple(i for i in range(layers) if i not in low)
+    groups = [(1e-5, low), (1e-4, high)]
+    offsets = (C.c_size_t * (2 * count))(0, 512, 4096, 4608, 8192, 8704)
+    sizes = (C.c_size_t * (2 * count))(500, 3000, 500, 3000, 500, 3000)
+    bounds = (C.c_float * (2 * count))(1e-5, 1e-4, 2e-5, 2e-4, 3e-5, 3e-4)
+    hdr = ko.JobHeader.bytes_for(count, 2, layers)
+    assert hdr % 256 == 0
+    slab = torch.zeros(hdr + 11704, dtype=torch.uint8)
+    ko.JobHeader.write(slab, prefix * layers * 4096, 1e-4, True, offsets, sizes, bounds, 11704,
+                       groups, prefix, layers)
+    job = ko.JobHeader.read(slab)
+    assert job["count"] == count and job["segments"] == 2 and job["payload_at"] == hdr
+    assert job["prefix"] == prefix and job["layers"] == layers
+    assert [sel for _b, sel in job["groups"]] == [low, high]
+    assert [np.float32(b) for b, _s in job["groups"]] == [np.float32(1e-5), np.float32(1e-4)]
+    assert job["sizes"].tolist() == list(sizes)
+    assert job["bounds"].tolist() == [np.float32(b) for b in bounds]
+    bad = slab.clone()
+    bad[ko.JobHeader._HEAD.size + 3] = 7          # layer 3 in a segment that does not exist
+    with pytest.raises(ValueError):
+        ko.JobHeader.read(bad)
+
+
+def test_layer_bounds_group_like_the_reference():
+    """Segments are the distinct bounds in ascending order, each with its
+    layers in ascending order; missing layers take the handler's bound."""
+    e = ko._Engine.__new__(ko._Engine)
+    e.n, e.error_bound, e.device = 2 * 28 * 4096, 1e-4, "cpu"
+    low = [0, 1, 2, 5, 19, 20, 21]
+    e._set_groups({i: 1e-5 for i in low} | {i: 1e-4 for i in range(28) if i not in low}, 2)
+    assert e.segments == 2 and e.epl == 4096 and e.layers == 28
+    assert e.groups[0] == (1e-5, tuple(low))
+    assert e.groups[1][1] == tuple(i for i in range(28) if i not in low)
+    assert list(e.sel) == [7, 21] and e.segment_numel(0) == 2 * 7 * 4096
+    e._set_groups([3e-4] * 28, 2)                 # one bound: whole pages
+    assert e.groups is None and e.segments == 1 and e.error_bound == 3e-4
+    with pytest.raises(ValueError):
+        e._set_groups([1e-4] * 27 + [0.0], 2)     # raw layers are not stored
+    with pytest.raises(ValueError):
+        e._set_groups([1e-4] * 27 + [1e-5], 3)    # page does not split
+
+
 def test_page_store_overwrite_evict_and_recycle():
     store = ko.CompressedPageStore(allocate=lambda n: torch.empty(n, dtype=torch.uint8))
     buffers = []
@@ -60,13 +105,13 @@ def test_page_store_overwrite_evict_and_recycle():
         buffers.append(store.slab(sid).buffer)
         entries = []
         for k, cpu in enumerate(pages):
-            rec = ko._PageRecord(sid, 64 * k, 64, 0.5, 32)
+            rec = ko._PageRecord(sid, (64 * k,), (64,), (0.5,), 32)
             entries.append((cpu, rec, ko.CompressedBundle((), 64, 64)))
         store.put_many_packed(entries)
         return sid
 
     slab_with([1, 2, 3])
-    assert len(store) == 3 and store.record(2).offset == 64
+    assert len(store) == 3 and store.record(2).offsets == (64,)
     s2 = slab_with([3, 4])             # block 3 moves to the new slab
     assert store.record(3).slab == s2 and len(store) == 4
     store.evict([1, 2])                # the first slab is unreferenced now
@@ -180,5 +225,76 @@ def test_handlers_overlapping_jobs_and_slab_reuse():
         got = {r.job_id for r in h.gpu_to_cpu_handler.get_finished()}
         got |= {r.job_id for r in h.cpu_to_gpu_handler.get_finished()}
         assert got == {1, 2, 3, 4, 5}
+    finally:
+        h.shutdown()
+
+
+@pytest.mark.gpu
+def test_handlers_layer_groups_match_plain_calls():
+    """The mixed per-layer profile (7 layers at 1e-5, 21 at 1e-4) through the
+    handlers: two segments per page equal compress_batch_fixed_bf16_indexed
+    per group; a load restores what decompress_batch_fixed_bf16_indexed_scatter
+    restores, and so does the job read back from its slab bytes."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    import cuszp_wrapper_cpp as cpp
+
+    shape = (2, 28, 2, 16, 128)
+    layers, prefix, epl = 28, 2, 2 * 16 * 128
+    low = [0, 1, 2, 5, 19, 20, 21]
+    high = [i for i in range(layers) if i not in low]
+    bounds_of = {i: (1e-5 if i in low else 1e-4) for i in range(layers)}
+    kv = _kv(24, shape, seed=13).cuda()
+    h = ko.CompressedCpuGpuOffloadingHandlers(kv, error_bound=1e-4, device_id=0, chunk_pages=4,
+                                              layer_bounds=bounds_of)
+    try:
+        gpu_ids = np.array([1, 4, 7, 8, 9, 15, 16, 23, 0], dtype=np.int64)
+        cpu_ids = np.arange(300, 300 + len(gpu_ids), dtype=np.int64)
+        assert h.gpu_to_cpu_handler.transfer_async(1, (gpu_ids, cpu_ids))
+        h.gpu_to_cpu_handler.wait({1})
+        assert [r.success for r in h.gpu_to_cpu_handler.get_finished()] == [True]
+
+        cfg = cpp.CompressionConfig(error_bound=1e-4, use_relative_error=True,
+                                    processing_dim=cpp.CuszpDim.DIM_1D,
+                                    encoding_mode=cpp.CuszpMode.MODE_FIXED,
+                                    data_type=cpp.CuszpType.TYPE_FLOAT)
+        w = cpp.CuSZpWrapper(cfg, 0)
+        pages = [kv[i].view(-1) for i in gpu_ids]
+        ref = {}
+        for g, (eb, sel) in enumerate([(1e-5, low), (1e-4, high)]):
+            index = torch.tensor(sel, device="cuda")
+            outs = [torch.empty(w.estimate_compressed_buffer_size(prefix * len(sel) * epl * 4),
+                                dtype=torch.uint8, device="cuda") for _ in pages]
+            ok, sizes, bounds = w.compress_batch_fixed_bf16_indexed(
+                pages, outs, index, prefix, layers, epl, [eb] * len(pages))
+            assert ok
+            ref[g] = (index, outs, sizes, bounds)
+            for k, cpu in enumerate(cpu_ids):
+                seg = h.store.get(int(cpu)).segments[g]
+                assert seg.components[0].layer_indices == tuple(sel)
+                assert seg.compressed_size == sizes[k]
+                assert np.float32(seg.actual_error_bound) == np.float32(bounds[k])
+                assert torch.equal(seg.payload, outs[k][: sizes[k]].cpu())
+
+        restored = torch.zeros(len(pages), kv[0].numel(), dtype=torch.bfloat16, device="cuda")
+        for g in range(2):
+            index, outs, sizes, bounds = ref[g]
+            assert w.decompress_batch_fixed_bf16_indexed_scatter(
+                outs, sizes, list(restored), index, prefix, layers, epl, bounds)
+        dst_gpu = np.array([2, 3, 5, 6, 10, 11, 12, 13, 14], dtype=np.int64)   # not sources
+        kv[torch.as_tensor(dst_gpu, device="cuda")] = 0
+        assert h.cpu_to_gpu_handler.transfer_async(2, (cpu_ids, dst_gpu))
+        h.cpu_to_gpu_handler.wait({2})
+        torch.cuda.synchronize()
+        for j in range(len(gpu_ids)):
+            assert torch.equal(kv[dst_gpu[j]].view(-1).view(torch.int16),
+                               restored[j].view(torch.int16))
+
+        slab = h.store.slab(h.store.record(int(cpu_ids[0])).slab).buffer
+        dst = [torch.zeros(kv[0].numel(), dtype=torch.bfloat16, device="cuda") for _ in pages]
+        t = ko.restore_job(slab, dst, h.engine)
+        assert h.engine.lib.ckv_pipe_wait(h.engine.pipe, t) == 0
+        for k in range(len(pages)):
+            assert torch.equal(dst[k].view(torch.int16), restored[k].view(torch.int16))
     finally:
         h.shutdown()

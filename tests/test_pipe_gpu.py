@@ -159,3 +159,76 @@ def test_pipe_rejects_small_host_buffer(env):
         torch.cuda.synchronize()
     finally:
         lib.ckv_pipe_destroy(pipe)
+
+
+def test_pipe_layer_groups_match_plain_calls(env):
+    """The C3 layout: pages of 28 layers, 21 at 1e-4 and 7 at 1e-5 (the
+    reference's calibrated profile), stored as two segments per page through
+    the pipeline; bytes and bounds equal compress_batch_fixed_bf16_indexed_groups,
+    the restore equals decompress_batch_fixed_bf16_indexed_scatter per group."""
+    import cuszp_wrapper_cpp as cpp
+
+    _ckv, lib, ctx = env
+    layers, prefix, epl, count, chunk = 28, 2, 4096, 9, 4
+    low = [0, 1, 2, 5, 19, 20, 21]
+    high = [i for i in range(layers) if i not in low]
+    pages = _pages(count, prefix * layers * epl, seed=31).cuda()
+    groups = [torch.tensor(high, device="cuda"), torch.tensor(low, device="cuda")]
+    eps = [1e-4, 1e-5]
+
+    cfg = cpp.CompressionConfig(error_bound=1e-5, use_relative_error=True,
+                                processing_dim=cpp.CuszpDim.DIM_1D,
+                                encoding_mode=cpp.CuszpMode.MODE_FIXED,
+                                data_type=cpp.CuszpType.TYPE_FLOAT)
+    w = cpp.CuSZpWrapper(cfg, 0)
+    caps = [int(w.estimate_compressed_buffer_size(prefix * len(g) * epl * 4)) for g in (high, low)]
+    outs = [torch.zeros(caps[0], dtype=torch.uint8, device="cuda") for _ in range(count)] + \
+           [torch.zeros(caps[1], dtype=torch.uint8, device="cuda") for _ in range(count)]
+    ok, ref_sizes, ref_bounds = w.compress_batch_fixed_bf16_indexed_groups(
+        [pages[i] for i in range(count)] * 2, outs, groups, [count, count], prefix, layers, epl,
+        [eps[0]] * count + [eps[1]] * count)
+    assert ok
+    ref_restored = torch.zeros_like(pages)
+    dests = [ref_restored[i] for i in range(count)]
+    assert w.decompress_batch_fixed_bf16_indexed_scatter(
+        outs[:count], ref_sizes[:count], dests, groups[0], prefix, layers, epl, ref_bounds[:count])
+    assert w.decompress_batch_fixed_bf16_indexed_scatter(
+        outs[count:], ref_sizes[count:], dests, groups[1], prefix, layers, epl, ref_bounds[count:])
+    torch.cuda.synchronize()
+
+    pipe = C.c_void_p()
+    assert lib.ckv_pipe_create(ctx, chunk, C.byref(pipe)) == 0
+    try:
+        G = len(groups)
+        sel = (C.c_size_t * G)(*[len(high), len(low)])
+        idx = (C.c_void_p * G)(*[g.data_ptr() for g in groups])
+        epsa = (C.c_float * G)(*eps)
+        cap = int(lib.ckv_pipe_host_capacity_groups(count, sel, G, prefix, epl))
+        host = torch.empty(cap, dtype=torch.uint8, pin_memory=True)
+        offsets = (C.c_size_t * (count * G))()
+        sizes = (C.c_size_t * (count * G))()
+        bounds = (C.c_float * (count * G))()
+        total = C.c_size_t(0)
+        t1, t2 = C.c_uint64(0), C.c_uint64(0)
+        s = torch.cuda.current_stream().cuda_stream
+        ptrs = _ckv.ptr_array([pages[i].data_ptr() for i in range(count)])
+        assert lib.ckv_pipe_store_bf16_groups(pipe, ptrs, count, idx, sel, G, prefix, layers, epl,
+                                              epsa, host.data_ptr(), cap, offsets, sizes, bounds,
+                                              C.byref(total), 0, C.byref(t1), s) == 0
+        assert lib.ckv_pipe_wait(pipe, t1.value) == 0
+        for i in range(count):
+            for g in range(G):
+                j, r = i * G + g, g * count + i
+                assert sizes[j] == ref_sizes[r]
+                assert C.c_float(bounds[j]).value == C.c_float(ref_bounds[r]).value
+                got = host[offsets[j]:offsets[j] + sizes[j]]
+                assert torch.equal(got, outs[r][:sizes[j]].cpu()), (i, g)
+        restored = torch.zeros_like(pages)
+        assert lib.ckv_pipe_restore_bf16_groups(
+            pipe, host.data_ptr(), offsets, sizes, bounds, count, idx, sel, G, prefix, layers, epl,
+            _ckv.ptr_array([restored[i].data_ptr() for i in range(count)]), t1.value,
+            C.byref(t2), s) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(restored.view(torch.int16), ref_restored.view(torch.int16))
+    finally:
+        lib.ckv_pipe_destroy(pipe)
