@@ -678,6 +678,111 @@ def pipeline_codecs(codec, steps: int, flush: torch.Tensor, device) -> dict:
     return out
 
 
+C3_LOW_LAYERS = (0, 1, 2, 5, 19, 20, 21)   # 1e-5; the other 21 layers at 1e-4
+
+
+def layer_groups_c3(codec, steps: int, flush: torch.Tensor, device, repeat: int = 8,
+                    chunk_pages: int = 0) -> dict:
+    """C3: the mixed per-layer profile (7 layers at 1e-5, 21 at 1e-4, the
+    reference's calibrated assignment) over 2048 pages, each page stored as
+    two layer segments (ckv_pipe_store_bf16_groups) while the previous
+    step's slab is restored into all 28 layers (ckv_pipe_restore_bf16_groups),
+    timed like the fixed-mode e2e.  The 2048 pages are the C2 pages repeated
+    `repeat` times on the device.  The restore is checked per element against
+    its segment's bound."""
+    lib, ck = codec.lib, codec.ckv
+    prefix, layers = 2, LAYERS
+    epl = codec.n // (prefix * layers)
+    high = tuple(i for i in range(layers) if i not in C3_LOW_LAYERS)
+    groups = [(1e-5, C3_LOW_LAYERS), (1e-4, high)]          # ascending bound
+    G = len(groups)
+    pages = codec.pages.repeat(repeat, 1)
+    count = pages.shape[0]
+    raw_bytes = count * codec.n * 2
+    index = [torch.tensor(sel, dtype=torch.int64, device=device) for _b, sel in groups]
+    idx = (C.c_void_p * G)(*[t.data_ptr() for t in index])
+    sel = (C.c_size_t * G)(*[len(s) for _b, s in groups])
+    eps = (C.c_float * G)(*[b for b, _s in groups])
+    pipe = C.c_void_p()
+    codec._check(lib.ckv_pipe_create(codec.ctx, chunk_pages or count, C.byref(pipe)), "c3 pipe")
+    try:
+        cap = int(lib.ckv_pipe_host_capacity_groups(count, sel, G, prefix, epl))
+        slabs = [torch.empty(cap, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        meta = [{"o": (C.c_size_t * (count * G))(), "s": (C.c_size_t * (count * G))(),
+                 "b": (C.c_float * (count * G))(), "t": C.c_size_t(0)} for _ in range(2)]
+        dst = torch.zeros_like(pages)
+        src_ptrs = ck.ptr_array([pages[i].data_ptr() for i in range(count)])
+        dptr = ck.ptr_array([dst[i].data_ptr() for i in range(count)])
+        side = torch.cuda.Stream(device)
+        state = {"k": 0, "ts": 0, "tr": 0}
+
+        def step():
+            k = state["k"]
+            state["k"] += 1
+            main = torch.cuda.current_stream(device)
+            a, b = meta[k % 2], meta[(k + 1) % 2]
+            prev_restore = state["tr"]
+            restored = 0
+            if k > 0:
+                side.wait_stream(main)
+                tr = C.c_uint64(0)
+                codec._check(lib.ckv_pipe_restore_bf16_groups(
+                    pipe, slabs[(k + 1) % 2].data_ptr(), b["o"], b["s"], b["b"], count, idx, sel,
+                    G, prefix, layers, epl, dptr, state["ts"], C.byref(tr), side.cuda_stream),
+                    "c3 restore")
+                state["tr"] = tr.value
+                restored = b["t"].value
+            ts = C.c_uint64(0)
+            codec._check(lib.ckv_pipe_store_bf16_groups(
+                pipe, src_ptrs, count, idx, sel, G, prefix, layers, epl, eps,
+                slabs[k % 2].data_ptr(), cap, a["o"], a["s"], a["b"], C.byref(a["t"]),
+                prev_restore, C.byref(ts), main.cuda_stream), "c3 store")
+            state["ts"] = ts.value
+            codec._check(lib.ckv_pipe_join(pipe, state["ts"], main.cuda_stream), "c3 join")
+            main.wait_stream(side)
+            return a["t"].value, restored
+
+        for _ in range(3):
+            step()
+        times, totals = timed_steps(step, steps, flush, device)
+        torch.cuda.synchronize(device)
+        kms = [codec.kernel_ms(0), codec.kernel_ms(1)]
+        # the last restore read the slab of the second-to-last store: check
+        # it against that store's per-segment bounds
+        last = meta[state["k"] % 2]
+        bnd = torch.tensor(list(last["b"]), device=device).view(count, G)
+        owner = torch.zeros(layers, dtype=torch.long)
+        owner[list(high)] = 1
+        per_layer = bnd[:, owner.to(device)].view(count, 1, layers, 1)
+        ok = True
+        for c0 in range(0, count, 256):
+            x = pages[c0:c0 + 256].float().view(-1, prefix, layers, epl)
+            xh = dst[c0:c0 + 256].float().view(-1, prefix, layers, epl)
+            ok &= bool(((x - xh).abs() <= per_layer[c0:c0 + 256] * 1.01 + 1e-7 +
+                        x.abs() * 2.0 ** -8).all())
+        stored = totals[-1][0]
+        t = sum(times) / 1e3
+        segment_ratio = [
+            round(count * prefix * len(s) * epl * 2 / max(1, sum(list(meta[0]["s"])[g::G])), 4)
+            for g, (_b, s) in enumerate(groups)]
+        return {
+            "workload": f"C3: {count} pages x {codec.n} BF16 (the C2 pages x{repeat}), "
+                        "7 layers at REL 1e-5 + 21 at REL 1e-4, two segments per page",
+            "e2e_gbps": round(job_rate(1, raw_bytes, steps, t), 3),
+            "ms_per_step": round(t * 1e3 / steps, 4),
+            "compression_ratio": round(raw_bytes / stored, 4),
+            "segment_ratios": {"1e-5": segment_ratio[0], "1e-4": segment_ratio[1]},
+            "d2h_bytes_per_step": int(stored), "h2d_bytes_per_step": int(totals[-1][1]),
+            "store_kernel_ms": round(kms[0], 4), "restore_kernel_ms": round(kms[1], 4),
+            "restore_ok": ok,
+            "path": "ckv_pipe_store_bf16_groups overlapped with ckv_pipe_restore_bf16_groups of "
+                    f"the previous step's slab, {chunk_pages or count} pages per chunk",
+        }
+    finally:
+        torch.cuda.synchronize(device)
+        lib.ckv_pipe_destroy(pipe)
+
+
 def raw_pcie(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -> float:
     """Raw pinned D2H + H2D of the uncompressed pages, one after the other (the
     PCIe reference point): seconds for `steps` steps of 2 x the pages' bytes."""
@@ -748,6 +853,8 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--pages", type=int, default=PAGES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c3", action="store_true",
+                    help="skip the C3 mixed per-layer profile leg")
     ap.add_argument("--chunk-pages", type=int, default=0,
                     help="pages per pipeline chunk (0: the whole job in one chunk)")
     args = ap.parse_args()
@@ -848,6 +955,9 @@ def main() -> int:
     ok = ok and codec.verify()
     piped = (pipeline_codecs(codec, min(args.steps, 10), flush, device)
              if impl == "ours" and pipelined and rank == 0 else None)
+    c3 = (layer_groups_c3(codec, min(args.steps, 10), flush, device,
+                          chunk_pages=args.chunk_pages)
+          if impl == "ours" and pipelined and rank == 0 and not args.no_c3 else None)
 
     e2e_match = codec.e2e_matches() if pipelined else None
     t_step, t_e2e, t_serial = slowest_rank(
@@ -940,6 +1050,7 @@ def main() -> int:
         }
         line["kernels"] = kernels
         line["pipeline_codecs"] = piped
+        line["layer_groups_c3"] = c3
         line["gpu_launches"] = launches_total
         line["gpu_launches_value_region"] = launches_value
     else:
