@@ -783,6 +783,127 @@ def layer_groups_c3(codec, steps: int, flush: torch.Tensor, device, repeat: int 
         lib.ckv_pipe_destroy(pipe)
 
 
+# BASELINE.json configs[3] (C4) and configs[4] (C5, one GPU's shard): jobs of 2048 pages.
+STREAMED = {
+    "C4": {"layers": 28, "heads": 4, "jobs": 16, "eps": 1e-5, "seed": 1000,
+           "what": "Qwen2.5-7B KV, 16 requests x 32k tokens (2048 pages each), REL 1e-5"},
+    "C5": {"layers": 80, "heads": 1, "jobs": 4, "eps": 1e-4, "seed": 2000,
+           "what": "Llama-3-70B KV at 128k tokens, TP=8 shard of one GPU (8192 pages), REL 1e-4"},
+}
+
+
+def make_job_pages(layers: int, heads: int, pages: int, seed: int, device) -> torch.Tensor:
+    """Seeded synthetic KV pages [pages, 2 * layers * heads * 16 * 128] BF16, generated on the
+    device (the C2 distributions: K = N(0,1) x LogNormal(0, 0.5) per (layer, head, channel) with 4
+    outlier channels x8, V = N(0, 0.5^2))."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    kscale = torch.empty(layers, heads, HEAD_DIM, device=device).log_normal_(0.0, 0.5, generator=g)
+    outliers = torch.randperm(HEAD_DIM, generator=g, device=device)[:4]
+    kscale[:, :, outliers] *= 8.0
+    out = torch.empty(pages, 2, layers, heads, TOKENS, HEAD_DIM, dtype=torch.bfloat16, device=device)
+    for p0 in range(0, pages, 256):
+        p1 = min(pages, p0 + 256)
+        k = torch.randn(p1 - p0, layers, heads, TOKENS, HEAD_DIM, generator=g, device=device)
+        out[p0:p1, 0] = (k * kscale[None, :, :, None, :]).to(torch.bfloat16)
+        v = torch.randn(p1 - p0, layers, heads, TOKENS, HEAD_DIM, generator=g, device=device)
+        out[p0:p1, 1] = (v * 0.5).to(torch.bfloat16)
+    return out.view(pages, -1)
+
+
+def streamed_jobs(codec, name: str, steps: int, flush: torch.Tensor, device,
+                  chunk_pages: int = 256, pages_per_job: int = 2048) -> dict:
+    """C4 / C5 through the pipeline: a step stores every job (2048 pages each) from its own KV
+    pages into one of two page-locked slabs on the caller's stream while the previous job is
+    restored on a second stream (background store, on-demand restore), so the link carries a
+    store and a restore at once.  Restores are checked per element against their page's bound."""
+    cfg = STREAMED[name]
+    lib, ck = codec.lib, codec.ckv
+    jobs = cfg["jobs"]
+    raw_job = pages_per_job * 2 * cfg["layers"] * cfg["heads"] * TOKENS * HEAD_DIM * 2
+    try:
+        avail = int(next(l for l in open("/proc/meminfo") if l.startswith("MemAvailable")).split()[1]) * 1024
+    except (OSError, StopIteration, ValueError):
+        avail = 0
+    if avail < 8 * raw_job:   # two page-locked slabs, with room to spare
+        return {"workload": name, "skipped": f"{avail / 1e9:.1f} GB host memory available"}
+    pages = [make_job_pages(cfg["layers"], cfg["heads"], pages_per_job, cfg["seed"] + r, device)
+             for r in range(jobs)]
+    n = pages[0].shape[1]
+    dst = [torch.zeros_like(p) for p in pages]
+    src_ptrs = [ck.ptr_array([p[i].data_ptr() for i in range(pages_per_job)]) for p in pages]
+    dst_ptrs = [ck.ptr_array([d[i].data_ptr() for i in range(pages_per_job)]) for d in dst]
+    eps = (C.c_float * pages_per_job)(*([cfg["eps"]] * pages_per_job))
+    pipe = C.c_void_p()
+    codec._check(lib.ckv_pipe_create(codec.ctx, chunk_pages, C.byref(pipe)), f"{name} pipe")
+    try:
+        # slabs of the raw job size: the synthetic pages compress by more than 1.3x (a job that
+        # did not fit would fail the store with CKV_ERR_CAPACITY, not overrun)
+        slabs = [torch.empty(raw_job, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        meta = [{"o": (C.c_size_t * pages_per_job)(), "s": (C.c_size_t * pages_per_job)(),
+                 "b": (C.c_float * pages_per_job)(), "t": C.c_size_t(0)} for _ in range(jobs)]
+        side = torch.cuda.Stream(device)
+        last_reader = [0, 0]   # restore ticket that last read each slab
+        stored = [0] * jobs
+
+        def restore(r, after):
+            side.wait_stream(torch.cuda.current_stream(device))
+            t = C.c_uint64(0)
+            m = meta[r]
+            codec._check(lib.ckv_pipe_restore_bf16(
+                pipe, slabs[r % 2].data_ptr(), m["o"], m["s"], m["b"], pages_per_job, n,
+                dst_ptrs[r], after, C.byref(t), side.cuda_stream), f"{name} restore")
+            last_reader[r % 2] = t.value
+
+        def step():
+            main = torch.cuda.current_stream(device)
+            moved = 0
+            for r in range(jobs + 1):
+                if r >= 1:
+                    restore(r - 1, stored[r - 1])
+                if r < jobs:
+                    t = C.c_uint64(0)
+                    m = meta[r]
+                    codec._check(lib.ckv_pipe_store_bf16(
+                        pipe, src_ptrs[r], eps, pages_per_job, n, slabs[r % 2].data_ptr(), raw_job,
+                        m["o"], m["s"], m["b"], C.byref(m["t"]), last_reader[r % 2], C.byref(t),
+                        main.cuda_stream), f"{name} store")
+                    stored[r] = t.value
+                    moved += m["t"].value
+            codec._check(lib.ckv_pipe_join(pipe, last_reader[(jobs - 1) % 2], main.cuda_stream),
+                         f"{name} join")
+            main.wait_stream(side)
+            return moved
+
+        step()
+        times, moved = timed_steps(step, steps, flush, device)
+        torch.cuda.synchronize(device)
+        ok = True
+        for r in sorted({0, jobs - 1}):
+            b = torch.tensor(list(meta[r]["b"]), device=device).view(-1, 1)
+            for p0 in range(0, pages_per_job, 256):
+                x = pages[r][p0:p0 + 256].float()
+                xh = dst[r][p0:p0 + 256].float()
+                ok &= bool(((x - xh).abs() <= b[p0:p0 + 256] * 1.01 + 1e-7 +
+                            x.abs() * 2.0 ** -8).all())
+        t = sum(times) / 1e3
+        raw_step = jobs * raw_job
+        return {
+            "workload": f"{name}: {cfg['what']}; {jobs} jobs x {pages_per_job} pages x {n} BF16 "
+                        f"({raw_step / 1e9:.2f} GB), seeded on the device",
+            "e2e_gbps": round(job_rate(1, raw_step, steps, t), 3),
+            "ms_per_step": round(t * 1e3 / steps, 3),
+            "compression_ratio": round(raw_step / max(1, moved[-1]), 4),
+            "d2h_bytes_per_step": int(moved[-1]), "h2d_bytes_per_step": int(moved[-1]),
+            "restore_ok": ok,
+            "path": "per job: ckv_pipe_store_bf16 on the caller's stream into one of two slabs, "
+                    "overlapped with ckv_pipe_restore_bf16 of the previous job on a second stream; "
+                    f"{chunk_pages} pages per chunk",
+        }
+    finally:
+        torch.cuda.synchronize(device)
+        lib.ckv_pipe_destroy(pipe)
+
+
 def raw_pcie(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -> float:
     """Raw pinned D2H + H2D of the uncompressed pages, one after the other (the
     PCIe reference point): seconds for `steps` steps of 2 x the pages' bytes."""
@@ -855,6 +976,8 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c3", action="store_true",
                     help="skip the C3 mixed per-layer profile leg")
+    ap.add_argument("--streamed", default="",
+                    help="comma-separated extra legs: C4 (30 GB, 16 requests), C5 (5.4 GB shard)")
     ap.add_argument("--chunk-pages", type=int, default=0,
                     help="pages per pipeline chunk (0: the whole job in one chunk)")
     args = ap.parse_args()
@@ -958,6 +1081,10 @@ def main() -> int:
     c3 = (layer_groups_c3(codec, min(args.steps, 10), flush, device,
                           chunk_pages=args.chunk_pages)
           if impl == "ours" and pipelined and rank == 0 and not args.no_c3 else None)
+    streamed = {}
+    for name in [w.strip() for w in args.streamed.split(",") if w.strip()]:
+        if impl == "ours" and pipelined and rank == 0:
+            streamed[name] = streamed_jobs(codec, name, 3, flush, device)
 
     e2e_match = codec.e2e_matches() if pipelined else None
     t_step, t_e2e, t_serial = slowest_rank(
@@ -1051,6 +1178,8 @@ def main() -> int:
         line["kernels"] = kernels
         line["pipeline_codecs"] = piped
         line["layer_groups_c3"] = c3
+        if streamed:
+            line["streamed"] = streamed
         line["gpu_launches"] = launches_total
         line["gpu_launches_value_region"] = launches_value
     else:
