@@ -15,6 +15,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -77,6 +78,8 @@ struct ckv_ctx {
     cudaEvent_t t_start[kTimedKinds] = {};
     cudaEvent_t t_stop[kTimedKinds] = {};
     bool t_valid[kTimedKinds] = {};
+    // completion of a compress call's kernels (polled, see wait_stream)
+    cudaEvent_t sync_ev = nullptr;
 };
 
 namespace {
@@ -257,6 +260,26 @@ ckv_status status_to_code(ckv_ctx* ctx, uint32_t bits) {
     return fail(ctx, CKV_ERR_INTERNAL, "kernel consistency check failed (status 0x%x)", bits);
 }
 
+// Waits for the work queued on `stream` so far.  A compress call returns
+// once its kernels (tens to hundreds of microseconds) are done; a blocking
+// wait adds the host thread's wake-up latency to every call, so the event
+// is polled for up to 2 ms before the wait blocks.
+cudaError_t wait_stream(ckv_ctx* ctx, cudaStream_t stream) {
+    if (!ctx->sync_ev) {
+        cudaError_t e = cudaEventCreateWithFlags(&ctx->sync_ev, cudaEventDisableTiming);
+        if (e != cudaSuccess) return e;
+    }
+    cudaError_t e = cudaEventRecord(ctx->sync_ev, stream);
+    if (e != cudaSuccess) return e;
+    const auto start = std::chrono::steady_clock::now();
+    for (;;) {
+        e = cudaEventQuery(ctx->sync_ev);
+        if (e != cudaErrorNotReady) return e;
+        if (std::chrono::steady_clock::now() - start > std::chrono::milliseconds(2))
+            return cudaEventSynchronize(ctx->sync_ev);
+    }
+}
+
 // Encode a prepared batch and return sizes / bounds on the host.
 ckv_status run_encode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, size_t* sizes,
                       float* bounds, void* stream_ptr) {
@@ -293,7 +316,7 @@ ckv_status run_encode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, size_t* sizes,
     timing_end(ctx, 0, stream);
     release(slot, stream);
     if (e != cudaSuccess) return cuda_fail(ctx, "encode launch", e);
-    e = cudaStreamSynchronize(stream);
+    e = wait_stream(ctx, stream);
     if (e != cudaSuccess) return cuda_fail(ctx, "encode", e);
     uint32_t bits = 0;
     for (size_t i = 0; i < count; ++i) {
@@ -480,10 +503,11 @@ void ckv_destroy(ckv_ctx* ctx) {
         cudaFreeHost(ctx->bounds);
         cudaFreeHost(ctx->status);
         cudaFree(ctx->dec_status);
-        for (int k = 0; k < 3; ++k) {
+        for (int k = 0; k < ckv_ctx::kTimedKinds; ++k) {
             if (ctx->t_start[k]) cudaEventDestroy(ctx->t_start[k]);
             if (ctx->t_stop[k]) cudaEventDestroy(ctx->t_stop[k]);
         }
+        if (ctx->sync_ev) cudaEventDestroy(ctx->sync_ev);
     }
     delete ctx;
 }

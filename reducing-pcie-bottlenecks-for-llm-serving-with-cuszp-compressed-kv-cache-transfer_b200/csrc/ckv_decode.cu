@@ -37,6 +37,8 @@
 // zero_fill writes (float)0 * eb * 2.0f there instead.
 #include "ckv_launch.h"
 
+#include <atomic>
+
 namespace ckv {
 namespace {
 
@@ -553,28 +555,42 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
     if (status && lane == 0) atomicOr(&a.status[0], status);
 }
 
-int sm_count() {
-    static int count = 0;
-    if (!count) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-            count <= 0)
-            count = 148;
+// SMs of the current device, once the decoder's shared-memory size is set
+// on it (both done once per device and element type).
+template <typename T>
+cudaError_t prepare_device(int* sms) {
+    constexpr int kMaxDevices = 64;
+    static std::atomic<int> cache[kMaxDevices];
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    if (dev >= 0 && dev < kMaxDevices) {
+        const int v = cache[dev].load(std::memory_order_acquire);
+        if (v > 0) {
+            *sms = v;
+            return cudaSuccess;
+        }
     }
-    return count;
+    err = cudaFuncSetAttribute(decode_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (err != cudaSuccess) return err;
+    int count = 0;
+    err = cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+    if (err != cudaSuccess) return err;
+    if (count <= 0) return cudaErrorInvalidDevice;
+    if (dev >= 0 && dev < kMaxDevices) cache[dev].store(count, std::memory_order_release);
+    *sms = count;
+    return cudaSuccess;
 }
 
 template <typename T>
 cudaError_t launch_decode_t(const DecodeLaunch& l, cudaStream_t stream) {
     if (l.num_units == 0) return cudaErrorInvalidValue;
-    auto kernel = decode_kernel<T>;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kSmem);
+    int sms = 0;
+    cudaError_t err = prepare_device<T>(&sms);
     if (err != cudaSuccess) return err;
     DecodeArgs args{l.units, l.maps, l.num_units, l.total_items, l.uniform_items,
                     l.zero_fill ? 1u : 0u, l.status, shift_mul()};
-    const uint32_t ctas = static_cast<uint32_t>(sm_count() * kCtasPerSm);
+    const uint32_t ctas = static_cast<uint32_t>(sms * kCtasPerSm);
     const uint32_t grid = l.total_items < ctas ? l.total_items : ctas;
     if (grid == 0) return cudaSuccess;
     note_launch();
