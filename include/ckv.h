@@ -240,6 +240,10 @@ CKV_API ckv_status ckv_pipe_restore_bf16(ckv_pipe* pipe, const uint8_t* host,
  * query it (1 done, 0 pending, -1 unknown).  A pipeline keeps the last 64
  * tickets. */
 CKV_API ckv_status ckv_pipe_join(ckv_pipe* pipe, uint64_t ticket, void* stream);
+/* A ticket for the work queued on `stream` so far (the caller's own copies
+ * into or out of a host buffer, which later pipeline calls can then be
+ * ordered after with `after`). */
+CKV_API ckv_status ckv_pipe_record(ckv_pipe* pipe, void* stream, uint64_t* ticket);
 CKV_API ckv_status ckv_pipe_wait(ckv_pipe* pipe, uint64_t ticket);
 CKV_API int ckv_pipe_done(ckv_pipe* pipe, uint64_t ticket);
 

@@ -44,7 +44,7 @@ EXPORTS = (
     "ckv_device_status", "ckv_kernel_launches", "ckv_pack",
     "ckv_set_kernel_timing", "ckv_kernel_time", "ckv_compress_batch_fixed_bf16_noalloc",
     "ckv_pipe_create", "ckv_pipe_destroy", "ckv_pipe_store_bf16", "ckv_pipe_restore_bf16",
-    "ckv_pipe_join", "ckv_pipe_wait", "ckv_pipe_done", "ckv_pipe_host_capacity",
+    "ckv_pipe_join", "ckv_pipe_record", "ckv_pipe_wait", "ckv_pipe_done", "ckv_pipe_host_capacity",
     "ckv_pipe_store_int8", "ckv_pipe_restore_int8", "ckv_pipe_store_raw", "ckv_pipe_restore_raw",
     "ckv_pipe_host_capacity_int8", "ckv_pipe_host_capacity_raw",
     "ckv_pipe_store_bf16_groups", "ckv_pipe_restore_bf16_groups", "ckv_pipe_host_capacity_groups",
@@ -109,6 +109,7 @@ def _declare(lib: C.CDLL) -> None:
         "ckv_pipe_restore_bf16": (
             c_status, [P, P, P, P, P, c_size, c_size, P, C.c_uint64, P, P]),
         "ckv_pipe_join": (c_status, [P, C.c_uint64, P]),
+        "ckv_pipe_record": (c_status, [P, P, P]),
         "ckv_pipe_wait": (c_status, [P, C.c_uint64]),
         "ckv_pipe_done": (c_int, [P, C.c_uint64]),
         "ckv_pipe_host_capacity": (c_size, [c_size, c_size]),

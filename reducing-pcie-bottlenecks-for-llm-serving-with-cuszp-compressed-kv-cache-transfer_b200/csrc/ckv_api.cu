@@ -1579,6 +1579,12 @@ ckv_status ckv_pipe_join(ckv_pipe* p, uint64_t ticket, void* stream) {
     return pipe_after(p, ticket, static_cast<cudaStream_t>(stream));
 }
 
+ckv_status ckv_pipe_record(ckv_pipe* p, void* stream, uint64_t* ticket) {
+    if (!p || !ticket) return CKV_ERR_ARGUMENT;
+    DeviceGuard guard(p->ctx->device);
+    return pipe_issue(p, static_cast<cudaStream_t>(stream), ticket);
+}
+
 ckv_status ckv_pipe_wait(ckv_pipe* p, uint64_t ticket) {
     if (!p) return CKV_ERR_ARGUMENT;
     if (!ticket) return CKV_OK;

@@ -40,6 +40,10 @@ import torch
 
 import _ckv
 
+# Smallest unit the reference's connector compresses; smaller pages are
+# zero-padded to it (vllm_v1_compressed_offload.py:49).
+MIN_CUSZP_ELEMENTS = 36864
+
 # --------------------------------------------------------------------------
 # Host metadata (vllm_v1_compressed_offload.py:58-88)
 
@@ -98,20 +102,23 @@ class JobHeader:
     Layout (little-endian): magic b"CKVJ", u16 version, u16 element type
     (0 BF16), u32 page count, u64 elements per page, u64 payload bytes, f32
     requested bound, u32 flags (bit 0: relative bound), u32 segments per
-    page (G), u32 layer prefix count, u32 source layers (L; 0 when G = 1).
-    When G > 1 a layer table follows: L u8 segment indices (the segment that
-    holds each layer, padded to 4 bytes) and G f32 requested bounds.  Then
-    per page and segment (entry i*G + g) u64 offset (from the payload
-    start), u64 size, f32 absolute bound, u32 zero; the payload starts at
-    the next 256-byte boundary.  A segment of G > 1 holds the page's layers
-    of that segment, in ascending layer order, as
-    compress_batch_fixed_bf16_indexed encodes them.
+    page (G), u32 layer prefix count, u32 source layers (L; 0 when G = 1),
+    u64 elements per coded page (G = 1: the page zero-padded to the codec's
+    minimum, MIN_CUSZP_ELEMENTS; 0 when G > 1).  When G > 1 a layer table
+    follows: L u8 segment indices (the segment that holds each layer, padded
+    to 4 bytes) and G f32 requested bounds.  Then per page and segment (entry
+    i*G + g) u64 offset (from the payload start), u64 size, f32 absolute
+    bound, u32 flags (bit 0: the entry holds the raw BF16 bytes); the payload
+    starts at the next 256-byte boundary.  A segment of G > 1 holds the
+    page's layers of that segment, in ascending layer order, as
+    compress_batch_fixed_bf16_indexed encodes them (or their raw bytes).
     """
 
     MAGIC = b"CKVJ"
-    VERSION = 2
-    _HEAD = struct.Struct("<4sHHIQQfIIII")
-    _PAGE = np.dtype([("offset", "<u8"), ("size", "<u8"), ("bound", "<f4"), ("zero", "<u4")])
+    VERSION = 3
+    RAW = 1
+    _HEAD = struct.Struct("<4sHHIQQfIIIIQ")
+    _PAGE = np.dtype([("offset", "<u8"), ("size", "<u8"), ("bound", "<f4"), ("flags", "<u4")])
 
     @staticmethod
     def _layer_table_bytes(segments: int, layers: int) -> int:
@@ -125,17 +132,19 @@ class JobHeader:
     @classmethod
     def write(cls, slab: torch.Tensor, n: int, eps: float, relative: bool, offsets, sizes,
               bounds, payload_bytes: int, groups=None, prefix: int = 0,
-              layers: int = 0) -> None:
+              layers: int = 0, raw=None, coded: int = 0) -> None:
         """`groups`: None for whole pages, else [(requested bound, layer
         indices)] per segment, the pages viewed as [prefix, layers, n /
-        (prefix * layers)]."""
+        (prefix * layers)].  `raw`: per entry, whether it holds raw bytes.
+        `coded`: elements per coded page (whole pages; default n)."""
         segs = 1 if not groups else len(groups)
         count = len(offsets) // segs
         buf = slab[: cls.bytes_for(count, segs, layers)].numpy()
         buf[: cls._HEAD.size] = np.frombuffer(
             cls._HEAD.pack(cls.MAGIC, cls.VERSION, 0, count, n, payload_bytes, eps,
                            1 if relative else 0, segs, prefix if segs > 1 else 0,
-                           layers if segs > 1 else 0), dtype=np.uint8)
+                           layers if segs > 1 else 0, (coded or n) if segs == 1 else 0),
+            dtype=np.uint8)
         start = cls._HEAD.size
         if segs > 1:
             owner = np.zeros((layers + 3) // 4 * 4, dtype=np.uint8)
@@ -149,6 +158,8 @@ class JobHeader:
         table["offset"] = np.ctypeslib.as_array(offsets)
         table["size"] = np.ctypeslib.as_array(sizes)
         table["bound"] = np.ctypeslib.as_array(bounds)
+        if raw is not None:
+            table["flags"] = np.asarray(raw, dtype=bool).astype(np.uint32) * cls.RAW
         buf[start:start + table.nbytes] = table.view(np.uint8)
 
     @classmethod
@@ -158,11 +169,11 @@ class JobHeader:
         if len(raw) < cls._HEAD.size:
             raise ValueError("slab shorter than a job header")
         (magic, version, etype, count, n, payload, eps, flags, segs, prefix,
-         layers) = cls._HEAD.unpack(raw)
+         layers, coded) = cls._HEAD.unpack(raw)
         if magic != cls.MAGIC or version != cls.VERSION or etype != 0:
             raise ValueError("not a compressed KV job (bad magic, version or element type)")
         if segs == 0 or (segs > 1 and (prefix == 0 or layers < segs or
-                                       n % (prefix * layers))):
+                                       n % (prefix * layers))) or (segs == 1 and coded < n):
             raise ValueError("bad segment description")
         hdr = cls.bytes_for(count, segs, layers)
         if slab.numel() < hdr + payload:
@@ -184,12 +195,19 @@ class JobHeader:
                               .numpy().tobytes(), dtype=cls._PAGE)
         if np.any(table["offset"] + table["size"] > payload) or np.any(table["size"] == 0):
             raise ValueError("page table points outside the payload")
+        raw_entries = (table["flags"] & cls.RAW) != 0
+        seg_elems = ([n] if segs == 1 else
+                     [prefix * len(sel) * (n // (prefix * layers)) for _b, sel in groups])
+        want = np.tile(np.asarray(seg_elems, dtype=np.uint64) * 2, count)
+        if np.any(raw_entries & (table["size"] != want)):
+            raise ValueError("raw entry of the wrong size")
         return {"count": count, "n": n, "eps": eps, "relative": bool(flags & 1),
                 "segments": segs, "prefix": prefix, "layers": layers, "groups": groups,
-                "payload_at": hdr, "payload_bytes": payload,
+                "coded": coded, "payload_at": hdr, "payload_bytes": payload,
                 "offsets": table["offset"].astype(np.uint64),
                 "sizes": table["size"].astype(np.uint64),
-                "bounds": table["bound"].astype(np.float32)}
+                "bounds": table["bound"].astype(np.float32),
+                "raw": raw_entries}
 
 
 # --------------------------------------------------------------------------
@@ -212,6 +230,7 @@ class _PageRecord:
     sizes: tuple[int, ...]
     bounds: tuple[float, ...]
     n: int
+    raw: tuple[bool, ...] = ()       # per segment: raw BF16 bytes instead of a cuSZp stream
 
 
 class CompressedPageStore:
@@ -317,7 +336,9 @@ class _Engine:
     ``[layer_prefix, len(layer_bounds), n / (layer_prefix * layers)]`` and
     stored as one segment per distinct bound, in ascending bound order (the
     reference's ``sorted(grouped.items())``); layers missing from the mapping
-    take `error_bound`.  One distinct bound leaves whole pages."""
+    take `error_bound`.  One distinct bound leaves whole pages.  Whole pages
+    smaller than MIN_CUSZP_ELEMENTS are coded zero-padded to it, as the
+    reference's batched path pads them (:904-909)."""
 
     def __init__(self, kv_cache: torch.Tensor, error_bound: float, device_id: int,
                  chunk_pages: int, layer_bounds=None, layer_prefix: int = 2):
@@ -330,6 +351,7 @@ class _Engine:
         self.page_bytes = self.n * 2
         self.error_bound = float(error_bound)
         self._set_groups(layer_bounds, int(layer_prefix))
+        self.coded = max(self.n, MIN_CUSZP_ELEMENTS) if self.groups is None else self.n
         self.ctx = C.c_void_p()
         cfg = _ckv.Config(self.error_bound, 1, _ckv.DIM_1D, _ckv.MODE_FIXED, _ckv.TYPE_FLOAT)
         self._check(self.lib.ckv_create(cfg, int(device_id), C.byref(self.ctx)), "ckv_create")
@@ -337,6 +359,7 @@ class _Engine:
         self._check(self.lib.ckv_pipe_create(self.ctx, int(chunk_pages), C.byref(self.pipe)),
                     "ckv_pipe_create")
         self.lock = threading.Lock()
+        self._held: list[tuple[torch.cuda.Event, list[torch.Tensor]]] = []
 
     def _set_groups(self, layer_bounds, prefix: int) -> None:
         self.groups = None          # [(requested bound, layer indices)] per segment
@@ -360,9 +383,13 @@ class _Engine:
         if len(grouped) == 1:
             self.error_bound = next(iter(grouped))
             return
-        self.groups = [(b, tuple(sel)) for b, sel in sorted(grouped.items())]
-        self.segments = len(self.groups)
-        self.prefix, self.layers, self.epl = prefix, layers, self.n // (prefix * layers)
+        groups = [(b, tuple(sel)) for b, sel in sorted(grouped.items())]
+        epl = self.n // (prefix * layers)
+        if any(prefix * len(sel) * epl < MIN_CUSZP_ELEMENTS for _b, sel in groups):
+            raise ValueError(f"a layer segment is smaller than {MIN_CUSZP_ELEMENTS} elements")
+        self.groups = groups
+        self.segments = len(groups)
+        self.prefix, self.layers, self.epl = prefix, layers, epl
         self._index = [torch.tensor(sel, dtype=torch.int64, device=self.device)
                        for _b, sel in self.groups]
         G = self.segments
@@ -372,6 +399,13 @@ class _Engine:
 
     def segment_numel(self, g: int) -> int:
         return self.n if self.groups is None else self.prefix * len(self.groups[g][1]) * self.epl
+
+    def segment_bytes(self, page: torch.Tensor, g: int) -> torch.Tensor:
+        """The raw bytes of segment g of a page (a device tensor)."""
+        if self.groups is None:
+            return page.reshape(-1).view(torch.uint8)
+        view = page.reshape(self.prefix, self.layers, self.epl)
+        return view.index_select(1, self._index[g]).contiguous().view(-1).view(torch.uint8)
 
     def _check(self, status: int, what: str) -> None:
         if status != 0:
@@ -385,7 +419,7 @@ class _Engine:
 
     def host_capacity(self, count: int) -> int:
         if self.groups is None:
-            return int(self.lib.ckv_pipe_host_capacity(count, self.n))
+            return int(self.lib.ckv_pipe_host_capacity(count, self.coded))
         return int(self.lib.ckv_pipe_host_capacity_groups(count, self.sel, self.segments,
                                                           self.prefix, self.epl))
 
@@ -393,7 +427,7 @@ class _Engine:
               sizes, bounds, total, after: int, ticket, stream: int) -> None:
         if self.groups is None:
             self._check(self.lib.ckv_pipe_store_bf16(
-                self.pipe, pages, (C.c_float * count)(*([eps] * count)), count, self.n, host,
+                self.pipe, pages, (C.c_float * count)(*([eps] * count)), count, self.coded, host,
                 cap, offsets, sizes, bounds, total, after, ticket, stream), "store")
         else:
             self._check(self.lib.ckv_pipe_store_bf16_groups(
@@ -401,17 +435,112 @@ class _Engine:
                 self.layers, self.epl, self.eps, host, cap, offsets, sizes, bounds, total,
                 after, ticket, stream), "store")
 
-    def restore(self, host: int, offsets, sizes, bounds, count: int, pages: C.Array,
-                after: int, ticket, stream: int) -> None:
-        if self.groups is None:
-            self._check(self.lib.ckv_pipe_restore_bf16(
-                self.pipe, host, offsets, sizes, bounds, count, self.n, pages, after, ticket,
-                stream), "restore")
+    def join(self, ticket: int, stream: int) -> None:
+        self._check(self.lib.ckv_pipe_join(self.pipe, ticket, stream), "join")
+
+    def record(self, stream: int) -> int:
+        t = C.c_uint64(0)
+        self._check(self.lib.ckv_pipe_record(self.pipe, stream, C.byref(t)), "record")
+        return t.value
+
+    def hold(self, tensors: list[torch.Tensor], stream) -> None:
+        """Keeps device tensors the pipeline's own streams use alive until the
+        work queued on `stream` (ordered after them) is done."""
+        self._held = [(ev, ts) for ev, ts in self._held if not ev.query()]
+        if tensors:
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            self._held.append((ev, tensors))
+
+    def restore(self, payload: torch.Tensor, offsets, sizes, bounds, raw, dst, after: int,
+                stream) -> int:
+        """Restores a job's entries (page i, segment g at i * G + g) from
+        `payload` (the pinned bytes after the job header) into the 1-D page
+        tensors `dst`: cuSZp entries through the pipeline, raw entries by
+        copies, padded pages through a staging buffer.  Returns a ticket that
+        covers all of it."""
+        G, count = self.segments, len(dst)
+        sptr = stream.cuda_stream
+        offsets = np.asarray(offsets, dtype=np.uint64).reshape(count, G)
+        sizes = np.asarray(sizes, dtype=np.uint64).reshape(count, G)
+        bounds = np.asarray(bounds, dtype=np.float32).reshape(count, G)
+        raw = np.asarray(raw, dtype=bool).reshape(count, G)
+        base = payload.data_ptr()
+        tickets, held, extra = [], [], False
+
+        def arrays(sel, g=None):
+            cols = slice(None) if g is None else slice(g, g + 1)
+            o, z, b = offsets[sel][:, cols], sizes[sel][:, cols], bounds[sel][:, cols]
+            k = o.size
+            return ((C.c_size_t * k)(*o.reshape(-1).tolist()), (C.c_size_t * k)(*z.reshape(-1).tolist()),
+                    (C.c_float * k)(*b.reshape(-1).tolist()))
+
+        if G == 1 or not raw.any():
+            sel = np.flatnonzero(~raw.any(axis=1))
+            if sel.size:
+                o, z, b = arrays(sel)
+                t = C.c_uint64(0)
+                if G == 1:
+                    if self.coded > self.n:
+                        stage = torch.empty(len(sel), self.coded, dtype=torch.bfloat16,
+                                            device=self.device)
+                        held.append(stage)
+                        ptrs = _ckv.ptr_array([stage[k].data_ptr() for k in range(len(sel))])
+                    else:
+                        ptrs = _ckv.ptr_array([dst[i].data_ptr() for i in sel])
+                    self._check(self.lib.ckv_pipe_restore_bf16(
+                        self.pipe, base, o, z, b, len(sel), self.coded, ptrs, after,
+                        C.byref(t), sptr), "restore")
+                    if self.coded > self.n:
+                        self.join(t.value, sptr)
+                        for k, i in enumerate(sel):
+                            dst[i].copy_(stage[k, :self.n])
+                        extra = True
+                else:
+                    self._check(self.lib.ckv_pipe_restore_bf16_groups(
+                        self.pipe, base, o, z, b, len(sel), self.idx, self.sel, G, self.prefix,
+                        self.layers, self.epl, _ckv.ptr_array([dst[i].data_ptr() for i in sel]),
+                        after, C.byref(t), sptr), "restore")
+                tickets.append(t.value)
         else:
-            self._check(self.lib.ckv_pipe_restore_bf16_groups(
-                self.pipe, host, offsets, sizes, bounds, count, self.idx, self.sel,
-                self.segments, self.prefix, self.layers, self.epl, pages, after, ticket,
-                stream), "restore")
+            # some segments are raw: each group's cuSZp segments in a call of their own
+            for g in range(G):
+                sel = np.flatnonzero(~raw[:, g])
+                if not sel.size:
+                    continue
+                o, z, b = arrays(sel, g)
+                t = C.c_uint64(0)
+                self._check(self.lib.ckv_pipe_restore_bf16_groups(
+                    self.pipe, base, o, z, b, len(sel), (C.c_void_p * 1)(self.idx[g]),
+                    (C.c_size_t * 1)(self.sel[g]), 1, self.prefix, self.layers, self.epl,
+                    _ckv.ptr_array([dst[i].data_ptr() for i in sel]), after, C.byref(t), sptr),
+                    "restore")
+                tickets.append(t.value)
+        if raw.any():
+            # raw entries: copied from the page-locked payload after the store that wrote it
+            self.join(after, sptr)
+            with torch.cuda.stream(stream):
+                for i, g in zip(*np.nonzero(raw)):
+                    o, nbytes = int(offsets[i, g]), 2 * self.segment_numel(g)
+                    src = payload[o:o + nbytes]
+                    if self.groups is None:
+                        dst[i].view(torch.uint8).copy_(src, non_blocking=True)
+                    else:
+                        tmp = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+                        tmp.copy_(src, non_blocking=True)
+                        dst[i].view(self.prefix, self.layers, self.epl).index_copy_(
+                            1, self._index[g],
+                            tmp.view(torch.bfloat16).view(self.prefix, len(self.groups[g][1]),
+                                                          self.epl))
+            extra = True
+        if len(tickets) == 1 and not extra:
+            final = tickets[0]
+        else:
+            for t in tickets:
+                self.join(t, sptr)
+            final = self.record(sptr)
+        self.hold(held, stream)
+        return final
 
     def close(self) -> None:
         if self.pipe:
@@ -420,6 +549,7 @@ class _Engine:
         if self.ctx:
             self.lib.ckv_destroy(self.ctx)
             self.ctx = C.c_void_p()
+        self._held = []
 
 
 class CompressedOffloadingHandler:
@@ -451,6 +581,14 @@ class CompressedOffloadingHandler:
     def _store(self, gpu_ids: np.ndarray, cpu_ids: np.ndarray) -> tuple[list[int], int]:
         e = self.engine
         count, G = len(gpu_ids), e.segments
+        stream = torch.cuda.current_stream(e.device)
+        if e.coded > e.n:
+            # small pages, zero-padded to the codec's minimum (vllm_v1_compressed_offload.py:904-909)
+            src = torch.zeros(count, e.coded, dtype=torch.bfloat16, device=e.device)
+            src[:, :e.n] = e.kv.view(e.kv.shape[0], -1)[torch.as_tensor(gpu_ids, device=e.device)]
+            pages = _ckv.ptr_array([src[i].data_ptr() for i in range(count)])
+        else:
+            pages = e.page_ptrs(gpu_ids)
         hdr = JobHeader.bytes_for(count, G, e.layers)
         cap = e.host_capacity(count)
         sid = self.store._take_slab(hdr + cap, hdr,
@@ -461,12 +599,28 @@ class CompressedOffloadingHandler:
         bounds = (C.c_float * (count * G))()
         total = C.c_size_t(0)
         ticket = C.c_uint64(0)
-        stream = torch.cuda.current_stream(e.device).cuda_stream
-        e.store(e.page_ptrs(gpu_ids), count, self.error_bound, slab.buffer.data_ptr() + hdr, cap,
-                offsets, sizes, bounds, C.byref(total), slab.readers, C.byref(ticket), stream)
-        slab.ticket = ticket.value
+        e.store(pages, count, self.error_bound, slab.buffer.data_ptr() + hdr, cap, offsets, sizes,
+                bounds, C.byref(total), slab.readers, C.byref(ticket), stream.cuda_stream)
+        final = ticket.value
+        # A page (segment) that cuSZp would not shrink below its raw BF16 size is
+        # stored raw, with bound 0 (vllm_v1_compressed_offload.py:1000-1010): its
+        # raw bytes fit where its longer stream was packed.
+        seg_bytes = [2 * e.segment_numel(g) for g in range(G)]
+        raw = [int(sizes[j]) >= seg_bytes[j % G] for j in range(count * G)]
+        if any(raw):
+            e.join(final, stream.cuda_stream)
+            with torch.cuda.stream(stream):
+                for j in (j for j in range(count * G) if raw[j]):
+                    i, g = divmod(j, G)
+                    src_bytes = e.segment_bytes(e.kv[int(gpu_ids[i])], g)
+                    at = hdr + int(offsets[j])
+                    slab.buffer[at:at + seg_bytes[g]].copy_(src_bytes, non_blocking=True)
+                    sizes[j] = seg_bytes[g]
+                    bounds[j] = 0.0
+            final = e.record(stream.cuda_stream)
+        slab.ticket = final
         JobHeader.write(slab.buffer, e.n, self.error_bound, True, offsets, sizes, bounds,
-                        total.value, e.groups, e.prefix, e.layers)
+                        total.value, e.groups, e.prefix, e.layers, raw=raw, coded=e.coded)
         comps = [self._components(g) for g in range(G)]
         req = [self.error_bound] if e.groups is None else [b for b, _sel in e.groups]
         entries = []
@@ -474,41 +628,45 @@ class CompressedOffloadingHandler:
             span = range(i * G, i * G + G)
             rec = _PageRecord(sid, tuple(int(offsets[j]) for j in span),
                               tuple(int(sizes[j]) for j in span),
-                              tuple(float(bounds[j]) for j in span), e.n)
+                              tuple(float(bounds[j]) for j in span), e.n,
+                              tuple(raw[j] for j in span))
             segs = []
             for g in range(G):
                 numel = e.segment_numel(g)
+                coded = e.coded if e.groups is None else numel
                 payload = slab.buffer[hdr + rec.offsets[g]: hdr + rec.offsets[g] + rec.sizes[g]]
-                segs.append(EncodedSegment(payload, rec.sizes[g], rec.bounds[g], "cuszp",
-                                           comps[g], numel, numel, numel * 2, req[g],
-                                           cuszp_mode="fixed"))
+                segs.append(EncodedSegment(payload, rec.sizes[g], rec.bounds[g],
+                                           "raw" if rec.raw[g] else "cuszp", comps[g], numel,
+                                           coded, numel * 2, req[g],
+                                           cuszp_mode=None if rec.raw[g] else "fixed"))
             entries.append((int(cpu_ids[i]),
                             rec, CompressedBundle(tuple(segs), sum(rec.sizes), e.page_bytes)))
         self.store.put_many_packed(entries)
-        return [ticket.value], int(total.value)
+        return [final], int(total.value)
 
     def _load(self, cpu_ids: np.ndarray, gpu_ids: np.ndarray) -> tuple[list[int], int]:
         e = self.engine
         recs = [self.store.record(int(c)) for c in cpu_ids]
         if any(len(r.sizes) != e.segments or r.n != e.n for r in recs):
             raise ValueError("stored page does not match the KV cache layout")
+        if gpu_ids.size and (gpu_ids.min() < 0 or gpu_ids.max() >= e.kv.shape[0]):
+            raise IndexError("GPU block id out of range")
         by_slab: dict[int, list[int]] = {}
         for i, r in enumerate(recs):
             by_slab.setdefault(r.slab, []).append(i)
         tickets, nbytes = [], 0
-        stream = torch.cuda.current_stream(e.device).cuda_stream
+        stream = torch.cuda.current_stream(e.device)
         for sid, idx in by_slab.items():
             slab = self.store.slab(sid)
-            count = len(idx)
-            offsets = (C.c_size_t * (count * e.segments))(*[o for i in idx for o in recs[i].offsets])
-            sizes = (C.c_size_t * (count * e.segments))(*[z for i in idx for z in recs[i].sizes])
-            bounds = (C.c_float * (count * e.segments))(*[b for i in idx for b in recs[i].bounds])
-            base = slab.buffer.data_ptr() + slab.payload_at
-            ticket = C.c_uint64(0)
-            e.restore(base, offsets, sizes, bounds, count, e.page_ptrs(gpu_ids[np.asarray(idx)]),
-                      slab.ticket, C.byref(ticket), stream)
-            slab.readers = ticket.value
-            tickets.append(ticket.value)
+            offs = [o for i in idx for o in recs[i].offsets]
+            sizes = [z for i in idx for z in recs[i].sizes]
+            bounds = [b for i in idx for b in recs[i].bounds]
+            raw = [r for i in idx for r in (recs[i].raw or (False,) * e.segments)]
+            dst = [e.kv[int(gpu_ids[i])].view(-1) for i in idx]
+            t = e.restore(slab.buffer[slab.payload_at:], offs, sizes, bounds, raw, dst,
+                          slab.ticket, stream)
+            slab.readers = t
+            tickets.append(t)
             nbytes += sum(sizes)
         return tickets, nbytes
 
@@ -589,17 +747,12 @@ def restore_job(slab: torch.Tensor, dst_pages: Sequence[torch.Tensor], engine: _
     if job["n"] != engine.n or len(dst_pages) != job["count"]:
         raise ValueError("job does not match the destination pages")
     same = job["segments"] == engine.segments and (
-        engine.groups is None or
-        ([sel for _b, sel in job["groups"]] == [sel for _b, sel in engine.groups] and
+        (engine.groups is None and job["coded"] == engine.coded) or
+        (engine.groups is not None and
+         [sel for _b, sel in job["groups"]] == [sel for _b, sel in engine.groups] and
          job["prefix"] == engine.prefix and job["layers"] == engine.layers))
     if not same:
         raise ValueError("job segments do not match the engine's layer groups")
-    count, G = job["count"], job["segments"]
-    ticket = C.c_uint64(0)
-    engine.restore(slab.data_ptr() + job["payload_at"],
-                   (C.c_size_t * (count * G))(*job["offsets"].tolist()),
-                   (C.c_size_t * (count * G))(*job["sizes"].tolist()),
-                   (C.c_float * (count * G))(*job["bounds"].tolist()), count,
-                   _ckv.ptr_array([p.data_ptr() for p in dst_pages]), 0, C.byref(ticket),
-                   torch.cuda.current_stream(engine.device).cuda_stream)
-    return ticket.value
+    return engine.restore(slab[job["payload_at"]:], job["offsets"], job["sizes"], job["bounds"],
+                          job["raw"], [p.view(-1) for p in dst_pages], 0,
+                          torch.cuda.current_stream(engine.device))

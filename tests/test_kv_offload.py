@@ -77,6 +77,30 @@ def test_job_header_layer_groups_round_trip():
         ko.JobHeader.read(bad)
 
 
+def test_job_header_raw_entries():
+    """Raw entries are flagged in the page table and must hold exactly the
+    segment's BF16 bytes."""
+    count, n = 3, 36864
+    offsets = (C.c_size_t * count)(0, 73728, 80000)
+    sizes = (C.c_size_t * count)(2 * n, 5000, 2 * n)
+    bounds = (C.c_float * count)(0.0, 1e-4, 0.0)
+    hdr = ko.JobHeader.bytes_for(count)
+    slab = torch.zeros(hdr + 160000, dtype=torch.uint8)
+    ko.JobHeader.write(slab, n, 1e-4, True, offsets, sizes, bounds, 160000,
+                       raw=[True, False, True])
+    job = ko.JobHeader.read(slab)
+    assert job["raw"].tolist() == [True, False, True] and job["coded"] == n
+    ko.JobHeader.write(slab, 8192, 1e-4, True, offsets, sizes, bounds, 160000,
+                       raw=[True, False, True], coded=36864)
+    with pytest.raises(ValueError):
+        ko.JobHeader.read(slab)                 # a raw entry of 2 * 36864 bytes for 8192 elements
+    sizes[0] = sizes[2] = 2 * 8192
+    ko.JobHeader.write(slab, 8192, 1e-4, True, offsets, sizes, bounds, 160000,
+                       raw=[True, False, True], coded=36864)
+    job = ko.JobHeader.read(slab)
+    assert job["coded"] == 36864 and job["n"] == 8192
+
+
 def test_layer_bounds_group_like_the_reference():
     """Segments are the distinct bounds in ascending order, each with its
     layers in ascending order; missing layers take the handler's bound."""
@@ -296,5 +320,177 @@ def test_handlers_layer_groups_match_plain_calls():
         assert h.engine.lib.ckv_pipe_wait(h.engine.pipe, t) == 0
         for k in range(len(pages)):
             assert torch.equal(dst[k].view(torch.int16), restored[k].view(torch.int16))
+    finally:
+        h.shutdown()
+
+
+def _plain_wrapper(cpp, eb):
+    cfg = cpp.CompressionConfig(error_bound=eb, use_relative_error=True,
+                                processing_dim=cpp.CuszpDim.DIM_1D,
+                                encoding_mode=cpp.CuszpMode.MODE_FIXED,
+                                data_type=cpp.CuszpType.TYPE_FLOAT)
+    return cpp.CuSZpWrapper(cfg, 0)
+
+
+@pytest.mark.gpu
+def test_handlers_store_incompressible_pages_raw():
+    """Pages that cuSZp would not shrink below their BF16 size are stored raw
+    with bound 0 (vllm_v1_compressed_offload.py:1000-1010) and come back bit
+    for bit; the others keep the plain call's bytes."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    import cuszp_wrapper_cpp as cpp
+
+    shape = (2, 28, 2, 16, 128)
+    kv = _kv(16, shape, seed=21).cuda()
+    g = torch.Generator().manual_seed(22)
+    noisy = [2, 5, 6]
+    for b in noisy:   # uniform in [-1, 1]: 15 bits per value at REL 1e-5
+        kv[b] = (torch.rand(shape, generator=g) * 2 - 1).to(torch.bfloat16).cuda()
+    snapshot = kv.clone()
+    h = ko.CompressedCpuGpuOffloadingHandlers(kv, error_bound=1e-5, device_id=0, chunk_pages=4)
+    try:
+        gpu_ids = np.arange(0, 8, dtype=np.int64)
+        cpu_ids = gpu_ids + 500
+        h.gpu_to_cpu_handler.transfer_async(1, (gpu_ids, cpu_ids))
+        h.gpu_to_cpu_handler.wait({1})
+        w = _plain_wrapper(cpp, 1e-5)
+        n = kv[0].numel()
+        outs = [torch.empty(w.estimate_compressed_buffer_size(n * 4), dtype=torch.uint8,
+                            device="cuda") for _ in gpu_ids]
+        ok, sizes, bounds = w.compress_batch_fixed_bf16([kv[i].view(-1) for i in gpu_ids], outs,
+                                                        [1e-5] * len(gpu_ids))
+        assert ok
+        for k, cpu in enumerate(cpu_ids):
+            seg = h.store.get(int(cpu)).segments[0]
+            if k in noisy:
+                assert sizes[k] >= 2 * n
+                assert seg.encoding == "raw" and seg.compressed_size == 2 * n
+                assert seg.actual_error_bound == 0.0
+                assert torch.equal(seg.payload, kv[k].view(-1).view(torch.uint8).cpu())
+            else:
+                assert seg.encoding == "cuszp" and seg.compressed_size == sizes[k]
+                assert torch.equal(seg.payload, outs[k][: sizes[k]].cpu())
+        dst = np.arange(8, 16, dtype=np.int64)
+        kv[8:16] = 0
+        h.cpu_to_gpu_handler.transfer_async(2, (cpu_ids, dst))
+        h.cpu_to_gpu_handler.wait({2})
+        torch.cuda.synchronize()
+        restored = torch.zeros(len(gpu_ids), n, dtype=torch.bfloat16, device="cuda")
+        assert w.decompress_batch_fixed_bf16(outs, sizes, restored, n, bounds)
+        torch.cuda.synchronize()
+        for k in range(len(gpu_ids)):
+            want = snapshot[k].view(-1) if k in noisy else restored[k]
+            assert torch.equal(kv[8 + k].view(-1).view(torch.int16), want.view(torch.int16)), k
+        # and from the slab bytes alone
+        slab = h.store.slab(h.store.record(int(cpu_ids[0])).slab).buffer
+        pages = [torch.zeros(n, dtype=torch.bfloat16, device="cuda") for _ in gpu_ids]
+        t = ko.restore_job(slab, pages, h.engine)
+        assert h.engine.lib.ckv_pipe_wait(h.engine.pipe, t) == 0
+        for k in range(len(gpu_ids)):
+            assert torch.equal(pages[k].view(torch.int16), kv[8 + k].view(-1).view(torch.int16))
+    finally:
+        h.shutdown()
+
+
+@pytest.mark.gpu
+def test_handlers_pad_small_pages():
+    """Pages below 36864 elements are coded zero-padded to 36864, as the
+    reference's connector pads them (vllm_v1_compressed_offload.py:904-909):
+    the stored bytes equal the plain call on padded pages, the restore its
+    first n elements."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    import cuszp_wrapper_cpp as cpp
+
+    shape = (2, 1, 2, 16, 128)            # one layer's K and V: 8192 elements
+    kv = _kv(32, shape, seed=23).cuda()
+    n, coded = kv[0].numel(), 36864
+    h = ko.CompressedCpuGpuOffloadingHandlers(kv, error_bound=1e-4, device_id=0, chunk_pages=8)
+    try:
+        gpu_ids = np.array([1, 3, 5, 7, 9, 11, 13, 15, 17, 19], dtype=np.int64)
+        cpu_ids = gpu_ids + 40
+        h.gpu_to_cpu_handler.transfer_async(1, (gpu_ids, cpu_ids))
+        h.gpu_to_cpu_handler.wait({1})
+        padded = torch.zeros(len(gpu_ids), coded, dtype=torch.bfloat16, device="cuda")
+        padded[:, :n] = kv[torch.as_tensor(gpu_ids)].view(len(gpu_ids), -1)
+        w = _plain_wrapper(cpp, 1e-4)
+        outs = [torch.empty(w.estimate_compressed_buffer_size(coded * 4), dtype=torch.uint8,
+                            device="cuda") for _ in gpu_ids]
+        ok, sizes, bounds = w.compress_batch_fixed_bf16(list(padded), outs, [1e-4] * len(gpu_ids))
+        assert ok
+        for k, cpu in enumerate(cpu_ids):
+            seg = h.store.get(int(cpu)).segments[0]
+            assert seg.encoding == "cuszp" and seg.compressed_numel == coded
+            assert seg.compressed_size == sizes[k]
+            assert np.float32(seg.actual_error_bound) == np.float32(bounds[k])
+            assert torch.equal(seg.payload, outs[k][: sizes[k]].cpu())
+        dst = gpu_ids - 1
+        kv[torch.as_tensor(dst)] = 0
+        h.cpu_to_gpu_handler.transfer_async(2, (cpu_ids, dst))
+        h.cpu_to_gpu_handler.wait({2})
+        restored = torch.zeros(len(gpu_ids) * coded, dtype=torch.bfloat16, device="cuda")
+        assert w.decompress_batch_fixed_bf16(outs, sizes, restored, coded, bounds)
+        torch.cuda.synchronize()
+        restored = restored.view(len(gpu_ids), coded)[:, :n]
+        for k, d in enumerate(dst):
+            assert torch.equal(kv[d].view(-1).view(torch.int16), restored[k].view(torch.int16))
+    finally:
+        h.shutdown()
+
+
+@pytest.mark.gpu
+def test_handlers_layer_groups_with_a_raw_segment():
+    """A layer segment that does not compress is stored raw; the page's
+    other segment keeps the indexed call's bytes; the load restores both."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    import cuszp_wrapper_cpp as cpp
+
+    shape = (2, 28, 2, 16, 128)
+    layers, prefix, epl = 28, 2, 2 * 16 * 128
+    low = [0, 1, 2, 5, 19, 20, 21]
+    high = [i for i in range(layers) if i not in low]
+    kv = _kv(12, shape, seed=24).cuda()
+    g = torch.Generator().manual_seed(25)
+    # page 1's low-bound layers: uniform noise (incompressible at 1e-5)
+    noise = (torch.rand(2, len(low), 2, 16, 128, generator=g) * 2 - 1).to(torch.bfloat16).cuda()
+    kv[1][:, low] = noise
+    snapshot = kv.clone()
+    bounds_of = {i: (1e-5 if i in low else 1e-4) for i in range(layers)}
+    h = ko.CompressedCpuGpuOffloadingHandlers(kv, error_bound=1e-4, device_id=0, chunk_pages=2,
+                                              layer_bounds=bounds_of)
+    try:
+        gpu_ids = np.array([0, 1, 2, 3], dtype=np.int64)
+        cpu_ids = gpu_ids + 70
+        h.gpu_to_cpu_handler.transfer_async(1, (gpu_ids, cpu_ids))
+        h.gpu_to_cpu_handler.wait({1})
+        seg = h.store.get(71).segments[0]
+        assert seg.encoding == "raw" and seg.actual_error_bound == 0.0
+        assert torch.equal(seg.payload, kv[1][:, low].contiguous().view(-1).view(torch.uint8).cpu())
+        assert h.store.get(71).segments[1].encoding == "cuszp"
+        assert all(s.encoding == "cuszp" for c in (70, 72, 73) for s in h.store.get(c).segments)
+
+        w = _plain_wrapper(cpp, 1e-4)
+        want = torch.zeros(len(gpu_ids), kv[0].numel(), dtype=torch.bfloat16, device="cuda")
+        for gi, (eb, sel) in enumerate([(1e-5, low), (1e-4, high)]):
+            index = torch.tensor(sel, device="cuda")
+            pages = [kv[i].view(-1) for i in gpu_ids]
+            outs = [torch.empty(w.estimate_compressed_buffer_size(prefix * len(sel) * epl * 4),
+                                dtype=torch.uint8, device="cuda") for _ in pages]
+            ok, sizes, bounds = w.compress_batch_fixed_bf16_indexed(
+                pages, outs, index, prefix, layers, epl, [eb] * len(pages))
+            assert ok
+            assert w.decompress_batch_fixed_bf16_indexed_scatter(
+                outs, sizes, list(want), index, prefix, layers, epl, bounds)
+        torch.cuda.synchronize()
+        want[1].view(prefix, layers, epl)[:, low] = snapshot[1].view(prefix, layers, epl)[:, low]
+        dst = np.array([8, 9, 10, 11], dtype=np.int64)
+        kv[8:12] = 0
+        h.cpu_to_gpu_handler.transfer_async(2, (cpu_ids, dst))
+        h.cpu_to_gpu_handler.wait({2})
+        torch.cuda.synchronize()
+        for k, d in enumerate(dst):
+            assert torch.equal(kv[d].view(-1).view(torch.int16), want[k].view(torch.int16)), k
     finally:
         h.shutdown()
