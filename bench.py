@@ -35,6 +35,7 @@ from __future__ import annotations
 
 import argparse
 import ctypes as C
+import gc
 import json
 import os
 import statistics
@@ -211,7 +212,7 @@ class ClockSampler:
 def cpu_baseline(host_pages: torch.Tensor, reps: int = 1) -> dict:
     from oracle.oracle import COracle, capacity_for
     co = COracle()
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or 1
     bits = host_pages.view(torch.int16).numpy().view(np.uint16)
     pages = [np.ascontiguousarray(bits[i]) for i in range(bits.shape[0])]
     n = pages[0].size
@@ -286,7 +287,7 @@ def codec_baselines(host_pages: torch.Tensor, pages_dev: torch.Tensor, sample: i
                      f"all {pages_dev.shape[0]} pages (GPU INT8)"}
     pages = [np.ascontiguousarray(host_pages[i].view(torch.int16).numpy()) for i in range(sample)]
     raw = sum(p.nbytes for p in pages)
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or 1
     for name, (bound, comp, decomp) in _load_c_codecs().items():
         cap = bound(pages[0].nbytes)
         bufs = [np.empty(cap, dtype=np.uint8) for _ in pages]
@@ -569,20 +570,28 @@ class RefCodec:
 
 def timed_steps(fn, steps: int, flush: torch.Tensor, device, after=None):
     """Per-step CUDA-event times (ms) and fn's results; L2 flushed before
-    every step, outside the timed events."""
+    every step, outside the timed events.  The collector is paused meanwhile:
+    a collection between the compress call's return and the decompress
+    launch would stall the device for its whole length."""
     stream = torch.cuda.current_stream(device)
     times, results = [], []
-    for _ in range(steps):
-        flush.zero_()
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        results.append(fn())
-        end.record(stream)
-        end.synchronize()
-        times.append(start.elapsed_time(end))
-        if after is not None:
-            after()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+    collect = gc.isenabled()
+    gc.disable()
+    try:
+        for start, end in events:
+            flush.zero_()
+            start.record(stream)
+            results.append(fn())
+            end.record(stream)
+            end.synchronize()
+            if after is not None:
+                after()
+    finally:
+        if collect:
+            gc.enable()
+    times = [start.elapsed_time(end) for start, end in events]
     return times, results
 
 
@@ -966,6 +975,20 @@ def raw_pcie_duplex(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, de
     return sum(times) / 1e3
 
 
+def bind_host_threads(physical: int):
+    """Keeps this rank's host threads (and the page-locked memory they touch
+    first) on the CPUs NVML names as closest to its GPU; with one process per
+    GPU the ranks otherwise share and migrate across sockets.  Sets nothing
+    on the GPU.  Returns the CPUs kept, or None."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        pynvml.nvmlDeviceSetCpuAffinity(pynvml.nvmlDeviceGetHandleByIndex(physical))
+        return len(os.sched_getaffinity(0))
+    except Exception:   # no NVML or no affinity information: leave the threads as they are
+        return None
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -997,6 +1020,10 @@ def main() -> int:
                                 device_id=torch.device("cuda", local))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v for v in visible.split(",") if v.strip()]
+    physical = int(ids[local]) if len(ids) > local and ids[local].strip().isdigit() else local
+    affinity = bind_host_threads(physical) if world > 1 else None
 
     impl = args.impl
     ref_note = None
@@ -1055,9 +1082,6 @@ def main() -> int:
 
     barrier()
     launches0 = codec.launches()
-    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    ids = [v for v in visible.split(",") if v.strip()]
-    physical = int(ids[local]) if len(ids) > local and ids[local].strip().isdigit() else local
     with ClockSampler(device, physical) as clocks:
         step_ms, _ = timed_steps(codec.step, args.steps, flush, device, after=kernel_times)
         barrier()
@@ -1131,6 +1155,7 @@ def main() -> int:
             "error_bound": EPS, "relative": True,
             "l2_flush": "256 MB write between timed steps",
             "parallelism": "one process per GPU, pages sharded, no data-path collective",
+            "host_cpus_per_rank": affinity,
         },
         "compression_ratio": round(raw_bytes / compressed, 4),
         "store_restore_ok": ok,
