@@ -101,7 +101,8 @@ class JobHeader:
 
     Layout (little-endian): magic b"CKVJ", u16 version, u16 element type
     (0 BF16), u32 page count, u64 elements per page, u64 payload bytes, f32
-    requested bound, u32 flags (bit 0: relative bound), u32 segments per
+    requested bound, u32 flags (bit 0: relative bound; bits 1-2: codec, 0 cuSZp
+    fixed mode, 1 INT8, 2 raw), u32 segments per
     page (G), u32 layer prefix count, u32 source layers (L; 0 when G = 1),
     u64 elements per coded page (G = 1: the page zero-padded to the codec's
     minimum, MIN_CUSZP_ELEMENTS; 0 when G > 1).  When G > 1 a layer table
@@ -111,12 +112,15 @@ class JobHeader:
     bound, u32 flags (bit 0: the entry holds the raw BF16 bytes); the payload
     starts at the next 256-byte boundary.  A segment of G > 1 holds the
     page's layers of that segment, in ascending layer order, as
-    compress_batch_fixed_bf16_indexed encodes them (or their raw bytes).
+    compress_batch_fixed_bf16_indexed encodes them (or their raw bytes).  An
+    INT8 entry is the page's n int8 values and its FP32 scale at byte
+    align4(n) (its bound field is 0: the scale is in the payload).
     """
 
     MAGIC = b"CKVJ"
     VERSION = 3
     RAW = 1
+    CODECS = ("cuszp", "int8", "raw")
     _HEAD = struct.Struct("<4sHHIQQfIIIIQ")
     _PAGE = np.dtype([("offset", "<u8"), ("size", "<u8"), ("bound", "<f4"), ("flags", "<u4")])
 
@@ -132,7 +136,7 @@ class JobHeader:
     @classmethod
     def write(cls, slab: torch.Tensor, n: int, eps: float, relative: bool, offsets, sizes,
               bounds, payload_bytes: int, groups=None, prefix: int = 0,
-              layers: int = 0, raw=None, coded: int = 0) -> None:
+              layers: int = 0, raw=None, coded: int = 0, codec: str = "cuszp") -> None:
         """`groups`: None for whole pages, else [(requested bound, layer
         indices)] per segment, the pages viewed as [prefix, layers, n /
         (prefix * layers)].  `raw`: per entry, whether it holds raw bytes.
@@ -142,7 +146,8 @@ class JobHeader:
         buf = slab[: cls.bytes_for(count, segs, layers)].numpy()
         buf[: cls._HEAD.size] = np.frombuffer(
             cls._HEAD.pack(cls.MAGIC, cls.VERSION, 0, count, n, payload_bytes, eps,
-                           1 if relative else 0, segs, prefix if segs > 1 else 0,
+                           (1 if relative else 0) | (cls.CODECS.index(codec) << 1), segs,
+                           prefix if segs > 1 else 0,
                            layers if segs > 1 else 0, (coded or n) if segs == 1 else 0),
             dtype=np.uint8)
         start = cls._HEAD.size
@@ -199,9 +204,17 @@ class JobHeader:
         seg_elems = ([n] if segs == 1 else
                      [prefix * len(sel) * (n // (prefix * layers)) for _b, sel in groups])
         want = np.tile(np.asarray(seg_elems, dtype=np.uint64) * 2, count)
+        codec_id = (flags >> 1) & 3
+        if codec_id >= len(cls.CODECS) or (codec_id and segs != 1):
+            raise ValueError("bad codec")
+        codec = cls.CODECS[codec_id]
+        if codec == "raw":
+            raw_entries = np.ones(count, dtype=bool)
         if np.any(raw_entries & (table["size"] != want)):
             raise ValueError("raw entry of the wrong size")
-        return {"count": count, "n": n, "eps": eps, "relative": bool(flags & 1),
+        if codec == "int8" and np.any(table["size"] != (n + 3) // 4 * 4 + 4):
+            raise ValueError("INT8 entry of the wrong size")
+        return {"count": count, "n": n, "eps": eps, "relative": bool(flags & 1), "codec": codec,
                 "segments": segs, "prefix": prefix, "layers": layers, "groups": groups,
                 "coded": coded, "payload_at": hdr, "payload_bytes": payload,
                 "offsets": table["offset"].astype(np.uint64),
@@ -341,9 +354,15 @@ class _Engine:
     reference's batched path pads them (:904-909)."""
 
     def __init__(self, kv_cache: torch.Tensor, error_bound: float, device_id: int,
-                 chunk_pages: int, layer_bounds=None, layer_prefix: int = 2):
+                 chunk_pages: int, layer_bounds=None, layer_prefix: int = 2,
+                 codec: str = "cuszp"):
         if kv_cache.dtype != torch.bfloat16 or not kv_cache.is_cuda or not kv_cache.is_contiguous():
             raise ValueError("kv_cache must be a contiguous BF16 CUDA tensor [num_blocks, ...]")
+        if codec not in JobHeader.CODECS:
+            raise ValueError(f"unsupported offload codec: {codec}")
+        if codec != "cuszp" and layer_bounds is not None:
+            raise ValueError("layer bounds apply to the cuSZp codec only")
+        self.codec = codec
         self.lib = _ckv.load()
         self.kv = kv_cache
         self.device = kv_cache.device
@@ -351,7 +370,8 @@ class _Engine:
         self.page_bytes = self.n * 2
         self.error_bound = float(error_bound)
         self._set_groups(layer_bounds, int(layer_prefix))
-        self.coded = max(self.n, MIN_CUSZP_ELEMENTS) if self.groups is None else self.n
+        self.coded = (max(self.n, MIN_CUSZP_ELEMENTS)
+                      if self.groups is None and codec == "cuszp" else self.n)
         self.ctx = C.c_void_p()
         cfg = _ckv.Config(self.error_bound, 1, _ckv.DIM_1D, _ckv.MODE_FIXED, _ckv.TYPE_FLOAT)
         self._check(self.lib.ckv_create(cfg, int(device_id), C.byref(self.ctx)), "ckv_create")
@@ -418,6 +438,10 @@ class _Engine:
         return (C.c_void_p * len(addrs)).from_buffer_copy(addrs.astype(np.uint64).tobytes())
 
     def host_capacity(self, count: int) -> int:
+        if self.codec == "int8":
+            return int(self.lib.ckv_pipe_host_capacity_int8(count, self.n))
+        if self.codec == "raw":
+            return int(self.lib.ckv_pipe_host_capacity_raw(count, self.page_bytes))
         if self.groups is None:
             return int(self.lib.ckv_pipe_host_capacity(count, self.coded))
         return int(self.lib.ckv_pipe_host_capacity_groups(count, self.sel, self.segments,
@@ -425,7 +449,17 @@ class _Engine:
 
     def store(self, pages: C.Array, count: int, eps: float, host: int, cap: int, offsets,
               sizes, bounds, total, after: int, ticket, stream: int) -> None:
-        if self.groups is None:
+        if self.codec == "int8":
+            self._check(self.lib.ckv_pipe_store_int8(
+                self.pipe, pages, count, self.n, host, cap, offsets, sizes, total, after, ticket,
+                stream), "store")
+        elif self.codec == "raw":
+            self._check(self.lib.ckv_pipe_store_raw(
+                self.pipe, pages, count, self.page_bytes, host, cap, offsets, total, after, ticket,
+                stream), "store")
+            for i in range(count):
+                sizes[i] = self.page_bytes
+        elif self.groups is None:
             self._check(self.lib.ckv_pipe_store_bf16(
                 self.pipe, pages, (C.c_float * count)(*([eps] * count)), count, self.coded, host,
                 cap, offsets, sizes, bounds, total, after, ticket, stream), "store")
@@ -461,6 +495,19 @@ class _Engine:
         covers all of it."""
         G, count = self.segments, len(dst)
         sptr = stream.cuda_stream
+        if self.codec != "cuszp":
+            t = C.c_uint64(0)
+            offs = (C.c_size_t * count)(*[int(o) for o in offsets])
+            ptrs = _ckv.ptr_array([d.data_ptr() for d in dst])
+            if self.codec == "int8":
+                self._check(self.lib.ckv_pipe_restore_int8(
+                    self.pipe, payload.data_ptr(), offs, count, self.n, ptrs, after, C.byref(t),
+                    sptr), "restore")
+            else:
+                self._check(self.lib.ckv_pipe_restore_raw(
+                    self.pipe, payload.data_ptr(), offs, count, self.page_bytes, ptrs, after,
+                    C.byref(t), sptr), "restore")
+            return t.value
         offsets = np.asarray(offsets, dtype=np.uint64).reshape(count, G)
         sizes = np.asarray(sizes, dtype=np.uint64).reshape(count, G)
         bounds = np.asarray(bounds, dtype=np.float32).reshape(count, G)
@@ -567,6 +614,7 @@ class CompressedOffloadingHandler:
         self._pending: dict[int, tuple[list[int], int]] = {}   # job -> (tickets, bytes)
         self._finished: list[TransferResult] = []
         self._lock = threading.Lock()
+        self._finalize: dict[int, list] = {}   # INT8 store ticket -> its page entries
 
     def _components(self, g: int) -> tuple[BundleComponent, ...]:
         e = self.engine
@@ -606,8 +654,9 @@ class CompressedOffloadingHandler:
         # stored raw, with bound 0 (vllm_v1_compressed_offload.py:1000-1010): its
         # raw bytes fit where its longer stream was packed.
         seg_bytes = [2 * e.segment_numel(g) for g in range(G)]
-        raw = [int(sizes[j]) >= seg_bytes[j % G] for j in range(count * G)]
-        if any(raw):
+        raw = [e.codec == "raw" or (e.codec == "cuszp" and int(sizes[j]) >= seg_bytes[j % G])
+               for j in range(count * G)]
+        if e.codec == "cuszp" and any(raw):
             e.join(final, stream.cuda_stream)
             with torch.cuda.stream(stream):
                 for j in (j for j in range(count * G) if raw[j]):
@@ -620,7 +669,8 @@ class CompressedOffloadingHandler:
             final = e.record(stream.cuda_stream)
         slab.ticket = final
         JobHeader.write(slab.buffer, e.n, self.error_bound, True, offsets, sizes, bounds,
-                        total.value, e.groups, e.prefix, e.layers, raw=raw, coded=e.coded)
+                        total.value, e.groups, e.prefix, e.layers, raw=raw, coded=e.coded,
+                        codec=e.codec)
         comps = [self._components(g) for g in range(G)]
         req = [self.error_bound] if e.groups is None else [b for b, _sel in e.groups]
         entries = []
@@ -635,13 +685,15 @@ class CompressedOffloadingHandler:
                 numel = e.segment_numel(g)
                 coded = e.coded if e.groups is None else numel
                 payload = slab.buffer[hdr + rec.offsets[g]: hdr + rec.offsets[g] + rec.sizes[g]]
-                segs.append(EncodedSegment(payload, rec.sizes[g], rec.bounds[g],
-                                           "raw" if rec.raw[g] else "cuszp", comps[g], numel,
-                                           coded, numel * 2, req[g],
-                                           cuszp_mode=None if rec.raw[g] else "fixed"))
+                encoding = "raw" if rec.raw[g] else e.codec
+                segs.append(EncodedSegment(payload, rec.sizes[g], rec.bounds[g], encoding,
+                                           comps[g], numel, coded, numel * 2, req[g],
+                                           cuszp_mode="fixed" if encoding == "cuszp" else None))
             entries.append((int(cpu_ids[i]),
                             rec, CompressedBundle(tuple(segs), sum(rec.sizes), e.page_bytes)))
         self.store.put_many_packed(entries)
+        if e.codec == "int8":
+            self._finalize[final] = entries
         return [final], int(total.value)
 
     def _load(self, cpu_ids: np.ndarray, gpu_ids: np.ndarray) -> tuple[list[int], int]:
@@ -698,6 +750,8 @@ class CompressedOffloadingHandler:
                 if all(s != 0 for s in states):
                     done.append((job_id, all(s == 1 for s in states), nbytes))
             for job_id, ok, nbytes in done:
+                for t in self._pending[job_id][0]:
+                    self._scales(t)
                 del self._pending[job_id]
                 self._finished.append(TransferResult(job_id, ok, nbytes,
                                                      transfer_type=self.transfer_type))
@@ -710,6 +764,24 @@ class CompressedOffloadingHandler:
             tickets = [t for j in job_ids for t in self._pending.get(int(j), ([], 0))[0]]
         for t in tickets:
             self.engine._check(lib.ckv_pipe_wait(pipe, t), "wait")
+            with self._lock:
+                self._scales(t)
+
+    def _scales(self, ticket: int) -> None:
+        """Once an INT8 store has landed: each page's FP32 scale (at byte
+        align4(n) of its stored form) into its metadata, and the bound the
+        reference records for it, scale / 2 (vllm_v1_compressed_offload.py:
+        711-724)."""
+        entries = self._finalize.pop(ticket, None)
+        if not entries:
+            return
+        at = (self.engine.n + 3) // 4 * 4
+        for _cpu, rec, bundle in entries:
+            seg = bundle.segments[0]
+            scale = float(np.frombuffer(seg.payload[at:at + 4].numpy().tobytes(), dtype="<f4")[0])
+            seg.quant_scale = scale
+            seg.actual_error_bound = scale / 2.0
+            rec.bounds = (scale / 2.0,)
 
     def shutdown(self) -> None:
         with self._lock:
@@ -723,12 +795,15 @@ class CompressedCpuGpuOffloadingHandlers:
     `layer_bounds` / `layer_prefix`: a fixed per-layer bound assignment (the
     reference's calibrated mixed profiles, e.g. 1e-5 on a few sensitive
     layers and 1e-4 on the rest), stored as one segment per distinct bound
-    (see ``_Engine``)."""
+    (see ``_Engine``).  `codec`: "cuszp" (fixed mode), or the reference
+    connector's GPU comparison codecs "int8" (per-page absmax / 127) and
+    "raw" (vllm_v1_compressed_offload.py:508-511)."""
 
     def __init__(self, kv_cache: torch.Tensor, error_bound: float = 1e-4, device_id: int = 0,
-                 chunk_pages: int = 64, layer_bounds=None, layer_prefix: int = 2):
+                 chunk_pages: int = 64, layer_bounds=None, layer_prefix: int = 2,
+                 codec: str = "cuszp"):
         self.engine = _Engine(kv_cache, error_bound, device_id, chunk_pages, layer_bounds,
-                              layer_prefix)
+                              layer_prefix, codec)
         self.store = CompressedPageStore()
         self.gpu_to_cpu_handler = CompressedOffloadingHandler(self.engine, self.store, True)
         self.cpu_to_gpu_handler = CompressedOffloadingHandler(self.engine, self.store, False)
@@ -746,6 +821,8 @@ def restore_job(slab: torch.Tensor, dst_pages: Sequence[torch.Tensor], engine: _
     job = JobHeader.read(slab)
     if job["n"] != engine.n or len(dst_pages) != job["count"]:
         raise ValueError("job does not match the destination pages")
+    if job["codec"] != engine.codec:
+        raise ValueError(f"job stored with the {job['codec']} codec, engine uses {engine.codec}")
     same = job["segments"] == engine.segments and (
         (engine.groups is None and job["coded"] == engine.coded) or
         (engine.groups is not None and

@@ -101,6 +101,27 @@ def test_job_header_raw_entries():
     assert job["coded"] == 36864 and job["n"] == 8192
 
 
+def test_job_header_codecs():
+    count, n = 2, 8192
+    offsets = (C.c_size_t * count)(0, 8208)
+    sizes = (C.c_size_t * count)(n + 4, n + 4)
+    bounds = (C.c_float * count)(0.0, 0.0)
+    hdr = ko.JobHeader.bytes_for(count)
+    slab = torch.zeros(hdr + 16416, dtype=torch.uint8)
+    ko.JobHeader.write(slab, n, 1e-4, True, offsets, sizes, bounds, 16416, codec="int8")
+    assert ko.JobHeader.read(slab)["codec"] == "int8"
+    sizes[1] = n + 8
+    ko.JobHeader.write(slab, n, 1e-4, True, offsets, sizes, bounds, 16416, codec="int8")
+    with pytest.raises(ValueError):
+        ko.JobHeader.read(slab)                 # an INT8 page is n + 4 bytes
+    sizes[0] = sizes[1] = 2 * n
+    offsets[1] = 2 * n
+    slab = torch.zeros(hdr + 4 * n, dtype=torch.uint8)
+    ko.JobHeader.write(slab, n, 1e-4, True, offsets, sizes, bounds, 4 * n, codec="raw")
+    job = ko.JobHeader.read(slab)
+    assert job["codec"] == "raw" and job["raw"].tolist() == [True, True]
+
+
 def test_layer_bounds_group_like_the_reference():
     """Segments are the distinct bounds in ascending order, each with its
     layers in ascending order; missing layers take the handler's bound."""
@@ -492,5 +513,57 @@ def test_handlers_layer_groups_with_a_raw_segment():
         torch.cuda.synchronize()
         for k, d in enumerate(dst):
             assert torch.equal(kv[d].view(-1).view(torch.int16), want[k].view(torch.int16)), k
+    finally:
+        h.shutdown()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("codec", ["int8", "raw"])
+def test_handlers_comparison_codecs(codec):
+    """The connector's INT8 and raw codecs through the handlers: INT8 pages
+    restore to what the reference's torch expression gives on the GPU
+    (vllm_v1_compressed_offload.py:711-724, 2090-2116) and carry its scale
+    and bound once stored; raw pages restore bit for bit."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    shape = (2, 28, 2, 16, 128)
+    kv = _kv(20, shape, seed=31).cuda()
+    snapshot = kv.clone()
+    h = ko.CompressedCpuGpuOffloadingHandlers(kv, error_bound=1e-4, device_id=0, chunk_pages=4,
+                                              codec=codec)
+    try:
+        gpu_ids = np.arange(0, 10, dtype=np.int64)
+        cpu_ids = gpu_ids + 900
+        h.gpu_to_cpu_handler.transfer_async(1, (gpu_ids, cpu_ids))
+        h.gpu_to_cpu_handler.wait({1})
+        assert [r.success for r in h.gpu_to_cpu_handler.get_finished()] == [True]
+        x = snapshot[:10].view(10, -1).float()
+        if codec == "int8":
+            scale = x.abs().amax(dim=1, keepdim=True) / 127.0
+            scale = torch.where(scale == 0, torch.ones_like(scale), scale)
+            q = torch.clamp(torch.round(x / scale), -127, 127).to(torch.int8)
+            want = (q.to(torch.float32) * scale).to(torch.bfloat16)
+            for k, cpu in enumerate(cpu_ids):
+                seg = h.store.get(int(cpu)).segments[0]
+                assert seg.encoding == "int8" and seg.compressed_size == kv[0].numel() + 4
+                assert np.float32(seg.quant_scale) == np.float32(scale[k].item())
+                assert seg.actual_error_bound == seg.quant_scale / 2.0
+                assert torch.equal(seg.payload[:kv[0].numel()].view(torch.int8), q[k].cpu())
+        else:
+            want = snapshot[:10].view(10, -1)
+            for cpu in cpu_ids:
+                seg = h.store.get(int(cpu)).segments[0]
+                assert seg.encoding == "raw" and seg.compressed_size == 2 * kv[0].numel()
+        dst = np.arange(10, 20, dtype=np.int64)
+        kv[10:20] = 0
+        h.cpu_to_gpu_handler.transfer_async(2, (cpu_ids, dst))
+        h.cpu_to_gpu_handler.wait({2})
+        torch.cuda.synchronize()
+        assert torch.equal(kv[10:20].view(10, -1).view(torch.int16), want.view(torch.int16))
+        slab = h.store.slab(h.store.record(int(cpu_ids[0])).slab).buffer
+        pages = [torch.zeros(kv[0].numel(), dtype=torch.bfloat16, device="cuda") for _ in gpu_ids]
+        t = ko.restore_job(slab, pages, h.engine)
+        assert h.engine.lib.ckv_pipe_wait(h.engine.pipe, t) == 0
+        assert torch.equal(torch.stack(pages).view(torch.int16), want.view(torch.int16))
     finally:
         h.shutdown()
