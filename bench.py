@@ -687,6 +687,66 @@ def pipeline_codecs(codec, steps: int, flush: torch.Tensor, device) -> dict:
     return out
 
 
+def c1_leg(codec, steps: int, flush: torch.Tensor, device) -> dict:
+    """C1: one layer's K and V of 64 pages, 8192
+    BF16 each (K, V ~ N(0,1) x LogNormal(0, 0.5) per (head, channel),
+    seeded), REL 1e-4, compressed and decompressed through the C ABI; and
+    the same pages zero-padded to 36864 elements, the unit the reference's
+    connector would compress (vllm_v1_compressed_offload.py:49, 904-909)."""
+    lib, ck = codec.lib, codec.ckv
+    g = torch.Generator().manual_seed(0)
+    scale = torch.empty(2, HEADS, HEAD_DIM).log_normal_(0.0, 0.5, generator=g)
+    x = torch.randn(64, 2, TOKENS, HEADS, HEAD_DIM, generator=g) * scale[None, :, None, :, :]
+    pages8k = x.to(torch.bfloat16).view(64, -1).to(device)
+    out = {}
+    for label, n in (("n8192", 8192), ("padded36864", 36864)):
+        pages = torch.zeros(64, n, dtype=torch.bfloat16, device=device)
+        pages[:, :8192] = pages8k
+        cap = int(lib.ckv_estimate_compressed_buffer_size(n * 4))
+        slab = torch.zeros(64 * cap, dtype=torch.uint8, device=device)
+        restored = torch.zeros_like(pages)
+        ins = ck.ptr_array([pages[i].data_ptr() for i in range(64)])
+        outs = ck.ptr_array([slab.data_ptr() + i * cap for i in range(64)])
+        dsts = ck.ptr_array([restored[i].data_ptr() for i in range(64)])
+        eps = (C.c_float * 64)(*([1e-4] * 64))
+        sizes, bounds = (C.c_size_t * 64)(), (C.c_float * 64)()
+        s = torch.cuda.current_stream(device).cuda_stream
+        enc_ms, dec_ms = [], []
+
+        def step():
+            codec._check(lib.ckv_compress_batch_fixed_bf16(codec.ctx, ins, outs, eps, 64, n, cap,
+                                                           sizes, bounds, s), "c1 compress")
+            codec._check(lib.ckv_decompress_batch_fixed_bf16_scatter(
+                codec.ctx, outs, sizes, 64, dsts, 64, n, 1, n, bounds, s), "c1 decompress")
+
+        def kernel_times():
+            enc_ms.append(codec.kernel_ms(0))
+            dec_ms.append(codec.kernel_ms(1))
+
+        for _ in range(3):
+            step()
+        times, _ = timed_steps(step, steps, flush, device, after=kernel_times)
+        torch.cuda.synchronize(device)
+        raw = 64 * n * 2
+        comp = int(sum(sizes))
+        b = torch.tensor(list(bounds), device=device).view(-1, 1)
+        ok = bool(((pages.float() - restored.float()).abs() <=
+                   b * 1.01 + 1e-7 + pages.float().abs() * 2.0 ** -8).all())
+        enc, dec = statistics.mean(enc_ms) / 1e3, statistics.mean(dec_ms) / 1e3
+        out[label] = {
+            "value_gbps": round(job_rate(1, raw, steps, sum(times) / 1e3), 3),
+            "compression_ratio": round(raw / comp, 4),
+            "ratio_of_the_8192_elements": round(64 * 8192 * 2 / comp, 4),
+            "encode_ms": round(enc * 1e3, 4), "decode_ms": round(dec * 1e3, 4),
+            "encode_gbps": round((raw + comp) / enc / 1e9, 2),
+            "decode_gbps": round((raw + comp) / dec / 1e9, 2),
+            "round_trip_ok": ok,
+        }
+    out["workload"] = ("C1: 64 pages x [K,V][16 tokens][2 heads][128] = 8192 BF16, REL 1e-4, "
+                       "compress + decompress per step (1 MiB); L2 flushed between steps")
+    return out
+
+
 C3_LOW_LAYERS = (0, 1, 2, 5, 19, 20, 21)   # 1e-5; the other 21 layers at 1e-4
 
 
@@ -1102,6 +1162,8 @@ def main() -> int:
     ok = ok and codec.verify()
     piped = (pipeline_codecs(codec, min(args.steps, 10), flush, device)
              if impl == "ours" and pipelined and rank == 0 else None)
+    c1 = (c1_leg(codec, min(args.steps, 10), flush, device)
+          if impl == "ours" and pipelined and rank == 0 else None)
     c3 = (layer_groups_c3(codec, min(args.steps, 10), flush, device,
                           chunk_pages=args.chunk_pages)
           if impl == "ours" and pipelined and rank == 0 and not args.no_c3 else None)
@@ -1202,6 +1264,7 @@ def main() -> int:
         }
         line["kernels"] = kernels
         line["pipeline_codecs"] = piped
+        line["c1"] = c1
         line["layer_groups_c3"] = c3
         if streamed:
             line["streamed"] = streamed
