@@ -349,13 +349,19 @@ class _Engine:
     ``[layer_prefix, len(layer_bounds), n / (layer_prefix * layers)]`` and
     stored as one segment per distinct bound, in ascending bound order (the
     reference's ``sorted(grouped.items())``); layers missing from the mapping
-    take `error_bound`.  One distinct bound leaves whole pages.  Whole pages
-    smaller than MIN_CUSZP_ELEMENTS are coded zero-padded to it, as the
-    reference's batched path pads them (:904-909)."""
+    take `error_bound`.  One distinct bound leaves whole pages.  Layers of
+    bound zero form a segment stored raw (:1381-1409), and a zero bound for
+    whole pages stores them raw (:639-656).  Whole pages smaller than
+    MIN_CUSZP_ELEMENTS are coded zero-padded to it, as the reference's batched
+    path pads them (:904-909).  A KV cache with byte backing storage (uint8 /
+    int8) is read as the BF16 pages it holds (:1330-1334)."""
 
     def __init__(self, kv_cache: torch.Tensor, error_bound: float, device_id: int,
                  chunk_pages: int, layer_bounds=None, layer_prefix: int = 2,
                  codec: str = "cuszp"):
+        if kv_cache.dtype in (torch.uint8, torch.int8) and kv_cache.is_contiguous():
+            # byte backing storage of BF16 pages (vllm_v1_compressed_offload.py:1330-1334)
+            kv_cache = kv_cache.view(torch.uint8).view(kv_cache.shape[0], -1).view(torch.bfloat16)
         if kv_cache.dtype != torch.bfloat16 or not kv_cache.is_cuda or not kv_cache.is_contiguous():
             raise ValueError("kv_cache must be a contiguous BF16 CUDA tensor [num_blocks, ...]")
         if codec not in JobHeader.CODECS:
@@ -370,10 +376,14 @@ class _Engine:
         self.page_bytes = self.n * 2
         self.error_bound = float(error_bound)
         self._set_groups(layer_bounds, int(layer_prefix))
+        if self.codec == "cuszp" and self.groups is None and self.error_bound <= 0:
+            self.codec = "raw"   # a zero bound stores raw bytes (:639-656)
         self.coded = (max(self.n, MIN_CUSZP_ELEMENTS)
-                      if self.groups is None and codec == "cuszp" else self.n)
+                      if self.groups is None and self.codec == "cuszp" else self.n)
         self.ctx = C.c_void_p()
-        cfg = _ckv.Config(self.error_bound, 1, _ckv.DIM_1D, _ckv.MODE_FIXED, _ckv.TYPE_FLOAT)
+        # (the context's bound is a default only: every call passes its bounds)
+        cfg = _ckv.Config(self.error_bound if self.error_bound > 0 else 1e-4, 1, _ckv.DIM_1D,
+                          _ckv.MODE_FIXED, _ckv.TYPE_FLOAT)
         self._check(self.lib.ckv_create(cfg, int(device_id), C.byref(self.ctx)), "ckv_create")
         self.pipe = C.c_void_p()
         self._check(self.lib.ckv_pipe_create(self.ctx, int(chunk_pages), C.byref(self.pipe)),
@@ -397,25 +407,26 @@ class _Engine:
             raise ValueError("page does not split into [layer_prefix, layers, elements] rows")
         grouped: dict[float, list[int]] = {}
         for layer, bound in enumerate(bound_of):
-            grouped.setdefault(bound, []).append(layer)
-        if any(b <= 0 for b in grouped):
-            raise ValueError("layer bounds must be positive (raw layer segments are not stored)")
+            grouped.setdefault(max(bound, 0.0), []).append(layer)
         if len(grouped) == 1:
+            # one bound: whole pages (a zero bound: raw pages)
             self.error_bound = next(iter(grouped))
             return
         groups = [(b, tuple(sel)) for b, sel in sorted(grouped.items())]
         epl = self.n // (prefix * layers)
-        if any(prefix * len(sel) * epl < MIN_CUSZP_ELEMENTS for _b, sel in groups):
+        if any(b > 0 and prefix * len(sel) * epl < MIN_CUSZP_ELEMENTS for b, sel in groups):
             raise ValueError(f"a layer segment is smaller than {MIN_CUSZP_ELEMENTS} elements")
         self.groups = groups
         self.segments = len(groups)
         self.prefix, self.layers, self.epl = prefix, layers, epl
         self._index = [torch.tensor(sel, dtype=torch.int64, device=self.device)
                        for _b, sel in self.groups]
-        G = self.segments
-        self.sel = (C.c_size_t * G)(*[len(sel) for _b, sel in self.groups])
-        self.idx = (C.c_void_p * G)(*[t.data_ptr() for t in self._index])
-        self.eps = (C.c_float * G)(*[b for b, _sel in self.groups])
+        # segments of zero bound are stored raw (:1381-1409); the others through the pipeline
+        self.cg = [g for g, (b, _sel) in enumerate(groups) if b > 0]
+        Gc = len(self.cg)
+        self.sel = (C.c_size_t * Gc)(*[len(groups[g][1]) for g in self.cg])
+        self.idx = (C.c_void_p * Gc)(*[self._index[g].data_ptr() for g in self.cg])
+        self.eps = (C.c_float * Gc)(*[groups[g][0] for g in self.cg])
 
     def segment_numel(self, g: int) -> int:
         return self.n if self.groups is None else self.prefix * len(self.groups[g][1]) * self.epl
@@ -444,8 +455,10 @@ class _Engine:
             return int(self.lib.ckv_pipe_host_capacity_raw(count, self.page_bytes))
         if self.groups is None:
             return int(self.lib.ckv_pipe_host_capacity(count, self.coded))
-        return int(self.lib.ckv_pipe_host_capacity_groups(count, self.sel, self.segments,
-                                                          self.prefix, self.epl))
+        raw = sum((2 * self.segment_numel(g) + 15) // 16 * 16
+                  for g in range(self.segments) if g not in self.cg)
+        return int(self.lib.ckv_pipe_host_capacity_groups(count, self.sel, len(self.cg),
+                                                          self.prefix, self.epl)) + count * raw
 
     def store(self, pages: C.Array, count: int, eps: float, host: int, cap: int, offsets,
               sizes, bounds, total, after: int, ticket, stream: int) -> None:
@@ -464,8 +477,9 @@ class _Engine:
                 self.pipe, pages, (C.c_float * count)(*([eps] * count)), count, self.coded, host,
                 cap, offsets, sizes, bounds, total, after, ticket, stream), "store")
         else:
+            # the compressed segments (entry i * Gc + j); the caller places raw ones
             self._check(self.lib.ckv_pipe_store_bf16_groups(
-                self.pipe, pages, count, self.idx, self.sel, self.segments, self.prefix,
+                self.pipe, pages, count, self.idx, self.sel, len(self.cg), self.prefix,
                 self.layers, self.epl, self.eps, host, cap, offsets, sizes, bounds, total,
                 after, ticket, stream), "store")
 
@@ -522,12 +536,14 @@ class _Engine:
             return ((C.c_size_t * k)(*o.reshape(-1).tolist()), (C.c_size_t * k)(*z.reshape(-1).tolist()),
                     (C.c_float * k)(*b.reshape(-1).tolist()))
 
-        if G == 1 or not raw.any():
-            sel = np.flatnonzero(~raw.any(axis=1))
+        cg = [0] if G == 1 else self.cg
+        comp = ~raw[:, cg]
+        if G == 1 or comp.all():
+            sel = np.flatnonzero(comp.all(axis=1))
             if sel.size:
-                o, z, b = arrays(sel)
                 t = C.c_uint64(0)
                 if G == 1:
+                    o, z, b = arrays(sel)
                     if self.coded > self.n:
                         stage = torch.empty(len(sel), self.coded, dtype=torch.bfloat16,
                                             device=self.device)
@@ -544,22 +560,28 @@ class _Engine:
                             dst[i].copy_(stage[k, :self.n])
                         extra = True
                 else:
+                    k = len(sel) * len(cg)
+                    o = (C.c_size_t * k)(*offsets[sel][:, cg].reshape(-1).tolist())
+                    z = (C.c_size_t * k)(*sizes[sel][:, cg].reshape(-1).tolist())
+                    b = (C.c_float * k)(*bounds[sel][:, cg].reshape(-1).tolist())
                     self._check(self.lib.ckv_pipe_restore_bf16_groups(
-                        self.pipe, base, o, z, b, len(sel), self.idx, self.sel, G, self.prefix,
-                        self.layers, self.epl, _ckv.ptr_array([dst[i].data_ptr() for i in sel]),
-                        after, C.byref(t), sptr), "restore")
+                        self.pipe, base, o, z, b, len(sel), self.idx, self.sel, len(cg),
+                        self.prefix, self.layers, self.epl,
+                        _ckv.ptr_array([dst[i].data_ptr() for i in sel]), after, C.byref(t),
+                        sptr), "restore")
                 tickets.append(t.value)
         else:
-            # some segments are raw: each group's cuSZp segments in a call of their own
-            for g in range(G):
-                sel = np.flatnonzero(~raw[:, g])
+            # some compressed segments were stored raw: each group's cuSZp
+            # segments in a call of their own
+            for j, g in enumerate(cg):
+                sel = np.flatnonzero(comp[:, j])
                 if not sel.size:
                     continue
                 o, z, b = arrays(sel, g)
                 t = C.c_uint64(0)
                 self._check(self.lib.ckv_pipe_restore_bf16_groups(
-                    self.pipe, base, o, z, b, len(sel), (C.c_void_p * 1)(self.idx[g]),
-                    (C.c_size_t * 1)(self.sel[g]), 1, self.prefix, self.layers, self.epl,
+                    self.pipe, base, o, z, b, len(sel), (C.c_void_p * 1)(self.idx[j]),
+                    (C.c_size_t * 1)(self.sel[j]), 1, self.prefix, self.layers, self.epl,
                     _ckv.ptr_array([dst[i].data_ptr() for i in sel]), after, C.byref(t), sptr),
                     "restore")
                 tickets.append(t.value)
@@ -647,14 +669,34 @@ class CompressedOffloadingHandler:
         bounds = (C.c_float * (count * G))()
         total = C.c_size_t(0)
         ticket = C.c_uint64(0)
-        e.store(pages, count, self.error_bound, slab.buffer.data_ptr() + hdr, cap, offsets, sizes,
-                bounds, C.byref(total), slab.readers, C.byref(ticket), stream.cuda_stream)
+        cg = [0] if e.groups is None else e.cg
+        if len(cg) == G:
+            e.store(pages, count, self.error_bound, slab.buffer.data_ptr() + hdr, cap, offsets,
+                    sizes, bounds, C.byref(total), slab.readers, C.byref(ticket), stream.cuda_stream)
+        else:
+            Gc = len(cg)
+            co, cs = (C.c_size_t * (count * Gc))(), (C.c_size_t * (count * Gc))()
+            cb = (C.c_float * (count * Gc))()
+            e.store(pages, count, self.error_bound, slab.buffer.data_ptr() + hdr, cap, co, cs, cb,
+                    C.byref(total), slab.readers, C.byref(ticket), stream.cuda_stream)
+            pos = (total.value + 15) // 16 * 16
+            for i in range(count):
+                for j, g in enumerate(cg):
+                    offsets[i * G + g] = co[i * Gc + j]
+                    sizes[i * G + g] = cs[i * Gc + j]
+                    bounds[i * G + g] = cb[i * Gc + j]
+                for g in (g for g in range(G) if g not in cg):
+                    offsets[i * G + g] = pos
+                    sizes[i * G + g] = 2 * e.segment_numel(g)
+                    pos += (sizes[i * G + g] + 15) // 16 * 16
+            total.value = pos
         final = ticket.value
         # A page (segment) that cuSZp would not shrink below its raw BF16 size is
         # stored raw, with bound 0 (vllm_v1_compressed_offload.py:1000-1010): its
         # raw bytes fit where its longer stream was packed.
         seg_bytes = [2 * e.segment_numel(g) for g in range(G)]
-        raw = [e.codec == "raw" or (e.codec == "cuszp" and int(sizes[j]) >= seg_bytes[j % G])
+        raw = [e.codec == "raw" or (e.codec == "cuszp" and (j % G not in cg or
+                                                             int(sizes[j]) >= seg_bytes[j % G]))
                for j in range(count * G)]
         if e.codec == "cuszp" and any(raw):
             e.join(final, stream.cuda_stream)

@@ -135,8 +135,10 @@ def test_layer_bounds_group_like_the_reference():
     assert list(e.sel) == [7, 21] and e.segment_numel(0) == 2 * 7 * 4096
     e._set_groups([3e-4] * 28, 2)                 # one bound: whole pages
     assert e.groups is None and e.segments == 1 and e.error_bound == 3e-4
+    e._set_groups([1e-4] * 27 + [0.0], 2)         # a zero bound: a raw segment, first
+    assert e.groups[0] == (0.0, (27,)) and e.cg == [1] and list(e.sel) == [27]
     with pytest.raises(ValueError):
-        e._set_groups([1e-4] * 27 + [0.0], 2)     # raw layers are not stored
+        e._set_groups([1e-4] * 27 + [1e-5], 2)    # a compressed segment below 36864 elements
     with pytest.raises(ValueError):
         e._set_groups([1e-4] * 27 + [1e-5], 3)    # page does not split
 
@@ -567,3 +569,51 @@ def test_handlers_comparison_codecs(codec):
         assert torch.equal(torch.stack(pages).view(torch.int16), want.view(torch.int16))
     finally:
         h.shutdown()
+
+
+@pytest.mark.gpu
+def test_handlers_zero_bound_layers_stay_exact():
+    """The reference's mixed policy test (tests/test_vllm_v1_compressed_offload.py:654-716):
+    layers of bound zero are stored raw and restored exactly, the others within
+    their bound; the KV cache is byte storage holding BF16 pages; a page whose
+    layers all have bound zero is one raw segment."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    layers, prefix, epl = 24, 2, 2 * 16 * 64
+    page_numel = prefix * layers * epl
+    backing = torch.randn(3, page_numel, dtype=torch.bfloat16, device="cuda")
+    tensor = backing.view(torch.uint8).view(torch.int8).reshape(3, -1)
+    expected = backing[0].clone()
+    bounds_of = {i: (0.0 if i < 12 else 1e-2) for i in range(layers)}
+    h = ko.CompressedCpuGpuOffloadingHandlers(tensor, error_bound=1e-4, device_id=0,
+                                              chunk_pages=4, layer_bounds=bounds_of)
+    try:
+        h.gpu_to_cpu_handler.transfer_async(1, (np.array([0]), np.array([0])))
+        h.gpu_to_cpu_handler.wait({1})
+        stored = h.gpu_to_cpu_handler.get_finished()[0]
+        assert stored.success and stored.transfer_size < page_numel * 2
+        segs = h.store.get(0).segments
+        assert [s.encoding for s in segs] == ["raw", "cuszp"]
+        assert segs[0].components[0].layer_indices == tuple(range(12))
+        tensor[1].zero_()
+        h.cpu_to_gpu_handler.transfer_async(2, (np.array([0]), np.array([1])))
+        h.cpu_to_gpu_handler.wait({2})
+        torch.cuda.synchronize()
+        got = backing[1].view(prefix, layers, 2, 16, 64)
+        want = expected.view(prefix, layers, 2, 16, 64)
+        assert torch.equal(got[:, :12], want[:, :12])
+        assert torch.isfinite(got[:, 12:]).all()
+        assert torch.allclose(got[:, 12:].float(), want[:, 12:].float(), atol=0.12, rtol=0.12)
+    finally:
+        h.shutdown()
+    green = ko.CompressedCpuGpuOffloadingHandlers(tensor, error_bound=1e-4, device_id=0,
+                                                  layer_bounds={i: 0.0 for i in range(layers)})
+    try:
+        green.gpu_to_cpu_handler.transfer_async(1, (np.array([2]), np.array([5])))
+        green.gpu_to_cpu_handler.wait({1})
+        segs = green.store.get(5).segments
+        assert len(segs) == 1 and segs[0].encoding == "raw"
+        assert segs[0].components[0].layer_axis is None
+        assert torch.equal(segs[0].payload, tensor[2].view(torch.uint8).cpu())
+    finally:
+        green.shutdown()
