@@ -107,7 +107,9 @@ class ClockSampler:
                   "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                   "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device: torch.device, physical_index: int, period_s: float = 0.002):
+    def __init__(self, device: torch.device, physical_index: int, period_s: float = 0.002,
+                 enabled: bool = True):
+        self.enabled = enabled
         self.period = period_s
         self.samples: list[tuple[float, int]] = []
         self.max_mhz = None
@@ -116,6 +118,8 @@ class ClockSampler:
         self.handle = None
         self.proc = None
         self.lines: list[str] = []
+        if not enabled:
+            return
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -149,6 +153,8 @@ class ClockSampler:
             self._stop.wait(self.period)
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         if self.nvml is not None:
             import threading
             self._stop = threading.Event()
@@ -166,6 +172,8 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if not self.enabled:
+            return
         if self.nvml is not None:
             self._stop.set()
             self._thread.join(timeout=5)
@@ -1142,7 +1150,9 @@ def main() -> int:
 
     barrier()
     launches0 = codec.launches()
-    with ClockSampler(device, physical) as clocks:
+    # only rank 0's GPU is sampled (its line is the one printed): NVML queries
+    # from every rank at 2 ms would contend with the ranks' own driver calls
+    with ClockSampler(device, physical, enabled=rank == 0) as clocks:
         step_ms, _ = timed_steps(codec.step, args.steps, flush, device, after=kernel_times)
         barrier()
         launches_value = codec.launches() - launches0
