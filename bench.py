@@ -758,8 +758,20 @@ def c1_leg(codec, steps: int, flush: torch.Tensor, device) -> dict:
 C3_LOW_LAYERS = (0, 1, 2, 5, 19, 20, 21)   # 1e-5; the other 21 layers at 1e-4
 
 
+def c3_host_slabs(codec, repeat: int = 8) -> list[torch.Tensor]:
+    """The C3 leg's two page-locked slabs, allocated before the other legs'
+    (page-locked buffers allocated late in the run measured slower copies)."""
+    lib = codec.lib
+    prefix, layers = 2, LAYERS
+    epl = codec.n // (prefix * layers)
+    high = [i for i in range(layers) if i not in C3_LOW_LAYERS]
+    sel = (C.c_size_t * 2)(len(C3_LOW_LAYERS), len(high))
+    cap = int(lib.ckv_pipe_host_capacity_groups(codec.count * repeat, sel, 2, prefix, epl))
+    return [torch.empty(cap, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+
+
 def layer_groups_c3(codec, steps: int, flush: torch.Tensor, device, repeat: int = 8,
-                    chunk_pages: int = 0) -> dict:
+                    chunk_pages: int = 0, slabs=None) -> dict:
     """C3: the mixed per-layer profile (7 layers at 1e-5, 21 at 1e-4, the
     reference's calibrated assignment) over 2048 pages, each page stored as
     two layer segments (ckv_pipe_store_bf16_groups) while the previous
@@ -784,7 +796,8 @@ def layer_groups_c3(codec, steps: int, flush: torch.Tensor, device, repeat: int 
     codec._check(lib.ckv_pipe_create(codec.ctx, chunk_pages or count, C.byref(pipe)), "c3 pipe")
     try:
         cap = int(lib.ckv_pipe_host_capacity_groups(count, sel, G, prefix, epl))
-        slabs = [torch.empty(cap, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        if slabs is None or min(t.numel() for t in slabs) < cap:
+            slabs = [torch.empty(cap, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
         meta = [{"o": (C.c_size_t * (count * G))(), "s": (C.c_size_t * (count * G))(),
                  "b": (C.c_float * (count * G))(), "t": C.c_size_t(0)} for _ in range(2)]
         dst = torch.zeros_like(pages)
@@ -1124,6 +1137,8 @@ def main() -> int:
 
     codec = (OurCodec(device, pages_dev, args.chunk_pages) if impl == "ours"
              else RefCodec(device, pages_dev))
+    c3_slabs = (c3_host_slabs(codec) if impl == "ours" and rank == 0 and not args.no_c3
+                else None)
     pipelined = impl == "ours"
     for _ in range(args.warmup):
         codec.step()
@@ -1174,9 +1189,14 @@ def main() -> int:
              if impl == "ours" and pipelined and rank == 0 else None)
     c1 = (c1_leg(codec, min(args.steps, 10), flush, device)
           if impl == "ours" and pipelined and rank == 0 else None)
-    c3 = (layer_groups_c3(codec, min(args.steps, 10), flush, device,
-                          chunk_pages=args.chunk_pages)
-          if impl == "ours" and pipelined and rank == 0 and not args.no_c3 else None)
+    c3 = None
+    if impl == "ours" and pipelined and rank == 0 and not args.no_c3:
+        # a first pass warms the pipeline and its page-locked slabs: the first
+        # use of a freshly allocated 1 GiB slab pair ran the copies at half
+        # speed for its whole first pass, later passes at full speed
+        layer_groups_c3(codec, 3, flush, device, chunk_pages=args.chunk_pages, slabs=c3_slabs)
+        c3 = layer_groups_c3(codec, min(args.steps, 10), flush, device,
+                             chunk_pages=args.chunk_pages, slabs=c3_slabs)
     streamed = {}
     for name in [w.strip() for w in args.streamed.split(",") if w.strip()]:
         if impl == "ours" and pipelined and rank == 0:
