@@ -900,26 +900,36 @@ def make_job_pages(layers: int, heads: int, pages: int, seed: int, device) -> to
     return out.view(pages, -1)
 
 
-def streamed_jobs(codec, name: str, steps: int, flush: torch.Tensor, device,
+def streamed_host_bytes(name: str, pages_per_job: int = 2048) -> int:
+    """Page-locked bytes a rank's C4 / C5 leg holds (two raw-size job slabs)."""
+    cfg = STREAMED[name]
+    return 2 * pages_per_job * 2 * cfg["layers"] * cfg["heads"] * TOKENS * HEAD_DIM * 2
+
+
+def host_memory_available() -> int:
+    try:
+        with open("/proc/meminfo") as f:
+            return int(next(l for l in f if l.startswith("MemAvailable")).split()[1]) * 1024
+    except (OSError, StopIteration, ValueError):
+        return 0
+
+
+def streamed_jobs(codec, name: str, steps: int, flush: torch.Tensor, device, rank: int = 0,
                   chunk_pages: int = 256, pages_per_job: int = 2048) -> dict:
     """C4 / C5 through the pipeline: a step stores every job (2048 pages each) from its own KV
     pages into one of two page-locked slabs on the caller's stream while the previous job is
     restored on a second stream (background store, on-demand restore), so the link carries a
-    store and a restore at once.  Restores are checked per element against their page's bound."""
+    store and a restore at once.  Restores are checked per element against their page's bound.
+    Each rank runs its own jobs (its own seeds, as a tensor-parallel shard would)."""
     cfg = STREAMED[name]
     lib, ck = codec.lib, codec.ckv
     jobs = cfg["jobs"]
-    raw_job = pages_per_job * 2 * cfg["layers"] * cfg["heads"] * TOKENS * HEAD_DIM * 2
-    try:
-        avail = int(next(l for l in open("/proc/meminfo") if l.startswith("MemAvailable")).split()[1]) * 1024
-    except (OSError, StopIteration, ValueError):
-        avail = 0
-    if avail < 8 * raw_job:   # two page-locked slabs, with room to spare
-        return {"workload": name, "skipped": f"{avail / 1e9:.1f} GB host memory available"}
-    pages = [make_job_pages(cfg["layers"], cfg["heads"], pages_per_job, cfg["seed"] + r, device)
+    pages = [make_job_pages(cfg["layers"], cfg["heads"], pages_per_job,
+                            cfg["seed"] + rank * jobs + r, device)
              for r in range(jobs)]
     n = pages[0].shape[1]
     dst = [torch.zeros_like(p) for p in pages]
+    raw_job = pages_per_job * n * 2
     src_ptrs = [ck.ptr_array([p[i].data_ptr() for i in range(pages_per_job)]) for p in pages]
     dst_ptrs = [ck.ptr_array([d[i].data_ptr() for i in range(pages_per_job)]) for d in dst]
     eps = (C.c_float * pages_per_job)(*([cfg["eps"]] * pages_per_job))
@@ -982,6 +992,7 @@ def streamed_jobs(codec, name: str, steps: int, flush: torch.Tensor, device,
                         f"({raw_step / 1e9:.2f} GB), seeded on the device",
             "e2e_gbps": round(job_rate(1, raw_step, steps, t), 3),
             "ms_per_step": round(t * 1e3 / steps, 3),
+            "seconds": t, "raw_bytes_per_step": raw_step, "steps": steps,
             "compression_ratio": round(raw_step / max(1, moved[-1]), 4),
             "d2h_bytes_per_step": int(moved[-1]), "h2d_bytes_per_step": int(moved[-1]),
             "restore_ok": ok,
@@ -1199,8 +1210,23 @@ def main() -> int:
                              chunk_pages=args.chunk_pages, slabs=c3_slabs)
     streamed = {}
     for name in [w.strip() for w in args.streamed.split(",") if w.strip()]:
-        if impl == "ours" and pipelined and rank == 0:
-            streamed[name] = streamed_jobs(codec, name, 3, flush, device)
+        if impl != "ours" or not pipelined:
+            continue
+        # every rank runs its own shard; all ranks take the same branch
+        fits = torch.tensor([1 if host_memory_available() >= world * 2 *
+                             streamed_host_bytes(name) else 0], device=device)
+        if dist is not None:
+            dist.all_reduce(fits, op=dist.ReduceOp.MIN)
+        if not int(fits.item()):
+            streamed[name] = {"workload": name, "skipped": "not enough host memory"}
+            continue
+        barrier()
+        leg = streamed_jobs(codec, name, 3, flush, device, rank=rank)
+        (t_leg,) = slowest_rank([leg.pop("seconds")], dist, device)
+        leg["e2e_gbps_rank0"] = leg.pop("e2e_gbps")
+        leg["e2e_gbps"] = round(job_rate(world, leg["raw_bytes_per_step"], leg["steps"], t_leg), 3)
+        leg["n_gpus"] = world
+        streamed[name] = leg
 
     e2e_match = codec.e2e_matches() if pipelined else None
     t_step, t_e2e, t_serial = slowest_rank(
