@@ -1067,17 +1067,31 @@ def raw_pcie_duplex(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, de
     return sum(times) / 1e3
 
 
-def bind_host_threads(physical: int):
+def bind_host_threads(physical: int, local: int, local_world: int):
     """Keeps this rank's host threads (and the page-locked memory they touch
-    first) on the CPUs NVML names as closest to its GPU; with one process per
-    GPU the ranks otherwise share and migrate across sockets.  Sets nothing
-    on the GPU.  Returns the CPUs kept, or None."""
+    first) on CPUs of its own: the ones NVML names as closest to its GPU,
+    and of the machine's CPUs the local rank's equal share, where the two
+    overlap.  The timed steps wait on the host between the compress and the
+    decompress calls, so a rank whose thread is preempted or shares a core
+    with another rank's threads (torch keeps a pool of one thread per CPU in
+    every process) stalls its GPU, and the slowest rank sets the number.
+    Sets nothing on the GPU.  Returns the number of CPUs kept, or None."""
     try:
         import pynvml
         pynvml.nvmlInit()
         pynvml.nvmlDeviceSetCpuAffinity(pynvml.nvmlDeviceGetHandleByIndex(physical))
-        return len(os.sched_getaffinity(0))
-    except Exception:   # no NVML or no affinity information: leave the threads as they are
+    except Exception:   # no NVML or no affinity information
+        pass
+    try:
+        near = sorted(os.sched_getaffinity(0))
+        cpus = list(range(os.cpu_count() or 1))
+        per = max(1, len(cpus) // max(1, local_world))
+        share = cpus[local * per:(local + 1) * per]
+        mine = [c for c in share if c in near] or share
+        os.sched_setaffinity(0, mine)
+        torch.set_num_threads(len(mine))
+        return len(mine)
+    except Exception:
         return None
 
 
@@ -1115,7 +1129,8 @@ def main() -> int:
     visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     ids = [v for v in visible.split(",") if v.strip()]
     physical = int(ids[local]) if len(ids) > local and ids[local].strip().isdigit() else local
-    affinity = bind_host_threads(physical) if world > 1 else None
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    affinity = bind_host_threads(physical, local, local_world) if world > 1 else None
 
     impl = args.impl
     ref_note = None
@@ -1131,11 +1146,13 @@ def main() -> int:
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:   # the CPU baseline: N = 1 only
         cpu = cpu_baseline(host, reps=1)
 
     if impl == "reference_cpu":
         if rank == 0:
+            if cpu is None:
+                cpu = cpu_baseline(host, reps=1)
             line = {"metric": METRIC, "impl": "reference", "value": cpu["value"],
                     "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
                     "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
