@@ -617,3 +617,56 @@ def test_handlers_zero_bound_layers_stay_exact():
         assert torch.equal(segs[0].payload, tensor[2].view(torch.uint8).cpu())
     finally:
         green.shutdown()
+
+
+def test_job_header_round_trips_any_layout():
+    """Write / read of the job format over random layouts: page counts, layer
+    groups (including raw zero-bound ones), raw entries and codecs."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=60, deadline=None)
+    @given(st.integers(1, 9), st.integers(1, 4), st.integers(2, 30), st.integers(0, 2**31),
+           st.sampled_from(["cuszp", "int8", "raw"]))
+    def check(count, segs, layers, seed, codec):
+        rng = np.random.default_rng(seed)
+        if codec != "cuszp":
+            segs = 1
+        segs = min(segs, layers)
+        prefix, epl = 2, 64
+        n = prefix * layers * epl
+        groups = None
+        if segs > 1:
+            owner = rng.permutation(np.arange(layers) % segs)
+            groups = [(float(g) * 1e-4, tuple(int(x) for x in np.flatnonzero(owner == g)))
+                      for g in range(segs)]
+        seg_elems = [n] if groups is None else [prefix * len(sel) * epl for _b, sel in groups]
+        entries = count * segs
+        raw = (rng.random(entries) < 0.3) if codec == "cuszp" else np.full(entries, codec == "raw")
+        sizes, offsets, pos = [], [], 0
+        for j in range(entries):
+            full = 2 * seg_elems[j % segs]
+            if codec == "int8":
+                size = (n + 3) // 4 * 4 + 4
+            elif raw[j]:
+                size = full
+            else:
+                size = int(rng.integers(1, full))
+            offsets.append(pos)
+            sizes.append(size)
+            pos += (size + 15) // 16 * 16
+        bounds = rng.random(entries).astype(np.float32)
+        hdr = ko.JobHeader.bytes_for(count, segs, layers if segs > 1 else 0)
+        slab = torch.zeros(hdr + pos, dtype=torch.uint8)
+        ko.JobHeader.write(slab, n, 1e-4, True, (C.c_size_t * entries)(*offsets),
+                           (C.c_size_t * entries)(*sizes), (C.c_float * entries)(*bounds.tolist()),
+                           pos, groups, prefix, layers if segs > 1 else 0, raw=raw.tolist(),
+                           codec=codec)
+        job = ko.JobHeader.read(slab)
+        assert job["count"] == count and job["segments"] == segs and job["codec"] == codec
+        assert job["sizes"].tolist() == sizes and job["offsets"].tolist() == offsets
+        assert job["bounds"].tolist() == bounds.tolist()
+        assert job["raw"].tolist() == raw.tolist()
+        if groups is not None:
+            assert [sel for _b, sel in job["groups"]] == [sel for _b, sel in groups]
+
+    check()
