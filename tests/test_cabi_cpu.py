@@ -48,6 +48,22 @@ def test_host_only_entry_points():
     assert lib.ckv_max_compressed_size(32768) == 1024 + 1024 * 132
     assert lib.ckv_max_compressed_size(32769) == 2048 + 1025 * 132
     assert isinstance(lib.ckv_kernel_launches(), int)
+    # pipeline host buffers for cuSZp pages: every unit at its worst case,
+    # 16-byte aligned, plus the alignment slack of each unit
+    import ctypes as C
+
+    def worst(n):
+        nb = (n + 31) // 32
+        return ((n + 32767) // 32768 * 1024 + nb * 132 + 15) // 16 * 16
+
+    n = 229376
+    assert lib.ckv_pipe_host_capacity(5, n) == 5 * (worst(n) + 16)
+    sel = (C.c_size_t * 2)(7, 21)
+    cap = lib.ckv_pipe_host_capacity_groups(3, sel, 2, 2, 4096)
+    assert cap == 3 * (worst(2 * 7 * 4096) + 16 + worst(2 * 21 * 4096) + 16)
+    # INT8 and raw pages have known sizes: their 16-byte strides exactly
+    assert lib.ckv_pipe_host_capacity_int8(4, 1001) == 4 * ((1004 + 4 + 15) // 16 * 16)
+    assert lib.ckv_pipe_host_capacity_raw(4, 1002) == 4 * ((1002 + 15) // 16 * 16)
 
 
 def test_python_surface_matches_reference():
