@@ -108,7 +108,10 @@ CKV_API ckv_status ckv_compress_batch_fixed_bf16(ckv_ctx* ctx, const void* const
 
 /* compress_batch_fixed_bf16_indexed(...)       cuszp_wrapper.cpp:548-681.
  * Pages are [prefix_count][source_layers][elements_per_layer] BF16; unit i
- * is layers layer_indices[0..selected) (device int64 array) of page i. */
+ * is layers layer_indices[0..selected) (device int64 array) of page i.
+ * Every index must lie in [0, source_layers): the values live on the device
+ * and, as in the reference (cuszp_batched_fixed.cu:33-50), are not checked
+ * (this applies to every call below that takes layer indices). */
 CKV_API ckv_status ckv_compress_batch_fixed_bf16_indexed(
     ckv_ctx* ctx, const void* const* inputs, uint8_t* const* outputs,
     const int64_t* layer_indices, size_t selected, size_t prefix_count,
