@@ -160,4 +160,4 @@ def main(out_dir: str) -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(main(sys.argv[1] if len(sys.argv) > 1 else "gpurun_out/golden"))
+    sys.exit(main(sys.argv[1] if len(sys.argv) > 1 else "golden_out"))
