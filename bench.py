@@ -249,6 +249,63 @@ def cpu_baseline(host_pages: torch.Tensor, reps: int = 1) -> dict:
             "restore_gbps": round(raw / min(dec_t) / 1e9, 3)}
 
 
+def reference_arm(args, world: int) -> dict:
+    """The reference arm: the reference's path has no CPU implementation of
+    its own (its codec is CUDA), so the C restatement of its kernels
+    (oracle/fixed_codec.c, checked byte for byte against the reference's
+    kernels on the committed goldens) runs on all host cores: W untimed and K
+    timed steps, each an encode and a decode of the full C2 batch."""
+    from oracle.oracle import COracle
+    co = COracle()
+    threads = len(os.sched_getaffinity(0)) or 1
+    host = make_pages(args.pages, seed=0)
+    bits = host.view(torch.int16).numpy().view(np.uint16)
+    pages = [np.ascontiguousarray(bits[i]) for i in range(bits.shape[0])]
+    n = pages[0].size
+    raw = bits.nbytes
+    dest = [np.empty(n, dtype=np.uint16) for _ in pages]
+    dp = (C.c_void_p * len(dest))(*[d.ctypes.data for d in dest])
+
+    def step():
+        outs, sizes, ebs = co.encode_batch_bf16(pages, EPS, relative=True, threads=threads)
+        ins = (C.c_void_p * len(outs))(*[o.ctypes.data for o in outs])
+        sz = np.ascontiguousarray(sizes, dtype=np.uint64)
+        eb = np.ascontiguousarray(ebs, dtype=np.float32)
+        assert co.lib.ckvo_decode_batch_bf16(ins, sz.ctypes.data, eb.ctypes.data, dp, len(outs),
+                                             n, threads) == 0
+        return int(sz.sum())
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    comp = 0
+    for _ in range(args.steps):
+        comp = step()
+    t = time.perf_counter() - t0
+    value = round(2 * raw * args.steps / t / 1e9, 3)
+    sample = (f"{len(pages)} pages x {n} BF16 per step (the full C2 batch), encode + decode; "
+              f"oracle/fixed_codec.c on {threads} host threads")
+    return {
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t * 1e3 / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32/u32",
+        "data": "synthetic (seeded CPU generation, BASELINE.json configs[1] shapes)",
+        "config": {"workload": "C2: Qwen2.5-1.5B KV at 4k context, 256 pages x 229376 BF16 "
+                               "([2,28,2,16,128]), REL eb 1e-5, one store + one restore per step",
+                   "pages_per_gpu": args.pages, "elements_per_page": PAGE_NUMEL,
+                   "error_bound": EPS, "relative": True},
+        "compression_ratio": round(raw / max(1, comp), 4),
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_impl": ("the reference's codec is CUDA (integration/cuszp_wrapper/"
+                           "cuszp_batched_fixed.cu); its C restatement, byte-identical on the "
+                           "goldens, on the host cores. The reference's own kernels on the GPU "
+                           "are timed in the other arm's reference_kernels object."),
+    }
+
+
 # ---------------------------------------------------------------------------
 # Same-run comparison points for the page codec: the reference connector's
 # other codecs -- zstd level 1 and LZ4 through the system libraries (as its
@@ -755,6 +812,39 @@ def c1_leg(codec, steps: int, flush: torch.Tensor, device) -> dict:
     return out
 
 
+def reference_kernels_leg(device, pages_dev: torch.Tensor, steps: int, warmup: int,
+                          flush: torch.Tensor) -> dict | None:
+    """The reference's own kernels on the same GPU and pages: its batched BF16
+    kernels (integration/cuszp_wrapper/cuszp_batched_fixed.cu, built unchanged
+    in oracle/_ref) driven as CuSZpWrapper drives them, and its connector's
+    store / restore (torch.cat packing, one D2H, one H2D, batched scatter
+    decode) for the end-to-end number."""
+    from oracle import build as oracle_build
+    if not oracle_build.REF_SO.exists():
+        return None
+    ref = RefCodec(device, pages_dev)
+    for _ in range(warmup):
+        ref.step()
+        ref.step_e2e()
+    torch.cuda.synchronize(device)
+    raw = pages_dev.numel() * 2
+    v_ms, _ = timed_steps(ref.step, steps, flush, device)
+    e_ms, totals = timed_steps(ref.step_e2e, steps, flush, device)
+    ok = ref.verify()
+    return {
+        "value": round(job_rate(1, raw, steps, sum(v_ms) / 1e3), 3),
+        "ms_per_step": round(sum(v_ms) / steps, 4),
+        "e2e": round(job_rate(1, raw, steps, sum(e_ms) / 1e3), 3),
+        "e2e_ms_per_step": round(sum(e_ms) / steps, 4),
+        "h2d_bytes_per_step": int(totals[-1]), "d2h_bytes_per_step": int(totals[-1]),
+        "compression_ratio": round(raw / ref.compressed_bytes(), 4),
+        "restore_ok": ok,
+        "path": "the reference's batched BF16 kernels (oracle/_ref, built unchanged from "
+                "integration/cuszp_wrapper/cuszp_batched_fixed.cu) driven like CuSZpWrapper; "
+                "e2e: compress, torch.cat pack, one D2H, one H2D, decompress",
+    }
+
+
 C3_LOW_LAYERS = (0, 1, 2, 5, 19, 20, 21)   # 1e-5; the other 21 layers at 1e-4
 
 
@@ -1116,6 +1206,11 @@ def main() -> int:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        # on the host cores, rank 0 alone; the other ranks have nothing to do
+        if rank == 0:
+            print(json.dumps(reference_arm(args, world)))
+        return 0
     dist = None
     if world > 1:
         import datetime
@@ -1133,12 +1228,6 @@ def main() -> int:
     affinity = bind_host_threads(physical, local, local_world) if world > 1 else None
 
     impl = args.impl
-    ref_note = None
-    if impl == "reference":
-        from oracle import build as oracle_build
-        if not oracle_build.REF_SO.exists():
-            impl = "reference_cpu"
-            ref_note = "reference kernels not built here; the CPU port stands in"
 
     host = make_pages(args.pages, seed=rank)
     raw_bytes = host.numel() * 2
@@ -1149,19 +1238,6 @@ def main() -> int:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:   # the CPU baseline: N = 1 only
         cpu = cpu_baseline(host, reps=1)
 
-    if impl == "reference_cpu":
-        if rank == 0:
-            if cpu is None:
-                cpu = cpu_baseline(host, reps=1)
-            line = {"metric": METRIC, "impl": "reference", "value": cpu["value"],
-                    "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-                    "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-                    "vs_baseline": None, "dtype": "f32/u32", "data": "synthetic",
-                    "config": {"workload": "C2"}, "cpu_baseline": cpu, "note": ref_note,
-                    "e2e": {"value": cpu["value"], "unit": "GB/s",
-                            "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-            print(json.dumps(line))
-        return 0
 
     codec = (OurCodec(device, pages_dev, args.chunk_pages) if impl == "ours"
              else RefCodec(device, pages_dev))
@@ -1217,6 +1293,8 @@ def main() -> int:
              if impl == "ours" and pipelined and rank == 0 else None)
     c1 = (c1_leg(codec, min(args.steps, 10), flush, device)
           if impl == "ours" and pipelined and rank == 0 else None)
+    ref_kernels = (reference_kernels_leg(device, pages_dev, min(args.steps, 10), 3, flush)
+                   if impl == "ours" and rank == 0 else None)
     c3 = None
     if impl == "ours" and pipelined and rank == 0 and not args.no_c3:
         # a first pass warms the pipeline and its page-locked slabs: the first
@@ -1338,6 +1416,7 @@ def main() -> int:
         line["kernels"] = kernels
         line["pipeline_codecs"] = piped
         line["c1"] = c1
+        line["reference_kernels"] = ref_kernels
         line["layer_groups_c3"] = c3
         if streamed:
             line["streamed"] = streamed
