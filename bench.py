@@ -13,19 +13,22 @@ One step = store (compress every page, sizes back on the host) + restore
   value  -- uncompressed bytes through the codec (stored + restored) per
             second, inputs resident in HBM, C-ABI calls (include/ckv.h)
             timed with CUDA events; L2 flushed (256 MB write) between steps.
-  e2e    -- the same with host buffers: compress, pack the pages into one
-            slab, one D2H into pinned memory; one H2D back, decompress from
-            the slab into the KV pages.
+  e2e    -- the same with host buffers, through the store / restore
+            pipeline (ckv_pipe_*): step k's pages are stored into one
+            page-locked slab while step k-1's slab is restored.
   roofline -- the dominant kernel's algorithmic bytes (encode 2N + S_c,
             decode S_c + 2N per page) / its CUDA-event duration, against the
             measured HBM copy bandwidth (MEASURED_PEAKS.json).
   cpu_baseline -- the CPU port of the codec (oracle/fixed_codec.c) on all
             host cores, same pages, encode + decode.
 
---impl reference runs the reference's own kernels
+--impl reference is the reference arm on the host cores: the reference's
+codec is CUDA with no CPU implementation, so the C restatement of its
+kernels (oracle/fixed_codec.c) encodes and decodes the same pages on every
+host thread (rank 0 alone under torchrun).  The reference's own kernels
 (integration/cuszp_wrapper/cuszp_batched_fixed.cu, built unchanged into
-oracle/_ref) on the same workload, driven like its CuSZpWrapper and its
-connector's packed store / batched restore.
+oracle/_ref) run on the GPU inside this arm, driven like its CuSZpWrapper
+and its connector's packed store / batched restore: `reference_kernels`.
 
 Multi-GPU (torchrun, N ranks): each rank encodes and decodes its own 256
 pages (its tensor-parallel KV shard); no data-path collective; value is the
