@@ -60,3 +60,23 @@ def test_job_rate_counts_every_rank():
     assert abs(bench.job_rate(4, 117440512, 10, 0.01) - 4 * one) < 1e-9
     assert abs(one - 2 * 117440512 * 10 / 0.01 / 1e9) < 1e-9
     assert bench.slowest_rank([1.0, 2.0]) == [1.0, 2.0]
+
+
+def test_reference_arm_line_on_cpu():
+    """The reference arm runs on the host cores alone and prints the contract's
+    keys: impl, a cpu_baseline describing the run with value = the line's,
+    and an e2e with no copies."""
+    import argparse
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    args = argparse.Namespace(pages=2, steps=1, warmup=1)
+    line = bench.reference_arm(args, world=2)
+    assert line["impl"] == "reference" and line["n_gpus"] == 2
+    assert line["metric"] == bench.METRIC and line["unit"] == "GB/s"
+    assert line["value"] > 0 and line["higher_is_better"] is True
+    cb = line["cpu_baseline"]
+    assert cb["value"] == line["value"] and cb["kind"] == "port" and cb["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s",
+                           "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert 1.0 < line["compression_ratio"] < 3.0
