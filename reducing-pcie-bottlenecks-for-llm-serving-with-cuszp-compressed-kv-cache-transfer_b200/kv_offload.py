@@ -25,7 +25,14 @@ fixed-mode BF16 path, on top of libckv's store / restore pipeline
 
 A KV cache here is one contiguous tensor ``[num_blocks, *page_shape]`` of
 BF16 pages (the cross-layer page layout the reference compresses as one
-unit, e.g. ``[2, layers, heads, 16, head_dim]``).
+unit, e.g. ``[2, layers, heads, 16, head_dim]``), or its byte storage.
+
+What a stored page becomes follows the reference's handler: one cuSZp
+fixed-mode stream per page, or with per-layer bounds one segment per
+distinct bound (zero-bound layers raw); a page or segment that cuSZp would
+not shrink below its BF16 size is stored raw; pages below 36864 elements are
+coded zero-padded; and the handler's ``codec`` may instead be the
+reference's ``"int8"`` or ``"raw"`` comparison codecs.
 """
 from __future__ import annotations
 
