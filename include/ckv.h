@@ -240,8 +240,10 @@ CKV_API ckv_status ckv_pipe_restore_bf16(ckv_pipe* pipe, const uint8_t* host,
                                          void* stream);
 
 /* Make `stream` wait for a ticket (device side); wait for it on the host;
- * query it (1 done, 0 pending, -1 unknown).  A pipeline keeps the last 64
- * tickets. */
+ * query it (1 done, 0 pending, -1 unknown).  A pipeline keeps the events of
+ * its last 64 tickets: issuing a ticket first waits on the host for the one
+ * 64 before it, so an older ticket is complete (done 1, wait and join
+ * return at once). */
 CKV_API ckv_status ckv_pipe_join(ckv_pipe* pipe, uint64_t ticket, void* stream);
 /* A ticket for the work queued on `stream` so far (the caller's own copies
  * into or out of a host buffer, which later pipeline calls can then be

@@ -937,11 +937,23 @@ cudaEvent_t pipe_ticket_event(ckv_pipe* p, uint64_t ticket) {
     return p->tickets[ticket % ckv_pipe::kTickets];
 }
 
-// Records a new ticket on `stream`.
+// A ticket whose event slot a newer ticket took over.  pipe_issue waited for
+// it on the host before reusing the slot, so its work is complete.
+bool pipe_retired(const ckv_pipe* p, uint64_t ticket) {
+    return ticket + ckv_pipe::kTickets < p->next_ticket;
+}
+
+// Records a new ticket on `stream`.  Its slot's previous ticket (kTickets
+// older) retires: the host waits for it first, so that a retired ticket never
+// aliases newer work.
 ckv_status pipe_issue(ckv_pipe* p, cudaStream_t stream, uint64_t* ticket) {
-    const uint64_t t = p->next_ticket++;
-    cudaError_t e = cudaEventRecord(pipe_ticket_event(p, t), stream);
+    const uint64_t t = p->next_ticket;
+    cudaEvent_t ev = pipe_ticket_event(p, t);
+    cudaError_t e = cudaEventSynchronize(ev);
+    if (e != cudaSuccess) return cuda_fail(p->ctx, "retiring a pipeline ticket", e);
+    e = cudaEventRecord(ev, stream);
     if (e != cudaSuccess) return cuda_fail(p->ctx, "recording a pipeline ticket", e);
+    p->next_ticket = t + 1;
     if (ticket) *ticket = t;
     return CKV_OK;
 }
@@ -949,6 +961,7 @@ ckv_status pipe_issue(ckv_pipe* p, cudaStream_t stream, uint64_t* ticket) {
 ckv_status pipe_after(ckv_pipe* p, uint64_t after, cudaStream_t stream) {
     if (!after) return CKV_OK;
     if (after >= p->next_ticket) return fail(p->ctx, CKV_ERR_ARGUMENT, "unknown ticket");
+    if (pipe_retired(p, after)) return CKV_OK;
     cudaError_t e = cudaStreamWaitEvent(stream, pipe_ticket_event(p, after), 0);
     if (e != cudaSuccess) return cuda_fail(p->ctx, "ordering after a ticket", e);
     return CKV_OK;
@@ -1589,6 +1602,7 @@ ckv_status ckv_pipe_wait(ckv_pipe* p, uint64_t ticket) {
     if (!p) return CKV_ERR_ARGUMENT;
     if (!ticket) return CKV_OK;
     if (ticket >= p->next_ticket) return fail(p->ctx, CKV_ERR_ARGUMENT, "unknown ticket");
+    if (pipe_retired(p, ticket)) return CKV_OK;
     DeviceGuard guard(p->ctx->device);
     cudaError_t e = cudaEventSynchronize(pipe_ticket_event(p, ticket));
     if (e != cudaSuccess) return cuda_fail(p->ctx, "waiting for a pipeline ticket", e);
@@ -1597,7 +1611,7 @@ ckv_status ckv_pipe_wait(ckv_pipe* p, uint64_t ticket) {
 
 int ckv_pipe_done(ckv_pipe* p, uint64_t ticket) {
     if (!p || ticket >= p->next_ticket) return -1;
-    if (!ticket) return 1;
+    if (!ticket || pipe_retired(p, ticket)) return 1;
     DeviceGuard guard(p->ctx->device);
     const cudaError_t e = cudaEventQuery(pipe_ticket_event(p, ticket));
     if (e == cudaSuccess) return 1;

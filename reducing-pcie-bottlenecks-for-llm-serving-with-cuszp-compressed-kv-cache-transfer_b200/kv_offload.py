@@ -789,8 +789,7 @@ class CompressedOffloadingHandler:
         return True
 
     def get_finished(self) -> list[TransferResult]:
-        """Jobs finished since the last call (a pipeline keeps its last 64
-        tickets: poll at least that often)."""
+        """Jobs finished since the last call."""
         lib, pipe = self.engine.lib, self.engine.pipe
         with self._lock:
             done = []
