@@ -232,3 +232,26 @@ def test_pipe_layer_groups_match_plain_calls(env):
         assert torch.equal(restored.view(torch.int16), ref_restored.view(torch.int16))
     finally:
         lib.ckv_pipe_destroy(pipe)
+
+
+def test_pipe_tickets_retire(env):
+    """A ticket older than the pipeline's 64 ticket events reads as complete
+    (done 1, wait and join return at once) instead of aliasing newer work."""
+    _ckv, lib, ctx = env
+    pipe = C.c_void_p()
+    assert lib.ckv_pipe_create(ctx, 8, C.byref(pipe)) == 0
+    try:
+        s = torch.cuda.current_stream().cuda_stream
+        first, t = C.c_uint64(0), C.c_uint64(0)
+        assert lib.ckv_pipe_record(pipe, s, C.byref(first)) == 0
+        for _ in range(64):
+            assert lib.ckv_pipe_record(pipe, s, C.byref(t)) == 0
+        assert t.value == first.value + 64
+        assert lib.ckv_pipe_done(pipe, first.value) == 1
+        assert lib.ckv_pipe_wait(pipe, first.value) == 0
+        assert lib.ckv_pipe_join(pipe, first.value, s) == 0
+        assert lib.ckv_pipe_done(pipe, t.value + 1) == -1
+        assert lib.ckv_pipe_wait(pipe, t.value) == 0
+        assert lib.ckv_pipe_done(pipe, t.value) == 1
+    finally:
+        lib.ckv_pipe_destroy(pipe)
