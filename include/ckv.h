@@ -209,7 +209,9 @@ CKV_API ckv_status ckv_kernel_time(ckv_ctx* ctx, int kind, float* ms);
  * `chunk_pages` pages: the device-to-host copy of chunk k overlaps the
  * compression of chunk k+1, the host-to-device copy of chunk k+1 the
  * decompression of chunk k, and a store and a restore in flight together use
- * both directions of the link.  Not thread-safe; one pipeline per context. */
+ * both directions of the link.  Not thread-safe; one pipeline per context.
+ * Only ckv_pipe_done and ckv_pipe_wait may be called from another thread
+ * while a pipeline call runs (e.g. a poller of finished jobs). */
 typedef struct ckv_pipe ckv_pipe;
 CKV_API ckv_status ckv_pipe_create(ckv_ctx* ctx, size_t chunk_pages, ckv_pipe** out);
 CKV_API void ckv_pipe_destroy(ckv_pipe* pipe);

@@ -883,7 +883,8 @@ struct ckv_pipe {
     cudaEvent_t ev_in = nullptr;
     static constexpr int kTickets = 64;
     cudaEvent_t tickets[kTickets] = {};
-    uint64_t next_ticket = 1;
+    // read by ckv_pipe_done / ckv_pipe_wait, which other threads may call
+    std::atomic<uint64_t> next_ticket{1};
     std::vector<const uint8_t*> srcs;
     std::vector<size_t> local;
 };
