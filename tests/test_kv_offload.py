@@ -619,6 +619,72 @@ def test_handlers_zero_bound_layers_stay_exact():
         green.shutdown()
 
 
+@pytest.mark.gpu
+def test_handlers_many_jobs_polled_from_another_thread():
+    """More jobs than the pipeline's 64 ticket events, with finished jobs
+    polled from a second thread while the first submits them (the reference
+    runs its stores on a worker thread, vllm_v1_compressed_offload.py:2365-2385):
+    every job reports success once, and the pages stored first -- whose store
+    tickets have retired before their loads are issued -- restore bit for bit
+    as the plain calls restore them."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    import threading
+    import time
+
+    import cuszp_wrapper_cpp as cpp
+
+    jobs, shape = 70, (2, 8, 2, 16, 128)
+    kv = _kv(2 * jobs, shape, seed=14).cuda()
+    kv[jobs:].zero_()   # rate-0 blocks are not written on restore
+    n = kv[0].numel()
+    h = ko.CompressedCpuGpuOffloadingHandlers(kv, error_bound=1e-4, device_id=0, chunk_pages=4)
+    results: dict[int, list[bool]] = {}
+    submitted = threading.Event()
+
+    def poll():
+        deadline = time.monotonic() + 120
+        while time.monotonic() < deadline:
+            for handler in (h.gpu_to_cpu_handler, h.cpu_to_gpu_handler):
+                for r in handler.get_finished():
+                    results.setdefault(r.job_id, []).append(r.success)
+            if submitted.is_set() and len(results) == 2 * jobs:
+                return
+            time.sleep(1e-4)
+
+    poller = threading.Thread(target=poll)
+    poller.start()
+    try:
+        for i in range(jobs):
+            assert h.gpu_to_cpu_handler.transfer_async(i, (np.array([i]), np.array([1000 + i])))
+        for i in range(jobs):
+            assert h.cpu_to_gpu_handler.transfer_async(
+                jobs + i, (np.array([1000 + i]), np.array([jobs + i])))
+    finally:
+        submitted.set()
+        poller.join(timeout=150)
+    try:
+        assert not poller.is_alive()
+        assert results == {j: [True] for j in range(2 * jobs)}
+        torch.cuda.synchronize()
+        cfg = cpp.CompressionConfig(error_bound=1e-4, use_relative_error=True,
+                                    processing_dim=cpp.CuszpDim.DIM_1D,
+                                    encoding_mode=cpp.CuszpMode.MODE_FIXED,
+                                    data_type=cpp.CuszpType.TYPE_FLOAT)
+        w = cpp.CuSZpWrapper(cfg, 0)
+        pages = [kv[i].view(-1) for i in range(jobs)]
+        outs = [torch.empty(w.estimate_compressed_buffer_size(n * 4), dtype=torch.uint8,
+                            device="cuda") for _ in pages]
+        ok, sizes, bounds = w.compress_batch_fixed_bf16(pages, outs, [1e-4] * jobs)
+        assert ok
+        ref = torch.zeros(jobs * n, dtype=torch.bfloat16, device="cuda")
+        assert w.decompress_batch_fixed_bf16(outs, sizes, ref, n, bounds)
+        torch.cuda.synchronize()
+        assert torch.equal(kv[jobs:].reshape(-1).view(torch.int16), ref.view(torch.int16))
+    finally:
+        h.shutdown()
+
+
 def test_job_header_round_trips_any_layout():
     """Write / read of the job format over random layouts: page counts, layer
     groups (including raw zero-bound ones), raw entries and codecs."""
