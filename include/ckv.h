@@ -50,7 +50,13 @@ typedef int ckv_status;
 #define CKV_ERR_STREAM 5        /* corrupt or truncated bitstream */
 #define CKV_ERR_INTERNAL 6      /* device-side consistency check failed */
 
-/* cuszp_dim_t / cuszp_mode_t / cuszp_type_t (pybind11_bindings.cpp:13-28). */
+/* cuszp_dim_t / cuszp_mode_t / cuszp_type_t (pybind11_bindings.cpp:13-28).
+ * Upstream cuSZp's header is not vendored by the reference, so its numeric
+ * values cannot be read there; these follow the order in which the
+ * reference binds them (FIXED, PLAIN, OUTLIER: pybind11_bindings.cpp:19-22;
+ * DIM_1D..3D: :13-17; FLOAT, DOUBLE: :24-27).  oracle/ref_shim/cuSZp.h,
+ * which stands in for that header when the reference's kernels are built as
+ * a test oracle, uses the same values. */
 #define CKV_DIM_1D 0
 #define CKV_DIM_2D 1
 #define CKV_DIM_3D 2
@@ -180,6 +186,22 @@ CKV_API ckv_status ckv_set_zero_fill(ckv_ctx* ctx, int zero_fill);
 #define CKV_DEV_TIMEOUT 8u
 CKV_API ckv_status ckv_device_status(ckv_ctx* ctx, void* stream, int reset, uint32_t* bits);
 
+/* Status words (CKV_DEV_* bits, 0 = fine) of each of the first `count`
+ * units of the last compress call on this context, e.g. which unit did not
+ * fit its buffer. */
+CKV_API ckv_status ckv_unit_status(ckv_ctx* ctx, size_t count, uint32_t* out);
+
+/* Failure-path test hook.  The next encode launch on this context withholds
+ * the bound exchange of batch unit `unit` inside its thread-block cluster
+ * (the cluster's first CTA sends nothing for it), so every CTA of that
+ * cluster waits for data that never comes, and that cluster's waits give up
+ * after `wait_polls` polls instead of the default.  Every role of that
+ * cluster then stops once the copies it issued have landed and its units
+ * are marked CKV_DEV_TIMEOUT; the call fails with CKV_ERR_CUDA ("a bounded
+ * wait in the kernel ran out"), the other clusters' units complete
+ * normally, nothing faults or hangs, and the context stays usable. */
+CKV_API ckv_status ckv_test_withhold_exchange(ckv_ctx* ctx, uint32_t unit, uint32_t wait_polls);
+
 /* Gather `count` compressed units (device pointers srcs[i], sizes[i] bytes)
  * into the device slab `dst` (capacity bytes), unit i starting at
  * offsets[i] = previous end rounded up to `align` bytes (a power of two,
@@ -244,8 +266,9 @@ CKV_API ckv_status ckv_pipe_restore_bf16(ckv_pipe* pipe, const uint8_t* host,
 /* Make `stream` wait for a ticket (device side); wait for it on the host;
  * query it (1 done, 0 pending, -1 unknown).  A pipeline keeps the events of
  * its last 64 tickets: issuing a ticket first waits on the host for the one
- * 64 before it, so an older ticket is complete (done 1, wait and join
- * return at once). */
+ * 64 before it and marks it retired, so an older ticket is complete (done 1,
+ * wait and join return at once).  A wait from another thread that races with
+ * the issue retiring its ticket may also wait for the newer work. */
 CKV_API ckv_status ckv_pipe_join(ckv_pipe* pipe, uint64_t ticket, void* stream);
 /* A ticket for the work queued on `stream` so far (the caller's own copies
  * into or out of a host buffer, which later pipeline calls can then be
@@ -335,9 +358,14 @@ CKV_API size_t ckv_pipe_host_capacity_raw(size_t count, size_t page_bytes);
  * file-scope device array of CKV_NOALLOC_MAX_UNITS units (about 270 KB),
  * held by every GPU that loads the library until the process exits.
  * Larger batches are rejected with CKV_ERR_ARGUMENT and a message on stderr.
- * The first call on a device looks up the array's device address (with that
- * device current), so make it before any stream capture.  All calls share
- * the array: calls that overlap on the GPU race.  Otherwise as
+ * CUDA loads the library's kernels and its copy of the array on a device
+ * lazily, at first use, and that allocates device memory; so call this once
+ * per device with batch == 0 (every other argument is then ignored; the
+ * device must be current) at start-up, before HBM is reserved and before
+ * any stream capture.  That set-up call looks up the array's device address
+ * and runs a built-in 32-element unit, held in the array itself, through
+ * every launch a real call makes; later calls then allocate nothing.  All
+ * calls share the array: calls that overlap on the GPU race.  Otherwise as
  * ckv_compress_batch_fixed_bf16: `error_bound` and `relative` replace the
  * context's configuration, eps may be NULL, the call blocks until sizes and
  * bounds are on the host, and the bitstreams are identical. */

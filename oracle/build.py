@@ -6,11 +6,21 @@
   ``integration/cuszp_wrapper/cuszp_batched_fixed.cu``, compiled unchanged
   from where it lies under the reference checkout, with the two-constant
   stand-in headers in ``oracle/ref_shim`` and the host driver
-  ``oracle/ref_driver.cu``.  Built only where the reference checkout exists;
-  the .so then travels with the tree.
+  ``oracle/ref_driver.cu``.
+* ``oracle/_ref/py/`` -- the reference's vLLM connector
+  (``integration/compression_pipeline/*.py``) and its connector tests
+  (``tests/test_vllm_v1_compressed_offload.py``), byte-compiled unchanged
+  from where they lie (``.pyc`` only, no source copied).  The drop-in test
+  (tests/test_reference_connector_gpu.py) runs those tests with this
+  repository's ``cuszp_wrapper_cpp`` in place of the reference's binding.
 
-Neither library is part of the product; only tests/, the smoke check and
-bench.py's baseline legs load them.
+Both are built only where a reference checkout exists and then travel with
+the tree (``oracle/_ref`` is kept out of version control).  The checkout is
+``$CKV_REFERENCE_ROOT`` when set, else a sibling directory named
+``reference`` next to this repository.
+
+Nothing here is part of the product; only tests/, the smoke check and
+bench.py's baseline legs load it.
 """
 from __future__ import annotations
 
@@ -22,8 +32,18 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "_build" / "libckv_oracle.so"
 REF_SO = HERE / "_ref" / "libref_fixed.so"
-REFERENCE_ROOT = Path(os.environ.get("CKV_REFERENCE_ROOT", "/root/reference"))
+REF_PY = HERE / "_ref" / "py"
+_env_root = os.environ.get("CKV_REFERENCE_ROOT")
+REFERENCE_ROOT = Path(_env_root) if _env_root else HERE.parent.parent / "reference"
 REF_KERNEL = REFERENCE_ROOT / "integration" / "cuszp_wrapper" / "cuszp_batched_fixed.cu"
+# reference module -> its byte-compiled place under REF_PY
+CONNECTOR_MODULES = {
+    "integration/compression_pipeline/vllm_v1_compressed_offload.py":
+        "integration/compression_pipeline/vllm_v1_compressed_offload.pyc",
+    "integration/compression_pipeline/native_lossless.py":
+        "integration/compression_pipeline/native_lossless.pyc",
+    "tests/test_vllm_v1_compressed_offload.py": "ref_tests/test_vllm_v1_compressed_offload.pyc",
+}
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
@@ -72,6 +92,29 @@ def build_ref(force: bool = False) -> Path | None:
     return REF_SO
 
 
+def stage_connector(force: bool = False) -> Path | None:
+    """Byte-compile the reference's connector and its tests into REF_PY.
+
+    Sourceless ``.pyc`` files in the legacy location import without their
+    sources (Python's path finder loads ``name.pyc`` from a directory), so
+    the GPU box, which has no reference checkout, can still run the
+    unmodified connector.  Returns REF_PY, or None where neither the
+    checkout nor an earlier staging exists."""
+    import py_compile
+
+    sources = {REFERENCE_ROOT / src: REF_PY / dst for src, dst in CONNECTOR_MODULES.items()}
+    if not all(src.exists() for src in sources):
+        staged = all(dst.exists() for dst in sources.values())
+        return REF_PY if staged else None
+    for src, dst in sources.items():
+        if force or _stale(dst, [src, Path(__file__)]):
+            dst.parent.mkdir(parents=True, exist_ok=True)
+            py_compile.compile(str(src), cfile=str(dst), doraise=True,
+                               invalidation_mode=py_compile.PycInvalidationMode.UNCHECKED_HASH)
+    return REF_PY
+
+
 if __name__ == "__main__":
     print(build_oracle(force="--force" in sys.argv))
     print(build_ref(force="--force" in sys.argv))
+    print(stage_connector(force="--force" in sys.argv))

@@ -80,6 +80,11 @@ struct ckv_ctx {
     bool t_valid[kTimedKinds] = {};
     // completion of a compress call's kernels (polled, see wait_stream)
     cudaEvent_t sync_ev = nullptr;
+    // failure-path test hook for the next encode launch (0 polls: off)
+    uint32_t test_withhold = 0;
+    uint32_t test_polls = 0;
+    // units of the last compress call (their status words stay readable)
+    size_t last_units = 0;
 };
 
 namespace {
@@ -311,6 +316,10 @@ ckv_status run_encode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, size_t* sizes,
     l.bounds = ctx->bounds;
     l.status = ctx->status;
     l.type = type;
+    l.withhold_unit = ctx->test_withhold;
+    l.test_polls = ctx->test_polls;
+    ctx->test_polls = 0;
+    ctx->last_units = count;
     timing_begin(ctx, 0, stream);
     cudaError_t e = ckv::launch_encode(l, stream);
     timing_end(ctx, 0, stream);
@@ -838,6 +847,19 @@ ckv_status ckv_pack(ckv_ctx* ctx, const uint8_t* const* srcs, const size_t* size
     return CKV_OK;
 }
 
+ckv_status ckv_test_withhold_exchange(ckv_ctx* ctx, uint32_t unit, uint32_t wait_polls) {
+    if (check_ctx(ctx) || wait_polls == 0) return CKV_ERR_ARGUMENT;
+    ctx->test_withhold = unit;
+    ctx->test_polls = wait_polls;
+    return CKV_OK;
+}
+
+ckv_status ckv_unit_status(ckv_ctx* ctx, size_t count, uint32_t* out) {
+    if (check_ctx(ctx) || !out || count > ctx->last_units) return CKV_ERR_ARGUMENT;
+    for (size_t i = 0; i < count; ++i) out[i] = ctx->status[i];
+    return CKV_OK;
+}
+
 ckv_status ckv_set_kernel_timing(ckv_ctx* ctx, int enable) {
     if (!ctx) return CKV_ERR_ARGUMENT;
     ctx->timing = enable != 0;
@@ -885,6 +907,8 @@ struct ckv_pipe {
     cudaEvent_t tickets[kTickets] = {};
     // read by ckv_pipe_done / ckv_pipe_wait, which other threads may call
     std::atomic<uint64_t> next_ticket{1};
+    // every ticket <= retired is complete; raised before its event is reused
+    std::atomic<uint64_t> retired{0};
     std::vector<const uint8_t*> srcs;
     std::vector<size_t> local;
 };
@@ -938,20 +962,23 @@ cudaEvent_t pipe_ticket_event(ckv_pipe* p, uint64_t ticket) {
     return p->tickets[ticket % ckv_pipe::kTickets];
 }
 
-// A ticket whose event slot a newer ticket took over.  pipe_issue waited for
-// it on the host before reusing the slot, so its work is complete.
+// A ticket whose event slot a newer ticket took (or is taking) over.
+// pipe_issue waited for it on the host and raised `retired` before reusing
+// the slot, so its work is complete.
 bool pipe_retired(const ckv_pipe* p, uint64_t ticket) {
-    return ticket + ckv_pipe::kTickets < p->next_ticket;
+    return ticket <= p->retired.load();
 }
 
 // Records a new ticket on `stream`.  Its slot's previous ticket (kTickets
-// older) retires: the host waits for it first, so that a retired ticket never
-// aliases newer work.
+// older) retires: the host waits for it first and marks it retired before
+// the event is recorded again, so that a retired ticket never aliases newer
+// work.
 ckv_status pipe_issue(ckv_pipe* p, cudaStream_t stream, uint64_t* ticket) {
     const uint64_t t = p->next_ticket;
     cudaEvent_t ev = pipe_ticket_event(p, t);
     cudaError_t e = cudaEventSynchronize(ev);
     if (e != cudaSuccess) return cuda_fail(p->ctx, "retiring a pipeline ticket", e);
+    if (t > ckv_pipe::kTickets) p->retired.store(t - ckv_pipe::kTickets);
     e = cudaEventRecord(ev, stream);
     if (e != cudaSuccess) return cuda_fail(p->ctx, "recording a pipeline ticket", e);
     p->next_ticket = t + 1;
@@ -1616,7 +1643,8 @@ int ckv_pipe_done(ckv_pipe* p, uint64_t ticket) {
     DeviceGuard guard(p->ctx->device);
     const cudaError_t e = cudaEventQuery(pipe_ticket_event(p, ticket));
     if (e == cudaSuccess) return 1;
-    if (e == cudaErrorNotReady) return 0;
+    // the event may already be newer work's: the ticket retired meanwhile
+    if (e == cudaErrorNotReady) return pipe_retired(p, ticket) ? 1 : 0;
     return -1;
 }
 

@@ -103,6 +103,17 @@ struct EncodeArgs {
     float* bounds;
     uint32_t* status;
     ShiftMul mul;
+    // Failure-path test hook: the cluster that owns unit withhold_unit
+    // (~0u: none) never completes that unit's bound exchange, and its waits
+    // on other roles and CTAs give up after test_polls polls.
+    uint32_t withhold_unit;
+    uint32_t test_polls;
+};
+
+// Poll limits of one CTA's waits on other roles and CTAs.
+struct Limits {
+    uint32_t polls;   // suspending waits (mbarrier try_wait)
+    uint32_t spins;   // non-suspending waits (cluster exchanges)
 };
 
 // This CTA's share of a unit of n elements.
@@ -461,15 +472,15 @@ __device__ __forceinline__ float elem_at(const uint8_t* blk, int v) {
 // of it, and publishes each unit's status word after its pack.  Returns once
 // the copies it issued have landed.
 template <typename T>
-__device__ void produce(const EncodeArgs& a, uint32_t count, uint32_t first, uint32_t stride,
-                        uint32_t rank, uint32_t csize, uint8_t* smem, Sync& sy) {
+__device__ void produce(const EncodeArgs& a, const Limits& lim, uint32_t count, uint32_t first,
+                        uint32_t stride, uint32_t rank, uint32_t csize, uint8_t* smem, Sync& sy) {
     uint32_t last[kBufs];
     for (uint32_t b = 0; b < kBufs; ++b) last[b] = ~0u;
     for (uint32_t j = 0; j < count + kBufs; ++j) {
         const uint32_t b = j % kBufs;
         if (j >= kBufs) {
             const uint32_t jj = j - kBufs;
-            if (!mbar_wait_bounded(&sy.packed[b], (jj / kBufs) & 1u, kWaitPolls)) {
+            if (!mbar_wait_bounded(&sy.packed[b], (jj / kBufs) & 1u, lim.polls)) {
                 sy.broken = 1;
                 break;
             }
@@ -510,8 +521,8 @@ __device__ void produce(const EncodeArgs& a, uint32_t count, uint32_t first, uin
 // ---- analysis warps -------------------------------------------------------------
 
 template <typename T>
-__device__ void analyse(const EncodeArgs& a, uint32_t count, uint32_t first, uint32_t stride,
-                        cg::cluster_group& cluster, uint8_t* smem, Sync& sy) {
+__device__ void analyse(const EncodeArgs& a, const Limits& lim, uint32_t count, uint32_t first,
+                        uint32_t stride, cg::cluster_group& cluster, uint8_t* smem, Sync& sy) {
     using L = Layout<T>;
     constexpr uint32_t BB = kBlock * Traits<T>::kBytes;  // input bytes per block
     const uint32_t rank = cluster.block_rank();
@@ -527,7 +538,7 @@ __device__ void analyse(const EncodeArgs& a, uint32_t count, uint32_t first, uin
         uint8_t* rates = smem + L::kRates + b * L::kRatesStride;
 
         // -- slice on chip, block extremes, slice extremes to the cluster
-        const bool landed = mbar_wait_bounded(&sy.full[b], (j / kBufs) & 1u, kWaitPolls);
+        const bool landed = mbar_wait_bounded(&sy.full[b], (j / kBufs) & 1u, lim.polls);
         const Job job = sy.job[b];
         const Slice& s = job.s;
         const uint32_t u = job.u;
@@ -618,12 +629,12 @@ __device__ void analyse(const EncodeArgs& a, uint32_t count, uint32_t first, uin
                 hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, d));
             }
             if (lane == 0) mbar_arrive_expect_tx(&sy.ext_bar[x], csize * sizeof(float2));
-            if (static_cast<uint32_t>(lane) < csize)
+            if (static_cast<uint32_t>(lane) < csize && !(u == a.withhold_unit && rank == 0))
                 st_async_f32x2(cluster_addr(&sy.ext[x][rank], lane), lo, hi,
                                cluster_addr(&sy.ext_bar[x], lane));
             // -- unit extremes -> bound
             const bool ok =
-                __all_sync(0xffffffffu, mbar_spin_bounded(&sy.ext_bar[x], xpar, kWaitSpins));
+                __all_sync(0xffffffffu, mbar_spin_bounded(&sy.ext_bar[x], xpar, lim.spins));
             lo = FLT_MAX;
             hi = -FLT_MAX;
             if (static_cast<uint32_t>(lane) < csize) {
@@ -714,7 +725,7 @@ __device__ void analyse(const EncodeArgs& a, uint32_t count, uint32_t first, uin
                              cluster_addr(&sy.tot_bar[x], lane));
             // -- slice totals -> this slice's output offset
             const bool ok =
-                __all_sync(0xffffffffu, mbar_spin_bounded(&sy.tot_bar[x], xpar, kWaitSpins));
+                __all_sync(0xffffffffu, mbar_spin_bounded(&sy.tot_bar[x], xpar, lim.spins));
             const uint32_t tv = static_cast<uint32_t>(lane) < csize ? sy.tot[x][lane] : 0u;
             uint32_t base = static_cast<uint32_t>(lane) < rank ? tv : 0u, all = tv;
 #pragma unroll
@@ -761,7 +772,8 @@ __device__ __forceinline__ void copy_out(const uint32_t* src, uint32_t* dst, uin
 }
 
 template <typename T>
-__device__ void pack(uint32_t count, const ShiftMul& mul, uint8_t* smem, Sync& sy) {
+__device__ void pack(const Limits& lim, uint32_t count, const ShiftMul& mul, uint8_t* smem,
+                     Sync& sy) {
     using L = Layout<T>;
     constexpr uint32_t BB = kBlock * Traits<T>::kBytes;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -770,7 +782,7 @@ __device__ void pack(uint32_t count, const ShiftMul& mul, uint8_t* smem, Sync& s
     uint32_t rot = 0;   // chunk c of this unit goes to pack warp (c + rot) % kPWarps
     for (uint32_t j = 0; j < count; ++j) {
         const uint32_t b = j % kBufs;
-        const bool ok = mbar_wait_bounded(&sy.ready[b], (j / kBufs) & 1u, kWaitPolls);
+        const bool ok = mbar_wait_bounded(&sy.ready[b], (j / kBufs) & 1u, lim.polls);
         if (!__all_sync(0xffffffffu, ok)) {
             sy.broken = 1;
             return;
@@ -853,6 +865,8 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_kernel(EncodeArgs a) {
     const uint32_t first = blockIdx.y, stride = gridDim.y;
     const uint32_t count =
         first < a.num_units ? (a.num_units - first + stride - 1) / stride : 0u;
+    const bool tested = a.withhold_unit != ~0u && first == a.withhold_unit % stride;
+    const Limits lim{tested ? a.test_polls : kWaitPolls, tested ? a.test_polls : kWaitSpins};
 
     if (tid == 0) {
         for (uint32_t b = 0; b < kBufs; ++b) {
@@ -871,11 +885,11 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_kernel(EncodeArgs a) {
     cluster_barrier();   // every barrier of the cluster initialised before any arrive
 
     if (warp == kProducerWarp) {
-        if ((tid & 31) == 0) produce<T>(a, count, first, stride, rank, csize, smem, sy);
+        if ((tid & 31) == 0) produce<T>(a, lim, count, first, stride, rank, csize, smem, sy);
     } else if (warp >= kPWarps) {
-        analyse<T>(a, count, first, stride, cluster, smem, sy);
+        analyse<T>(a, lim, count, first, stride, cluster, smem, sy);
     } else {
-        pack<T>(count, a.mul, smem, sy);
+        pack<T>(lim, count, a.mul, smem, sy);
     }
     // No peer touches this CTA's shared memory once every CTA is here.
     cluster_barrier();
@@ -950,7 +964,8 @@ cudaError_t launch_encode_t(const EncodeLaunch& l, cudaStream_t stream) {
     cudaError_t err = cluster_shape<T>(c_min, &shape);
     if (err != cudaSuccess) return err;
     EncodeArgs args{l.units, l.maps, l.num_units, l.relative ? 1u : 0u,
-                    l.sizes, l.bounds, l.status, shift_mul()};
+                    l.sizes, l.bounds, l.status, shift_mul(),
+                    l.test_polls ? l.withhold_unit : ~0u, l.test_polls};
     cudaLaunchConfig_t cfg = {};
     const uint32_t clusters = min(min(l.num_units, shape.clusters), 65535u);
     cfg.gridDim = dim3(shape.c, clusters, 1);

@@ -20,6 +20,11 @@ struct EncodeLaunch {
     float* bounds;             // device-visible, one per unit
     uint32_t* status;          // device-visible, one per unit
     ElemType type;
+    // Failure-path test hook (0: off): the cluster that owns unit
+    // withhold_unit never completes that unit's bound exchange, and its
+    // waits give up after test_polls polls (kErrTimeout on its units).
+    uint32_t withhold_unit;
+    uint32_t test_polls;
 };
 
 struct DecodeLaunch {

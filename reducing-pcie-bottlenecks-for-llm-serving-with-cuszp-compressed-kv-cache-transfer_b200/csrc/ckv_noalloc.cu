@@ -8,16 +8,27 @@
 // needs a context with grow-only workspaces; this entry point needs none.
 //
 // All of its scratch -- the unit descriptors, the copied pointer tables, the
-// per-unit sizes, bounds and status words -- lives in one file-scope
-// __device__ array of fixed size (kMaxUnits units, about 270 KB), which every
-// GPU that loads the library holds until the process exits.  Host code
-// cannot pass the array's name to a kernel (in host code it is a host-side
-// stand-in, not a device address), so the first call on each device looks
-// up the device address with cudaGetSymbolAddress, with that device
-// current, and caches it; that first call should therefore come before any
-// stream capture.  Every call reuses the same array, so calls that overlap
-// on the GPU (on different streams, or from different threads) race; the
-// status words that must start at zero are cleared by every call.
+// per-unit sizes, bounds and status words, and one built-in 32-element unit
+// for the set-up call -- lives in one file-scope __device__ array of fixed
+// size (kMaxUnits units, about 270 KB).  Host code cannot pass the array's
+// name to a kernel (in host code it is a host-side stand-in, not a device
+// address), so the device address is looked up with cudaGetSymbolAddress,
+// with that device current, once per device, and cached.
+//
+// CUDA loads a library's modules lazily: a device's copy of the array, and
+// the code of every kernel this entry point launches, are only created on
+// that device at first use, which allocates device memory.  A launch may
+// also grow the device's local-memory reservation.  The set-up call (batch
+// 0) does all of that at a moment the caller chooses: it looks up the
+// array, then compresses the built-in unit (in and out of the array itself)
+// through every launch a real call makes.  Make it once per device at
+// start-up, before the engine reserves its HBM and before any stream
+// capture; later calls then allocate nothing.  A real call made first does
+// the same set-up implicitly.
+//
+// Every call reuses the same array, so calls that overlap on the GPU (on
+// different streams, or from different threads) race; the status words that
+// must start at zero are cleared by every call.
 #include "ckv.h"
 
 #include <cuda_runtime.h>
@@ -43,6 +54,9 @@ struct Scratch {
     float bounds[kMaxUnits];
     uint32_t status[kMaxUnits];
     uint32_t status_all;
+    // the set-up call's unit: 32 BF16 zeros in, one compressed stream out
+    __align__(16) uint16_t warm_in[32];
+    __align__(16) uint8_t warm_out[2048];
 };
 
 static __device__ __align__(256) unsigned char g_scratch[sizeof(Scratch)];
@@ -95,12 +109,89 @@ Scratch* scratch_address(int device) {
 }  // namespace
 }  // namespace ckv
 
+namespace ckv {
+namespace {
+
+// One compress of `batch` units through the scratch array at `s`.
+ckv_status run_noalloc(Scratch* s, const void* const* inputs, uint8_t* const* outputs,
+                       const float* eps, size_t batch, size_t n, size_t capacity,
+                       float error_bound, int relative, size_t* sizes, float* bounds,
+                       cudaStream_t stream) {
+    cudaError_t e = cudaMemcpyAsync(s->inputs, inputs, batch * sizeof(void*),
+                                    cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(s->outputs, outputs, batch * sizeof(void*), cudaMemcpyHostToDevice,
+                            stream);
+    if (e == cudaSuccess && eps)
+        e = cudaMemcpyAsync(s->eps, eps, batch * sizeof(float), cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return CKV_ERR_CUDA;
+    const uint32_t b = static_cast<uint32_t>(batch);
+    note_launch();
+    fill_units<<<(b + 255) / 256, 256, 0, stream>>>(s, b, static_cast<uint32_t>(n), capacity,
+                                                    error_bound, eps ? 1 : 0);
+    if (cudaGetLastError() != cudaSuccess) return CKV_ERR_CUDA;
+
+    EncodeLaunch l{};
+    l.units = s->units;
+    l.maps = s->maps;
+    l.num_units = b;
+    l.max_n = static_cast<uint32_t>(n);
+    l.relative = relative != 0;
+    l.sizes = s->sizes;
+    l.bounds = s->bounds;
+    l.status = s->status;
+    l.type = ElemType::kBF16;
+    if (launch_encode(l, stream) != cudaSuccess) return CKV_ERR_CUDA;
+    note_launch();
+    fold_status<<<1, 256, 0, stream>>>(s, b);
+    if (cudaGetLastError() != cudaSuccess) return CKV_ERR_CUDA;
+
+    uint32_t bits = 0;
+    e = cudaMemcpyAsync(sizes, s->sizes, batch * sizeof(uint64_t), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(bounds, s->bounds, batch * sizeof(float), cudaMemcpyDeviceToHost,
+                            stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(&bits, &s->status_all, sizeof(bits), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return CKV_ERR_CUDA;
+    if (bits & kErrCapacity) return CKV_ERR_CAPACITY;
+    if (bits & kErrTimeout) return CKV_ERR_CUDA;
+    if (bits) return CKV_ERR_INTERNAL;
+    return CKV_OK;
+}
+
+// The set-up call: the built-in unit of 32 zeros through every launch.
+ckv_status warm_up(Scratch* s, cudaStream_t stream) {
+    const uint16_t zeros[32] = {};
+    if (cudaMemcpyAsync(s->warm_in, zeros, sizeof(zeros), cudaMemcpyHostToDevice, stream) !=
+        cudaSuccess)
+        return CKV_ERR_CUDA;
+    const void* in[1] = {s->warm_in};
+    uint8_t* out[1] = {s->warm_out};
+    size_t size = 0;
+    float bound = 0.0f;
+    return run_noalloc(s, in, out, nullptr, 1, 32, sizeof(s->warm_out), 1e-4f, 1, &size, &bound,
+                       stream);
+}
+
+}  // namespace
+}  // namespace ckv
+
 extern "C" ckv_status ckv_compress_batch_fixed_bf16_noalloc(
     const void* const* inputs, uint8_t* const* outputs, const float* eps, size_t batch,
     size_t n, size_t capacity, float error_bound, int relative, size_t* sizes, float* bounds,
     void* stream_ptr) {
     using ckv::Scratch;
-    if (!inputs || !outputs || !sizes || !bounds || batch == 0 || n == 0 || n > 0xffffffffu)
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (batch == 0) {   // set-up call: every other argument is ignored
+        int device = 0;
+        if (cudaGetDevice(&device) != cudaSuccess) return CKV_ERR_CUDA;
+        Scratch* s = ckv::scratch_address(device);
+        if (!s) return CKV_ERR_CUDA;
+        return ckv::warm_up(s, stream);
+    }
+    if (!inputs || !outputs || !sizes || !bounds || n == 0 || n > 0xffffffffu)
         return CKV_ERR_ARGUMENT;
     if (batch > ckv::kMaxUnits) {
         std::fprintf(stderr,
@@ -115,52 +206,10 @@ extern "C" ckv_status ckv_compress_batch_fixed_bf16_noalloc(
         if (!inputs[i] || !outputs[i] || (reinterpret_cast<uintptr_t>(inputs[i]) & 1u) ||
             (reinterpret_cast<uintptr_t>(outputs[i]) & 3u))
             return CKV_ERR_ARGUMENT;
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) return CKV_ERR_CUDA;
     Scratch* s = ckv::scratch_address(device);
     if (!s) return CKV_ERR_CUDA;
-
-    cudaError_t e = cudaMemcpyAsync(s->inputs, inputs, batch * sizeof(void*),
-                                    cudaMemcpyHostToDevice, stream);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(s->outputs, outputs, batch * sizeof(void*), cudaMemcpyHostToDevice,
-                            stream);
-    if (e == cudaSuccess && eps)
-        e = cudaMemcpyAsync(s->eps, eps, batch * sizeof(float), cudaMemcpyHostToDevice, stream);
-    if (e != cudaSuccess) return CKV_ERR_CUDA;
-    const uint32_t b = static_cast<uint32_t>(batch);
-    ckv::note_launch();
-    ckv::fill_units<<<(b + 255) / 256, 256, 0, stream>>>(s, b, static_cast<uint32_t>(n),
-                                                          capacity, error_bound, eps ? 1 : 0);
-    if (cudaGetLastError() != cudaSuccess) return CKV_ERR_CUDA;
-
-    ckv::EncodeLaunch l{};
-    l.units = s->units;
-    l.maps = s->maps;
-    l.num_units = b;
-    l.max_n = static_cast<uint32_t>(n);
-    l.relative = relative != 0;
-    l.sizes = s->sizes;
-    l.bounds = s->bounds;
-    l.status = s->status;
-    l.type = ckv::ElemType::kBF16;
-    if (ckv::launch_encode(l, stream) != cudaSuccess) return CKV_ERR_CUDA;
-    ckv::note_launch();
-    ckv::fold_status<<<1, 256, 0, stream>>>(s, b);
-    if (cudaGetLastError() != cudaSuccess) return CKV_ERR_CUDA;
-
-    uint32_t bits = 0;
-    e = cudaMemcpyAsync(sizes, s->sizes, batch * sizeof(uint64_t), cudaMemcpyDeviceToHost, stream);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(bounds, s->bounds, batch * sizeof(float), cudaMemcpyDeviceToHost,
-                            stream);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(&bits, &s->status_all, sizeof(bits), cudaMemcpyDeviceToHost, stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
-    if (e != cudaSuccess) return CKV_ERR_CUDA;
-    if (bits & ckv::kErrCapacity) return CKV_ERR_CAPACITY;
-    if (bits & ckv::kErrTimeout) return CKV_ERR_CUDA;
-    if (bits) return CKV_ERR_INTERNAL;
-    return CKV_OK;
+    return ckv::run_noalloc(s, inputs, outputs, eps, batch, n, capacity, error_bound, relative,
+                            sizes, bounds, stream);
 }

@@ -108,3 +108,25 @@ def test_python_surface_matches_reference():
         assert params == args, name
     assert m.CuSZpWrapper.estimate_compressed_buffer_size(4096) == 8192
     assert inspect.signature(m.CuSZpWrapper.compress).parameters["eps_override"].default == -1.0
+
+
+def test_enum_values_agree_everywhere():
+    """include/ckv.h, the stand-in cuSZp header the reference's kernels are
+    built with (oracle/ref_shim/cuSZp.h) and the Python enums give every
+    cuszp_dim_t / cuszp_mode_t / cuszp_type_t name the same value, in the
+    reference's binding order (pybind11_bindings.cpp:13-28), so a caller that
+    passes its configuration's encoding_mode straight through reads FIXED as
+    FIXED."""
+    import _ckv
+    import cuszp_wrapper_cpp as m
+
+    header = (ROOT / "include" / "ckv.h").read_text()
+    ckv = {k: int(v) for k, v in re.findall(r"^#define CKV_((?:DIM|MODE|TYPE)_\w+) (\d+)", header, re.M)}
+    shim = (ROOT / "oracle" / "ref_shim" / "cuSZp.h").read_text()
+    ref = {k: int(v) for k, v in re.findall(r"CUSZP_((?:DIM|MODE|TYPE)_\w+) = (\d+)", shim)}
+    assert ckv == ref and len(ckv) == 8
+    assert ckv == {"DIM_1D": 0, "DIM_2D": 1, "DIM_3D": 2, "MODE_FIXED": 0, "MODE_PLAIN": 1,
+                   "MODE_OUTLIER": 2, "TYPE_FLOAT": 0, "TYPE_DOUBLE": 1}
+    for enum in (m.CuszpDim, m.CuszpMode, m.CuszpType):
+        for e in enum:
+            assert int(e) == ckv[e.name] == getattr(_ckv, e.name), e.name

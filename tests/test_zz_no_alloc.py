@@ -65,6 +65,41 @@ def test_noalloc_matches_regular_entry_point(count, n, eb):
             assert torch.equal(out[i, :s], ref_out[i, :s]), f"call {call}, page {i}"
 
 
+def test_noalloc_allocates_no_device_memory_after_setup():
+    """After the set-up call (batch 0), compress calls leave the driver's free
+    device memory unchanged: torch.cuda.mem_get_info reads cudaMemGetInfo,
+    which sees allocations that torch's caching allocator would hide."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    import _ckv
+
+    lib = _ckv.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    count, n, eb = 8, 229376, 1e-5
+    pages = _pages(count, n, seed=7).to(dev)
+    cap = int(lib.ckv_estimate_compressed_buffer_size(n * 4))
+    out = torch.empty((count, cap), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    inputs = _ckv.ptr_array([pages[i].data_ptr() for i in range(count)])
+    outputs = _ckv.ptr_array([out[i].data_ptr() for i in range(count)])
+    sizes = (C.c_size_t * count)()
+    bounds = (C.c_float * count)()
+    torch.cuda.synchronize(dev)
+
+    assert lib.ckv_compress_batch_fixed_bf16_noalloc(
+        None, None, None, 0, 0, 0, 0.0, 0, None, None, stream) == 0
+    torch.cuda.synchronize(dev)
+    free_before, _ = torch.cuda.mem_get_info(dev)
+    for call in range(3):
+        status = lib.ckv_compress_batch_fixed_bf16_noalloc(
+            inputs, outputs, None, count, n, cap, eb, 1, sizes, bounds, stream)
+        assert status == 0, f"call {call}: status {status}"
+    torch.cuda.synchronize(dev)
+    free_after, _ = torch.cuda.mem_get_info(dev)
+    assert free_after == free_before, f"{free_before - free_after} bytes of device memory taken"
+
+
 def test_noalloc_rejects_batches_above_its_scratch():
     if not torch.cuda.is_available():
         pytest.skip("CUDA required")
