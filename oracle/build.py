@@ -36,13 +36,15 @@ REF_PY = HERE / "_ref" / "py"
 _env_root = os.environ.get("CKV_REFERENCE_ROOT")
 REFERENCE_ROOT = Path(_env_root) if _env_root else HERE.parent.parent / "reference"
 REF_KERNEL = REFERENCE_ROOT / "integration" / "cuszp_wrapper" / "cuszp_batched_fixed.cu"
-# reference module -> its byte-compiled place under REF_PY
+# reference module -> its byte-compiled place under REF_PY (".refpyc": the
+# tree is copied to the GPU box without *.pyc files, and nothing imports
+# these by accident; tests load them through an explicit finder)
 CONNECTOR_MODULES = {
     "integration/compression_pipeline/vllm_v1_compressed_offload.py":
-        "integration/compression_pipeline/vllm_v1_compressed_offload.pyc",
+        "integration/compression_pipeline/vllm_v1_compressed_offload.refpyc",
     "integration/compression_pipeline/native_lossless.py":
-        "integration/compression_pipeline/native_lossless.pyc",
-    "tests/test_vllm_v1_compressed_offload.py": "ref_tests/test_vllm_v1_compressed_offload.pyc",
+        "integration/compression_pipeline/native_lossless.refpyc",
+    "tests/test_vllm_v1_compressed_offload.py": "ref_tests/test_vllm_v1_compressed_offload.refpyc",
 }
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
@@ -95,11 +97,10 @@ def build_ref(force: bool = False) -> Path | None:
 def stage_connector(force: bool = False) -> Path | None:
     """Byte-compile the reference's connector and its tests into REF_PY.
 
-    Sourceless ``.pyc`` files in the legacy location import without their
-    sources (Python's path finder loads ``name.pyc`` from a directory), so
-    the GPU box, which has no reference checkout, can still run the
-    unmodified connector.  Returns REF_PY, or None where neither the
-    checkout nor an earlier staging exists."""
+    The compiled modules load without their sources (tests use Python's
+    sourceless loader on them), so the GPU box, which has no reference
+    checkout, can still run the unmodified connector.  Returns REF_PY, or
+    None where neither the checkout nor an earlier staging exists."""
     import py_compile
 
     sources = {REFERENCE_ROOT / src: REF_PY / dst for src, dst in CONNECTOR_MODULES.items()}

@@ -10,7 +10,8 @@ unchanged.
 
 The connector and its tests are the reference's files, byte-compiled where
 they lie by oracle/build.py (stage_connector) into oracle/_ref/py, which
-travels with the tree to the GPU box (the box has no reference checkout).
+travels with the tree to the GPU box (the box has no reference checkout);
+a finder on sys.meta_path loads them from there.
 Out of scope and therefore not run: the ``plain`` and ``outlier`` modes of
 test_real_cuszp_page_round_trip_through_vllm_specs (upstream cuSZp encoders
 this build does not implement; their ``compress`` returns False).
@@ -18,6 +19,7 @@ this build does not implement; their ``compress`` returns False).
 from __future__ import annotations
 
 import importlib
+import importlib.abc
 import importlib.machinery
 import importlib.util
 import sys
@@ -28,7 +30,8 @@ import pytest
 ROOT = Path(__file__).resolve().parents[1]
 PKG = ROOT / "reducing-pcie-bottlenecks-for-llm-serving-with-cuszp-compressed-kv-cache-transfer_b200"
 REF_PY = ROOT / "oracle" / "_ref" / "py"
-REF_TESTS = REF_PY / "ref_tests" / "test_vllm_v1_compressed_offload.pyc"
+REF_TESTS = REF_PY / "ref_tests" / "test_vllm_v1_compressed_offload.refpyc"
+REF_PACKAGES = ("integration", "integration.compression_pipeline")
 
 # (reference test function, its parameters); line numbers are the function's
 # line in the reference's tests/test_vllm_v1_compressed_offload.py
@@ -67,14 +70,42 @@ CODEC_CASES = {
 }
 
 
+class _PackageLoader(importlib.abc.Loader):
+    """The reference's package directories (no code of their own)."""
+
+    def create_module(self, spec):
+        return None
+
+    def exec_module(self, module):
+        pass
+
+
+class _StagedFinder(importlib.abc.MetaPathFinder):
+    """Finds the reference's staged, byte-compiled connector modules."""
+
+    def find_spec(self, name, path=None, target=None):
+        rel = name.replace(".", "/")
+        if name in REF_PACKAGES:
+            spec = importlib.util.spec_from_loader(name, _PackageLoader(), is_package=True)
+            spec.submodule_search_locations = [str(REF_PY / rel)]
+            return spec
+        if name.startswith("integration."):
+            f = REF_PY / (rel + ".refpyc")
+            if f.exists():
+                return importlib.util.spec_from_loader(
+                    name, importlib.machinery.SourcelessFileLoader(name, str(f)))
+        return None
+
+
 def _staged():
     if not REF_TESTS.exists():
         pytest.skip("reference connector not staged in oracle/_ref/py "
                     "(run oracle/build.py where a reference checkout exists)")
-    for p in (str(REF_PY), str(PKG)):   # this package first: its cuszp_wrapper_cpp
-        if p in sys.path:
-            sys.path.remove(p)
-        sys.path.insert(0, p)
+    if str(PKG) in sys.path:   # this package first: its cuszp_wrapper_cpp
+        sys.path.remove(str(PKG))
+    sys.path.insert(0, str(PKG))
+    if not any(isinstance(f, _StagedFinder) for f in sys.meta_path):
+        sys.meta_path.insert(0, _StagedFinder())
 
 
 def _reference_tests():
@@ -101,7 +132,7 @@ def test_reference_connector_binds_this_wrapper():
     assert offload.cuszp_wrapper_cpp is ours
     assert Path(ours.__file__).resolve().parent == PKG.resolve()
     assert offload.CUSZP_MODES["fixed"] == ours.CuszpMode.MODE_FIXED
-    assert Path(offload.__file__).suffix == ".pyc"
+    assert Path(offload.__file__).suffix == ".refpyc"
 
 
 @pytest.mark.gpu
