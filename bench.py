@@ -257,6 +257,53 @@ def cpu_baseline(host_pages: torch.Tensor, budget_s: float = 10.0) -> dict:
             "restore_gbps": round(raw * reps / sum(dec_t) / 1e9, 3)}
 
 
+DIRECTION_KEYS = ("store_gbps", "restore_gbps", "overlapped_gbps", "raw_d2h_gbps",
+                  "raw_h2d_gbps", "store_vs_raw_d2h", "restore_vs_raw_h2d", "compression_ratio",
+                  "restore_ok")
+
+
+def per_config_summary(world, line, c2_dirs, e2e, c1_pipe, c3, streamed) -> dict:
+    """Every BASELINE.json config with host copies, per direction: the store
+    alone and the restore alone (uncompressed GB/s, all ranks) next to raw
+    one-way page-locked copies of the same pages, and both directions in
+    flight together."""
+    out = {}
+    if c1_pipe:
+        for key in ("jobs_per_call_1", "jobs_per_call_16"):
+            if key in c1_pipe:
+                out[f"C1_{key}"] = {k: c1_pipe[key].get(k) for k in DIRECTION_KEYS}
+    if c2_dirs:
+        c2 = {k: c2_dirs.get(k) for k in DIRECTION_KEYS}
+        c2["overlapped_gbps"] = round(e2e, 3)
+        c2["compression_ratio"] = line.get("compression_ratio")
+        c2["restore_ok"] = bool(line.get("store_restore_ok")) and bool(
+            line["e2e"].get("restore_matches_kernel_path"))
+        out["C2"] = c2
+    if c3:
+        out["C3"] = {k: c3.get(k) for k in DIRECTION_KEYS}
+    for name, leg in (streamed or {}).items():
+        out[name] = ({k: leg.get(k) for k in DIRECTION_KEYS} if "skipped" not in leg
+                     else {"skipped": leg["skipped"]})
+        if "skipped" not in leg:
+            out[name]["n_gpus"] = leg.get("n_gpus")
+    for name, v in out.items():
+        if v.get("restore_gbps") and v.get("raw_h2d_gbps"):
+            v["restore_beats_raw_h2d"] = v["restore_gbps"] > v["raw_h2d_gbps"]
+    out["n_gpus"] = world
+    return out
+
+
+def config_block(pages: int) -> dict:
+    """The workload description both arms print (identical, so the two lines
+    compare as the same configuration)."""
+    return {"workload": "C2: Qwen2.5-1.5B KV at 4k context, 256 pages x 229376 BF16 "
+                        "([2,28,2,16,128]), REL eb 1e-5, one store + one restore per step",
+            "pages_per_gpu": pages, "elements_per_page": PAGE_NUMEL,
+            "error_bound": EPS, "relative": True,
+            "l2_flush": "256 MB write between timed steps",
+            "parallelism": "one process per GPU, pages sharded, no data-path collective"}
+
+
 def reference_arm(args, world: int) -> dict:
     """The reference arm: the reference's path has no CPU implementation of
     its own (its codec is CUDA), so the C restatement of its kernels
@@ -299,10 +346,7 @@ def reference_arm(args, world: int) -> dict:
         "ms_per_step": round(t * 1e3 / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32/u32",
         "data": "synthetic (seeded CPU generation, BASELINE.json configs[1] shapes)",
-        "config": {"workload": "C2: Qwen2.5-1.5B KV at 4k context, 256 pages x 229376 BF16 "
-                               "([2,28,2,16,128]), REL eb 1e-5, one store + one restore per step",
-                   "pages_per_gpu": args.pages, "elements_per_page": PAGE_NUMEL,
-                   "error_bound": EPS, "relative": True},
+        "config": config_block(args.pages),
         "compression_ratio": round(raw / max(1, comp), 4),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
@@ -541,6 +585,31 @@ class OurCodec:
                     "pipe join")
         main.wait_stream(self.side)
         return a["total"].value, restored
+
+    def step_store_only(self):
+        """One direction alone: every page stored into host slab 0 (device to
+        host), nothing else on the link."""
+        main = torch.cuda.current_stream(self.device)
+        a = self.hmeta[0]
+        t_store = C.c_uint64(0)
+        self._check(self.lib.ckv_pipe_store_bf16(
+            self.pipe, self.in_ptrs, None, self.count, self.n, self.hslab[0].data_ptr(),
+            self.hslab[0].numel(), a["offsets"], a["sizes"], a["bounds"], C.byref(a["total"]),
+            self.t_restore, C.byref(t_store), main.cuda_stream), "pipe store")
+        self.t_store = t_store.value
+        self._check(self.lib.ckv_pipe_join(self.pipe, self.t_store, main.cuda_stream), "pipe join")
+        return a["total"].value
+
+    def step_restore_only(self):
+        """The other direction alone: host slab 0 restored into the pages."""
+        main = torch.cuda.current_stream(self.device)
+        a = self.hmeta[0]
+        t_rest = C.c_uint64(0)
+        self._check(self.lib.ckv_pipe_restore_bf16(
+            self.pipe, self.hslab[0].data_ptr(), a["offsets"], a["sizes"], a["bounds"], self.count,
+            self.n, self.dst_e2e, self.t_store, C.byref(t_rest), main.cuda_stream), "pipe restore")
+        self.t_restore = t_rest.value
+        return a["total"].value
 
     def e2e_matches(self) -> bool:
         torch.cuda.synchronize(self.device)
@@ -820,8 +889,262 @@ def c1_leg(codec, steps: int, flush: torch.Tensor, device) -> dict:
     return out
 
 
+def pipe_pages_leg(codec, pages: torch.Tensor, eps: float, steps: int, flush: torch.Tensor,
+                   device) -> dict:
+    """Uniform pages through the store / restore pipeline (one chunk per call):
+    the store alone, the restore alone, a store overlapped with the restore of
+    the previous step's slab, and raw pinned copies of the same bytes one way
+    at a time; the restore is checked against the pages' bounds."""
+    lib, ck = codec.lib, codec.ckv
+    count, n = pages.shape
+    raw = count * n * 2
+    pipe = C.c_void_p()
+    codec._check(lib.ckv_pipe_create(codec.ctx, count, C.byref(pipe)), "pipe")
+    try:
+        cap = int(lib.ckv_pipe_host_capacity(count, n))
+        slabs = [torch.empty(cap, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        meta = [{"o": (C.c_size_t * count)(), "s": (C.c_size_t * count)(),
+                 "b": (C.c_float * count)(), "t": C.c_size_t(0)} for _ in range(2)]
+        dst = torch.zeros_like(pages)
+        src = ck.ptr_array([pages[i].data_ptr() for i in range(count)])
+        dptr = ck.ptr_array([dst[i].data_ptr() for i in range(count)])
+        epsa = (C.c_float * count)(*([eps] * count))
+        side = torch.cuda.Stream(device)
+        st = {"k": 0, "ts": 0, "tr": 0}
+
+        def store(k, stream):
+            a = meta[k]
+            t = C.c_uint64(0)
+            codec._check(lib.ckv_pipe_store_bf16(
+                pipe, src, epsa, count, n, slabs[k].data_ptr(), cap, a["o"], a["s"], a["b"],
+                C.byref(a["t"]), st["tr"], C.byref(t), stream), "pipe store")
+            st["ts"] = t.value
+            return a["t"].value
+
+        def restore(k, stream):
+            b = meta[k]
+            t = C.c_uint64(0)
+            codec._check(lib.ckv_pipe_restore_bf16(
+                pipe, slabs[k].data_ptr(), b["o"], b["s"], b["b"], count, n, dptr, st["ts"],
+                C.byref(t), stream), "pipe restore")
+            st["tr"] = t.value
+            return b["t"].value
+
+        def store_only():
+            main = torch.cuda.current_stream(device)
+            moved = store(0, main.cuda_stream)
+            codec._check(lib.ckv_pipe_join(pipe, st["ts"], main.cuda_stream), "join")
+            return moved
+
+        def restore_only():
+            return restore(0, torch.cuda.current_stream(device).cuda_stream)
+
+        def overlapped():
+            k = st["k"]
+            st["k"] += 1
+            main = torch.cuda.current_stream(device)
+            if k > 0:
+                side.wait_stream(main)
+                restore((k + 1) % 2, side.cuda_stream)
+            moved = store(k % 2, main.cuda_stream)
+            codec._check(lib.ckv_pipe_join(pipe, st["ts"], main.cuda_stream), "join")
+            main.wait_stream(side)
+            return moved
+
+        for fn in (store_only, restore_only):
+            for _ in range(3):
+                fn()
+        t_st, moved = timed_steps(store_only, steps, flush, device)
+        t_rs, _ = timed_steps(restore_only, steps, flush, device)
+        torch.cuda.synchronize(device)
+        b = torch.tensor(list(meta[0]["b"]), device=device).view(-1, 1)
+        ok = bool(((pages.float() - dst.float()).abs() <=
+                   b * 1.01 + 1e-7 + pages.float().abs() * 2.0 ** -8).all())
+        for _ in range(3):
+            overlapped()
+        t_ov, _ = timed_steps(overlapped, steps, flush, device)
+        t_d2h, t_h2d = raw_one_way(pages, steps, flush, device)
+        out = direction_fields(1, raw, steps, sum(t_st) / 1e3, sum(t_rs) / 1e3, raw, steps,
+                               t_d2h, t_h2d)
+        out.update({
+            "overlapped_gbps": round(job_rate(1, raw, steps, sum(t_ov) / 1e3), 3),
+            "ms_store": round(sum(t_st) / steps, 4), "ms_restore": round(sum(t_rs) / steps, 4),
+            "compression_ratio": round(raw / max(1, moved[-1]), 4),
+            "d2h_bytes_per_store": int(moved[-1]), "restore_ok": ok,
+        })
+        return out
+    finally:
+        torch.cuda.synchronize(device)
+        lib.ckv_pipe_destroy(pipe)
+
+
+def c1_pipeline(codec, steps: int, flush: torch.Tensor, device, batches=(1, 16)) -> dict:
+    """C1 with host copies: jobs of 64 one-layer units (8192 BF16 each, 1 MiB)
+    through the pipeline, one job per call and `batch` jobs per call (the
+    units of several jobs in one encode and one decode launch)."""
+    g = torch.Generator().manual_seed(0)
+    scale = torch.empty(2, HEADS, HEAD_DIM).log_normal_(0.0, 0.5, generator=g)
+    x = torch.randn(64, 2, TOKENS, HEADS, HEAD_DIM, generator=g) * scale[None, :, None, :, :]
+    job = x.to(torch.bfloat16).view(64, -1).to(device)
+    out = {"workload": "C1 with host copies: jobs of 64 units x 8192 BF16 (1 MiB), REL 1e-4, "
+                       "through ckv_pipe_store_bf16 / ckv_pipe_restore_bf16"}
+    for batch in batches:
+        out[f"jobs_per_call_{batch}"] = pipe_pages_leg(codec, job.repeat(batch, 1), 1e-4, steps,
+                                                       flush, device)
+    return out
+
+
+class _BlockSpec:
+    """A transfer spec as vLLM's GPULoadStoreSpec / CPULoadStoreSpec present
+    it to a handler: its block ids."""
+
+    def __init__(self, ids):
+        self.block_ids = np.asarray(ids, dtype=np.int64)
+
+
+def plugin_api_leg(codec, steps: int, flush: torch.Tensor, device) -> dict:
+    """The connector-facing API timed on the C2 pages: kv_offload's
+    CompressedCpuGpuOffloadingHandlers (vLLM's OffloadingHandler interface,
+    vllm_v1_compressed_offload.py:2365-2470) -- transfer_async of a store job
+    (GPU blocks -> CPU blocks) and of a load job (CPU blocks -> other GPU
+    blocks), each waited for with the handler's wait() -- next to the same
+    jobs through the C ABI (ckv_pipe_store_bf16 / ckv_pipe_restore_bf16 +
+    ckv_pipe_wait).  Both on the host clock (call to completion); the gap is
+    what the job layer (job header, slab pool, Python) costs."""
+    import kv_offload as ko
+    lib = codec.lib
+    count, n = codec.count, codec.n
+    raw = count * n * 2
+    kv = torch.empty(2 * count, n, dtype=torch.bfloat16, device=device)
+    kv[:count] = codec.pages
+    h = ko.CompressedCpuGpuOffloadingHandlers(kv, error_bound=EPS, device_id=device.index,
+                                              chunk_pages=count)
+    try:
+        gpu_src = _BlockSpec(range(count))
+        gpu_dst = _BlockSpec(range(count, 2 * count))
+        cpu = [_BlockSpec(range(count)), _BlockSpec(range(count, 2 * count))]
+        job = [0]
+
+        def timed(fn) -> float:
+            flush.zero_()
+            torch.cuda.synchronize(device)
+            t0 = time.perf_counter()
+            fn()
+            return time.perf_counter() - t0
+
+        def store(c):
+            job[0] += 1
+            assert h.gpu_to_cpu_handler.transfer_async(job[0], (gpu_src, cpu[c]))
+            return job[0]
+
+        def load(c):
+            job[0] += 1
+            assert h.cpu_to_gpu_handler.transfer_async(job[0], (cpu[c], gpu_dst))
+            return job[0]
+
+        def store_wait():
+            h.gpu_to_cpu_handler.wait({store(0)})
+
+        def load_wait():
+            h.cpu_to_gpu_handler.wait({load(0)})
+
+        state = {"k": 0}
+
+        def overlapped():
+            k = state["k"]
+            state["k"] += 1
+            ld = load((k + 1) % 2) if k > 0 else None
+            st = store(k % 2)
+            h.gpu_to_cpu_handler.wait({st})
+            if ld is not None:
+                h.cpu_to_gpu_handler.wait({ld})
+
+        collect = gc.isenabled()
+        gc.disable()
+        try:
+            for fn in (store_wait, load_wait, overlapped, overlapped, overlapped):
+                fn()
+            t_store = sum(timed(store_wait) for _ in range(steps))
+            t_load = sum(timed(load_wait) for _ in range(steps))
+            t_ov = sum(timed(overlapped) for _ in range(steps))
+            # the same jobs through the C ABI, host clock
+            a = codec.hmeta[0]
+            tick = C.c_uint64(0)
+
+            def abi_store():
+                codec._check(lib.ckv_pipe_store_bf16(
+                    codec.pipe, codec.in_ptrs, None, count, n, codec.hslab[0].data_ptr(),
+                    codec.hslab[0].numel(), a["offsets"], a["sizes"], a["bounds"],
+                    C.byref(a["total"]), codec.t_restore, C.byref(tick),
+                    torch.cuda.current_stream(device).cuda_stream), "pipe store")
+                codec.t_store = tick.value
+                codec._check(lib.ckv_pipe_wait(codec.pipe, codec.t_store), "pipe wait")
+
+            def abi_restore():
+                codec._check(lib.ckv_pipe_restore_bf16(
+                    codec.pipe, codec.hslab[0].data_ptr(), a["offsets"], a["sizes"], a["bounds"],
+                    count, n, codec.dst_e2e, codec.t_store, C.byref(tick),
+                    torch.cuda.current_stream(device).cuda_stream), "pipe restore")
+                codec.t_restore = tick.value
+                codec._check(lib.ckv_pipe_wait(codec.pipe, codec.t_restore), "pipe wait")
+
+            abi_store()
+            abi_restore()
+            t_abi_store = sum(timed(abi_store) for _ in range(steps))
+            t_abi_restore = sum(timed(abi_restore) for _ in range(steps))
+        finally:
+            if collect:
+                gc.enable()
+        torch.cuda.synchronize(device)
+        ok = bool(torch.equal(kv[count:].view(torch.int16), codec.restored.view(torch.int16)))
+        g = lambda t: round(raw * steps / t / 1e9, 3)   # noqa: E731
+        return {
+            "workload": "C2 pages through kv_offload.CompressedCpuGpuOffloadingHandlers "
+                        "(transfer_async + wait), host clock",
+            "store_gbps": g(t_store), "restore_gbps": g(t_load),
+            "overlapped_gbps": round(2 * raw * steps / t_ov / 1e9, 3),
+            "c_abi_store_gbps": g(t_abi_store), "c_abi_restore_gbps": g(t_abi_restore),
+            "handler_vs_c_abi_store": round(t_abi_store / t_store, 4),
+            "handler_vs_c_abi_restore": round(t_abi_restore / t_load, 4),
+            "restore_matches_kernel_path": ok,
+        }
+    finally:
+        h.shutdown()
+        del kv
+
+
+def compare_with_reference(codec, ref) -> dict:
+    """Our compressed pages against the reference kernels' on the same pages
+    and bounds: sizes, resolved bounds (bit for bit), the bytes the reference
+    defines (rate bytes of real blocks, [0, ceil(n/32)), and the payload,
+    [G*1024, size)), and the BF16 each decoder writes into zeroed pages."""
+    n, count = codec.n, codec.count
+    nb = (n + 31) // 32
+    hdr = (n + 32767) // 32768 * 1024
+    sizes_ok = [int(a) for a in codec.sizes] == [int(b) for b in ref.sizes]
+    bounds_ok = bool(np.array_equal(np.ctypeslib.as_array(codec.bounds).view(np.uint32),
+                                    np.asarray(ref.bounds, dtype=np.float32).view(np.uint32)))
+    ours = codec.slab.view(count, codec.cap)
+    theirs = ref.slab.view(count, ref.cap)
+    bytes_ok = sizes_ok and bool(torch.equal(ours[:, :nb], theirs[:, :nb]))
+    if bytes_ok:
+        for i in range(count):
+            size = int(codec.sizes[i])
+            if not torch.equal(ours[i, hdr:size], theirs[i, hdr:size]):
+                bytes_ok = False
+                break
+    codec.restored.zero_()
+    ref.restored.zero_()
+    codec.restore()
+    ref.restore()
+    torch.cuda.synchronize(codec.device)
+    decoded_ok = bool(torch.equal(codec.restored.view(torch.int16), ref.restored.view(torch.int16)))
+    return {"pages": count, "sizes_match": sizes_ok, "bounds_match": bounds_ok,
+            "bytes_match": bytes_ok, "decoded_match": decoded_ok}
+
+
 def reference_kernels_leg(device, pages_dev: torch.Tensor, steps: int, warmup: int,
-                          flush: torch.Tensor) -> dict | None:
+                          flush: torch.Tensor, codec=None) -> dict | None:
     """The reference's own kernels on the same GPU and pages: its batched BF16
     kernels (integration/cuszp_wrapper/cuszp_batched_fixed.cu, built unchanged
     in oracle/_ref) driven as CuSZpWrapper drives them, and its connector's
@@ -839,7 +1162,13 @@ def reference_kernels_leg(device, pages_dev: torch.Tensor, steps: int, warmup: i
     v_ms, _ = timed_steps(ref.step, steps, flush, device)
     e_ms, totals = timed_steps(ref.step_e2e, steps, flush, device)
     ok = ref.verify()
+    parity = None
+    if codec is not None:
+        ref.step()
+        codec.store()
+        parity = compare_with_reference(codec, ref)
     return {
+        "parity_with_ours": parity,
         "value": round(job_rate(1, raw, steps, sum(v_ms) / 1e3), 3),
         "ms_per_step": round(sum(v_ms) / steps, 4),
         "e2e": round(job_rate(1, raw, steps, sum(e_ms) / 1e3), 3),
@@ -865,7 +1194,10 @@ def c3_host_slabs(codec, repeat: int = 8) -> list[torch.Tensor]:
     high = [i for i in range(layers) if i not in C3_LOW_LAYERS]
     sel = (C.c_size_t * 2)(len(C3_LOW_LAYERS), len(high))
     cap = int(lib.ckv_pipe_host_capacity_groups(codec.count * repeat, sel, 2, prefix, epl))
-    return [torch.empty(cap, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+    import kv_offload as ko
+    slabs = [torch.empty(cap, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+    ko.prefault_pinned(slabs, codec.device)   # first use at full speed, no untimed pass
+    return slabs
 
 
 def layer_groups_c3(codec, steps: int, flush: torch.Tensor, device, repeat: int = 8,
@@ -935,9 +1267,40 @@ def layer_groups_c3(codec, steps: int, flush: torch.Tensor, device, repeat: int 
         times, totals = timed_steps(step, steps, flush, device)
         torch.cuda.synchronize(device)
         kms = [codec.kernel_ms(0), codec.kernel_ms(1)]
-        # the last restore read the slab of the second-to-last store: check
-        # it against that store's per-segment bounds
-        last = meta[state["k"] % 2]
+
+        # each direction alone: the store into slab 0, then its restore
+        def store_only():
+            main = torch.cuda.current_stream(device)
+            a = meta[0]
+            ts = C.c_uint64(0)
+            codec._check(lib.ckv_pipe_store_bf16_groups(
+                pipe, src_ptrs, count, idx, sel, G, prefix, layers, epl, eps,
+                slabs[0].data_ptr(), cap, a["o"], a["s"], a["b"], C.byref(a["t"]),
+                state["tr"], C.byref(ts), main.cuda_stream), "c3 store")
+            state["ts"] = ts.value
+            codec._check(lib.ckv_pipe_join(pipe, state["ts"], main.cuda_stream), "c3 join")
+
+        def restore_only():
+            main = torch.cuda.current_stream(device)
+            b = meta[0]
+            tr = C.c_uint64(0)
+            codec._check(lib.ckv_pipe_restore_bf16_groups(
+                pipe, slabs[0].data_ptr(), b["o"], b["s"], b["b"], count, idx, sel, G, prefix,
+                layers, epl, dptr, state["ts"], C.byref(tr), main.cuda_stream), "c3 restore")
+            state["tr"] = tr.value
+
+        store_only()
+        restore_only()
+        dir_steps = min(steps, 3)
+        t_st, _ = timed_steps(store_only, dir_steps, flush, device)
+        t_rs, _ = timed_steps(restore_only, dir_steps, flush, device)
+        torch.cuda.synchronize(device)
+        t_d2h, t_h2d = raw_one_way(pages, dir_steps, flush, device)
+        directions = direction_fields(1, raw_bytes, dir_steps, sum(t_st) / 1e3, sum(t_rs) / 1e3,
+                                      raw_bytes, dir_steps, t_d2h, t_h2d)
+        # the last restore read slab 0: check it against that store's
+        # per-segment bounds
+        last = meta[0]
         bnd = torch.tensor(list(last["b"]), device=device).view(count, G)
         owner = torch.zeros(layers, dtype=torch.long)
         owner[list(high)] = 1
@@ -953,10 +1316,11 @@ def layer_groups_c3(codec, steps: int, flush: torch.Tensor, device, repeat: int 
         segment_ratio = [
             round(count * prefix * len(s) * epl * 2 / max(1, sum(list(meta[0]["s"])[g::G])), 4)
             for g, (_b, s) in enumerate(groups)]
-        return {
+        out = {
             "workload": f"C3: {count} pages x {codec.n} BF16 (the C2 pages x{repeat}), "
                         "7 layers at REL 1e-5 + 21 at REL 1e-4, two segments per page",
             "e2e_gbps": round(job_rate(1, raw_bytes, steps, t), 3),
+            "overlapped_gbps": round(job_rate(1, raw_bytes, steps, t), 3),
             "ms_per_step": round(t * 1e3 / steps, 4),
             "compression_ratio": round(raw_bytes / stored, 4),
             "segment_ratios": {"1e-5": segment_ratio[0], "1e-4": segment_ratio[1]},
@@ -966,6 +1330,8 @@ def layer_groups_c3(codec, steps: int, flush: torch.Tensor, device, repeat: int 
             "path": "ckv_pipe_store_bf16_groups overlapped with ckv_pipe_restore_bf16_groups of "
                     f"the previous step's slab, {chunk_pages or count} pages per chunk",
         }
+        out.update(directions)
+        return out
     finally:
         torch.cuda.synchronize(device)
         lib.ckv_pipe_destroy(pipe)
@@ -1013,7 +1379,8 @@ def host_memory_available() -> int:
 
 
 def streamed_jobs(codec, name: str, steps: int, flush: torch.Tensor, device, rank: int = 0,
-                  chunk_pages: int = 256, pages_per_job: int = 2048) -> dict:
+                  chunk_pages: int = 256, pages_per_job: int = 2048, dist=None,
+                  world: int = 1) -> dict:
     """C4 / C5 through the pipeline: a step stores every job (2048 pages each) from its own KV
     pages into one of two page-locked slabs on the caller's stream while the previous job is
     restored on a second stream (background store, on-demand restore), so the link carries a
@@ -1073,16 +1440,65 @@ def streamed_jobs(codec, name: str, steps: int, flush: torch.Tensor, device, ran
             return moved
 
         step()
+        if dist is not None:
+            torch.cuda.synchronize(device)
+            dist.barrier()
         times, moved = timed_steps(step, steps, flush, device)
         torch.cuda.synchronize(device)
-        ok = True
-        for r in sorted({0, jobs - 1}):
+
+        def check(r) -> bool:
+            good = True
             b = torch.tensor(list(meta[r]["b"]), device=device).view(-1, 1)
             for p0 in range(0, pages_per_job, 256):
                 x = pages[r][p0:p0 + 256].float()
                 xh = dst[r][p0:p0 + 256].float()
-                ok &= bool(((x - xh).abs() <= b[p0:p0 + 256] * 1.01 + 1e-7 +
-                            x.abs() * 2.0 ** -8).all())
+                good &= bool(((x - xh).abs() <= b[p0:p0 + 256] * 1.01 + 1e-7 +
+                              x.abs() * 2.0 ** -8).all())
+            return good
+
+        ok = all(check(r) for r in sorted({0, jobs - 1}))
+
+        # each direction alone: every job stored (slab r % 2), then the last
+        # two stored jobs restored alternately, `jobs` restores in all
+        def store_only():
+            main = torch.cuda.current_stream(device)
+            for r in range(jobs):
+                t = C.c_uint64(0)
+                m = meta[r]
+                codec._check(lib.ckv_pipe_store_bf16(
+                    pipe, src_ptrs[r], eps, pages_per_job, n, slabs[r % 2].data_ptr(), raw_job,
+                    m["o"], m["s"], m["b"], C.byref(m["t"]), last_reader[r % 2], C.byref(t),
+                    main.cuda_stream), f"{name} store")
+                stored[r] = t.value
+            codec._check(lib.ckv_pipe_join(pipe, stored[jobs - 1], main.cuda_stream),
+                         f"{name} join")
+
+        def restore_only():
+            main = torch.cuda.current_stream(device)
+            for k in range(jobs):
+                r = jobs - 2 + k % 2 if jobs > 1 else 0
+                t = C.c_uint64(0)
+                m = meta[r]
+                codec._check(lib.ckv_pipe_restore_bf16(
+                    pipe, slabs[r % 2].data_ptr(), m["o"], m["s"], m["b"], pages_per_job, n,
+                    dst_ptrs[r], stored[r], C.byref(t), main.cuda_stream), f"{name} restore")
+                last_reader[r % 2] = t.value
+
+        def sync():
+            torch.cuda.synchronize(device)
+            if dist is not None:
+                dist.barrier()
+
+        store_only()
+        sync()
+        t_store, _ = timed_steps(store_only, 2, flush, device)
+        restore_only()
+        sync()
+        t_rest, _ = timed_steps(restore_only, 2, flush, device)
+        torch.cuda.synchronize(device)
+        ok &= check(jobs - 1)
+        sync()
+        t_d2h, t_h2d = raw_one_way(pages[0], 2, flush, device, dist)
         t = sum(times) / 1e3
         raw_step = jobs * raw_job
         return {
@@ -1091,6 +1507,8 @@ def streamed_jobs(codec, name: str, steps: int, flush: torch.Tensor, device, ran
             "e2e_gbps": round(job_rate(1, raw_step, steps, t), 3),
             "ms_per_step": round(t * 1e3 / steps, 3),
             "seconds": t, "raw_bytes_per_step": raw_step, "steps": steps,
+            "direction_seconds": [sum(t_store) / 1e3, sum(t_rest) / 1e3, t_d2h, t_h2d],
+            "raw_sample_bytes": raw_job,
             "compression_ratio": round(raw_step / max(1, moved[-1]), 4),
             "d2h_bytes_per_step": int(moved[-1]), "h2d_bytes_per_step": int(moved[-1]),
             "restore_ok": ok,
@@ -1119,6 +1537,43 @@ def raw_pcie(pages_dev: torch.Tensor, steps: int, flush: torch.Tensor, device) -
     torch.cuda.synchronize(device)
     times, _ = timed_steps(step, steps, flush, device)
     return sum(times) / 1e3
+
+
+def raw_one_way(src: torch.Tensor, steps: int, flush: torch.Tensor, device,
+                dist=None) -> tuple[float, float]:
+    """Raw pinned copies of `src`'s bytes, one direction at a time: seconds
+    for `steps` device-to-host copies, then for `steps` host-to-device
+    copies (every rank at once under torchrun; the slowest rank's times)."""
+    flat = src.reshape(-1).view(torch.uint8)
+    pinned = torch.empty(flat.numel(), dtype=torch.uint8, pin_memory=True)
+    back = torch.empty_like(flat)
+    d2h = lambda: pinned.copy_(flat, non_blocking=True)   # noqa: E731
+    h2d = lambda: back.copy_(pinned, non_blocking=True)   # noqa: E731
+    for fn in (d2h, h2d):
+        fn()
+    torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    t_d2h, _ = timed_steps(d2h, steps, flush, device)
+    torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    t_h2d, _ = timed_steps(h2d, steps, flush, device)
+    del pinned, back
+    return tuple(slowest_rank([sum(t_d2h) / 1e3, sum(t_h2d) / 1e3], dist, device))
+
+
+def direction_fields(world: int, raw_bytes: int, steps: int, t_store: float, t_restore: float,
+                     raw_sample: int, raw_steps: int, t_d2h: float, t_h2d: float) -> dict:
+    """Store alone and restore alone (uncompressed bytes / device time, all
+    ranks) next to raw one-way pinned copies of the same pages."""
+    store = world * raw_bytes * steps / t_store / 1e9
+    restore = world * raw_bytes * steps / t_restore / 1e9
+    d2h = world * raw_sample * raw_steps / t_d2h / 1e9
+    h2d = world * raw_sample * raw_steps / t_h2d / 1e9
+    return {"store_gbps": round(store, 3), "restore_gbps": round(restore, 3),
+            "raw_d2h_gbps": round(d2h, 3), "raw_h2d_gbps": round(h2d, 3),
+            "store_vs_raw_d2h": round(store / d2h, 4), "restore_vs_raw_h2d": round(restore / h2d, 4)}
 
 
 def slowest_rank(seconds: list[float], dist=None, device=None) -> list[float]:
@@ -1203,8 +1658,10 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c3", action="store_true",
                     help="skip the C3 mixed per-layer profile leg")
-    ap.add_argument("--streamed", default="",
-                    help="comma-separated extra legs: C4 (30 GB, 16 requests), C5 (5.4 GB shard)")
+    ap.add_argument("--streamed", default="default",
+                    help="comma-separated streamed legs: C4 (30 GB, 16 requests; one GPU), "
+                         "C5 (5.4 GB TP=8 shard per GPU); 'default' runs C4 at N = 1 and C5 "
+                         "at every N, 'none' neither")
     ap.add_argument("--chunk-pages", type=int, default=0,
                     help="pages per pipeline chunk (0: the whole job in one chunk)")
     args = ap.parse_args()
@@ -1288,10 +1745,24 @@ def main() -> int:
         barrier()
     launches_total = codec.launches() - launches0
     e2e_serial_ms = None
+    c2_dirs = {}
     if pipelined:
         # the same step through the plain calls: compress, pack, one D2H, one
         # H2D, decompress, one after the other (outside the clock sampling)
         e2e_serial_ms, _ = timed_steps(codec.step_e2e, args.steps, flush, device)
+        barrier()
+        # each direction alone, next to raw one-way copies of the same pages
+        for fn in (codec.step_store_only, codec.step_restore_only):
+            fn()
+        barrier()
+        st_ms, _ = timed_steps(codec.step_store_only, args.steps, flush, device)
+        barrier()
+        rs_ms, _ = timed_steps(codec.step_restore_only, args.steps, flush, device)
+        barrier()
+        t_d2h1, t_h2d1 = raw_one_way(pages_dev, min(args.steps, 10), flush, device, dist)
+        t_st1, t_rs1 = slowest_rank([sum(st_ms) / 1e3, sum(rs_ms) / 1e3], dist, device)
+        c2_dirs = direction_fields(world, raw_bytes, args.steps, t_st1, t_rs1, raw_bytes,
+                                   min(args.steps, 10), t_d2h1, t_h2d1)
         barrier()
     if impl == "ours":
         pack_ms.append(codec.kernel_ms(2))
@@ -1301,18 +1772,28 @@ def main() -> int:
              if impl == "ours" and pipelined and rank == 0 else None)
     c1 = (c1_leg(codec, min(args.steps, 10), flush, device)
           if impl == "ours" and pipelined and rank == 0 else None)
-    ref_kernels = (reference_kernels_leg(device, pages_dev, min(args.steps, 10), 3, flush)
+    ref_kernels = (reference_kernels_leg(device, pages_dev, min(args.steps, 10), 3, flush,
+                                         codec=codec)
                    if impl == "ours" and rank == 0 else None)
     c3 = None
     if impl == "ours" and pipelined and rank == 0 and not args.no_c3:
-        # a first pass warms the pipeline and its page-locked slabs: the first
-        # use of a freshly allocated 1 GiB slab pair ran the copies at half
-        # speed for its whole first pass, later passes at full speed
-        layer_groups_c3(codec, 3, flush, device, chunk_pages=args.chunk_pages, slabs=c3_slabs)
+        # its page-locked slabs were prefaulted when allocated (a freshly
+        # allocated 1 GiB slab pair used to run its first pass of copies at
+        # half speed)
         c3 = layer_groups_c3(codec, min(args.steps, 10), flush, device,
                              chunk_pages=args.chunk_pages, slabs=c3_slabs)
+    c1_pipe = (c1_pipeline(codec, min(args.steps, 10), flush, device)
+               if impl == "ours" and pipelined and rank == 0 else None)
+    plugin = (plugin_api_leg(codec, min(args.steps, 10), flush, device)
+              if impl == "ours" and pipelined and rank == 0 else None)
     streamed = {}
-    for name in [w.strip() for w in args.streamed.split(",") if w.strip()]:
+    if args.streamed == "default":
+        wanted = ["C4", "C5"] if world == 1 else ["C5"]
+    elif args.streamed == "none":
+        wanted = []
+    else:
+        wanted = [w.strip() for w in args.streamed.split(",") if w.strip()]
+    for name in wanted:
         if impl != "ours" or not pipelined:
             continue
         # every rank runs its own shard; all ranks take the same branch
@@ -1324,12 +1805,19 @@ def main() -> int:
             streamed[name] = {"workload": name, "skipped": "not enough host memory"}
             continue
         barrier()
-        leg = streamed_jobs(codec, name, 3, flush, device, rank=rank)
-        (t_leg,) = slowest_rank([leg.pop("seconds")], dist, device)
+        leg = streamed_jobs(codec, name, 3, flush, device, rank=rank, dist=dist, world=world)
+        t_st, t_rs, t_d2h, t_h2d = leg.pop("direction_seconds")
+        (t_leg, t_st, t_rs) = slowest_rank([leg.pop("seconds"), t_st, t_rs], dist, device)
         leg["e2e_gbps_rank0"] = leg.pop("e2e_gbps")
         leg["e2e_gbps"] = round(job_rate(world, leg["raw_bytes_per_step"], leg["steps"], t_leg), 3)
+        leg["overlapped_gbps"] = leg["e2e_gbps"]
+        leg.update(direction_fields(world, leg["raw_bytes_per_step"], 2, t_st, t_rs,
+                                    leg.pop("raw_sample_bytes"), 2, t_d2h, t_h2d))
         leg["n_gpus"] = world
+        leg["gpus_active"] = world
         streamed[name] = leg
+        gc.collect()
+        torch.cuda.empty_cache()
 
     e2e_match = codec.e2e_matches() if pipelined else None
     t_step, t_e2e, t_serial = slowest_rank(
@@ -1369,15 +1857,8 @@ def main() -> int:
         "vs_baseline": None,
         "dtype": "f32/u32",
         "data": "synthetic (seeded CPU generation, BASELINE.json configs[1] shapes)",
-        "config": {
-            "workload": "C2: Qwen2.5-1.5B KV at 4k context, 256 pages x 229376 BF16 "
-                        "([2,28,2,16,128]), REL eb 1e-5, one store + one restore per step",
-            "pages_per_gpu": args.pages, "elements_per_page": PAGE_NUMEL,
-            "error_bound": EPS, "relative": True,
-            "l2_flush": "256 MB write between timed steps",
-            "parallelism": "one process per GPU, pages sharded, no data-path collective",
-            "host_cpus_per_rank": affinity,
-        },
+        "config": config_block(args.pages),
+        "host_cpus_per_rank": affinity,
         "compression_ratio": round(raw_bytes / compressed, 4),
         "store_restore_ok": ok,
         "e2e": {"value": round(e2e, 3), "unit": "GB/s",
@@ -1395,7 +1876,8 @@ def main() -> int:
                 "pcie_raw_gbps": round(pcie, 3) if pcie else None,
                 "pcie_raw_duplex_gbps": round(pcie_duplex, 3) if pcie_duplex else None,
                 "fraction_of_raw_pcie": round(e2e / (pcie_duplex if pipelined else pcie), 4)
-                if pcie and pcie_duplex else None},
+                if pcie and pcie_duplex else None,
+                **c2_dirs},
     }
     if impl == "ours":
         enc = statistics.mean(enc_ms) / 1e3
@@ -1424,10 +1906,13 @@ def main() -> int:
         line["kernels"] = kernels
         line["pipeline_codecs"] = piped
         line["c1"] = c1
+        line["c1_pipeline"] = c1_pipe
+        line["plugin_api"] = plugin
         line["reference_kernels"] = ref_kernels
         line["layer_groups_c3"] = c3
         if streamed:
             line["streamed"] = streamed
+        line["per_config"] = per_config_summary(world, line, c2_dirs, e2e, c1_pipe, c3, streamed)
         line["gpu_launches"] = launches_total
         line["gpu_launches_value_region"] = launches_value
     else:

@@ -169,6 +169,25 @@ def test_page_store_overwrite_evict_and_recycle():
     assert store.slab(s3).buffer is buffers[0] and not store._free
 
 
+def test_page_store_reserve_fills_the_pool_first():
+    made = []
+
+    def allocate(n):
+        made.append(n)
+        return torch.empty(n, dtype=torch.uint8)
+
+    store = ko.CompressedPageStore(allocate=allocate)
+    store.reserve(4096, 2)
+    assert made == [4096, 4096] and len(store._free) == 2
+    reserved = {id(b) for b, _t in store._free}
+    a = store._take_slab(1000, 0, lambda t: None)
+    b = store._take_slab(4096, 0, lambda t: None)
+    assert {id(store.slab(a).buffer), id(store.slab(b).buffer)} == reserved
+    assert made == [4096, 4096] and not store._free     # no allocation for the first jobs
+    store._take_slab(64, 0, lambda t: None)
+    assert made == [4096, 4096, 64]
+
+
 # ---------------------------------------------------------------- GPU
 
 
