@@ -128,6 +128,35 @@ struct Batch {
     uint32_t max_n = 0;
 };
 
+// Grows every staging slot to at least `need` bytes (the next power of two,
+// 16 KB at least).  Freeing and allocating page-locked or device memory
+// synchronises the device, so all slots grow together: a context pays that a
+// few times in its life, not once per slot as a batch size first appears.
+ckv_status grow_slots(ckv_ctx* ctx, size_t need) {
+    size_t cap = 16384;
+    while (cap < need) cap <<= 1;
+    for (Slot& s : ctx->slots) {
+        if (s.cap >= cap) continue;
+        if (s.pending) {   // its upload may still be read
+            cudaError_t e = cudaEventSynchronize(s.done);
+            if (e != cudaSuccess) return cuda_fail(ctx, "waiting for a descriptor slot", e);
+            s.pending = false;
+        }
+        cudaFreeHost(s.host);
+        cudaFree(s.dev);
+        s.host = nullptr;
+        s.dev = nullptr;
+        s.cap = 0;
+        cudaError_t e = cudaHostAlloc(&s.host, cap, cudaHostAllocMapped);
+        if (e == cudaSuccess) e = cudaHostGetDevicePointer(&s.host_dev, s.host, 0);
+        if (e != cudaSuccess) return cuda_fail(ctx, "allocating pinned descriptors", e);
+        e = cudaMalloc(&s.dev, cap);
+        if (e != cudaSuccess) return cuda_fail(ctx, "allocating device descriptors", e);
+        s.cap = cap;
+    }
+    return CKV_OK;
+}
+
 // Next staging slot with at least `need` bytes, once its previous upload
 // and the kernel that read it have finished.
 ckv_status acquire_slot(ckv_ctx* ctx, size_t need, Slot** out) {
@@ -142,20 +171,8 @@ ckv_status acquire_slot(ckv_ctx* ctx, size_t need, Slot** out) {
         cudaError_t e = cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming);
         if (e != cudaSuccess) return cuda_fail(ctx, "creating an event", e);
     }
-    if (need > s.cap) {
-        size_t cap = std::max<size_t>(need, 16384);
-        cudaFreeHost(s.host);
-        cudaFree(s.dev);
-        s.host = nullptr;
-        s.dev = nullptr;
-        s.cap = 0;
-        cudaError_t e = cudaHostAlloc(&s.host, cap, cudaHostAllocMapped);
-        if (e == cudaSuccess) e = cudaHostGetDevicePointer(&s.host_dev, s.host, 0);
-        if (e != cudaSuccess) return cuda_fail(ctx, "allocating pinned descriptors", e);
-        e = cudaMalloc(&s.dev, cap);
-        if (e != cudaSuccess) return cuda_fail(ctx, "allocating device descriptors", e);
-        s.cap = cap;
-    }
+    if (need > s.cap)
+        if (ckv_status st = grow_slots(ctx, need)) return st;
     *out = &s;
     return CKV_OK;
 }
@@ -219,7 +236,8 @@ ckv_status ensure_results(ckv_ctx* ctx, size_t count) {
     ctx->bounds = nullptr;
     ctx->status = nullptr;
     ctx->results_cap = 0;
-    const size_t cap = std::max<size_t>(count, 256);
+    size_t cap = 256;
+    while (cap < count) cap <<= 1;
     cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&ctx->sizes), cap * sizeof(uint64_t), cudaHostAllocMapped);
     if (e == cudaSuccess) e = cudaHostAlloc(reinterpret_cast<void**>(&ctx->bounds), cap * sizeof(float), cudaHostAllocMapped);
     if (e == cudaSuccess) e = cudaHostAlloc(reinterpret_cast<void**>(&ctx->status), cap * sizeof(uint32_t), cudaHostAllocMapped);
@@ -240,7 +258,8 @@ ckv_status ensure_dec_status(ckv_ctx* ctx, size_t count) {
         cudaFree(ctx->dec_status);
         ctx->dec_status = nullptr;
     }
-    const size_t cap = std::max<size_t>(count, 1024);
+    size_t cap = 1024;
+    while (cap < count) cap <<= 1;
     cudaError_t e = cudaMalloc(&ctx->dec_status, cap * sizeof(uint32_t));
     if (e != cudaSuccess) return cuda_fail(ctx, "allocating decode status", e);
     e = cudaMemset(ctx->dec_status, 0, cap * sizeof(uint32_t));

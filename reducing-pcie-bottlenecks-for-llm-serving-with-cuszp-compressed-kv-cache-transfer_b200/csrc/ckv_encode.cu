@@ -26,8 +26,9 @@
 //                    transpose into sign word + bit planes in registers,
 //                    compact the chunk's payload in place over its own input
 //                    (a block of rate <= 15 packs into at most the 64 bytes it
-//                    came from; a warp barrier suffices) and copy it out with
-//                    coalesced stores.
+//                    came from; a warp barrier suffices), placed at the
+//                    destination's offset modulo 16, and copy it out with one
+//                    bulk copy (shared -> global) plus the ragged edge words.
 //
 // Rate <= 15 blocks without NaN (every block at REL bounds >= 1e-5 on
 // two-sided data) use a quantiser that truncates with a round-toward-zero
@@ -785,6 +786,7 @@ __device__ void pack(const Limits& lim, uint32_t count, const ShiftMul& mul, uin
         const bool ok = mbar_wait_bounded(&sy.ready[b], (j / kBufs) & 1u, lim.polls);
         if (!__all_sync(0xffffffffu, ok)) {
             sy.broken = 1;
+            if (lane == 0) bulk_wait<0>();
             return;
         }
         const SetInfo info = sy.info[b];
@@ -818,20 +820,49 @@ __device__ void pack(const Limits& lim, uint32_t count, const ShiftMul& mul, uin
                         if (32u - __clz(orv >> 1) != r) status |= kErrRateCheck;
                     }
                     // Every input of the chunk is in registers: its payload is
-                    // compacted over the chunk's own input, then copied out.
+                    // compacted over the chunk's own input, then copied out --
+                    // by one bulk copy where the payload, placed at the same
+                    // offset modulo 16 as its global destination, still fits
+                    // the chunk's bytes (the ragged first and last words by
+                    // lanes).
                     __syncwarp();
                     const uint32_t p0 = __shfl_sync(0xffffffffu, pos, 0);
+                    const uint32_t end =
+                        __reduce_max_sync(0xffffffffu, active && r ? pos + 4 + 4 * r : 0u);
+                    const uint32_t bytes = end > p0 ? end - p0 : 0u;
+                    uint8_t* gdst = info.out + p0;
+                    const uint32_t shift =
+                        static_cast<uint32_t>(reinterpret_cast<uintptr_t>(gdst) & 15u);
+                    const bool bulk = bytes >= 64 && shift + bytes <= 32 * BB;
+                    uint8_t* sbase = chunk + (bulk ? shift : 0u);
                     if (active && r) {
-                        uint32_t* out = reinterpret_cast<uint32_t*>(chunk + (pos - p0));
+                        uint32_t* out = reinterpret_cast<uint32_t*>(sbase + (pos - p0));
 #pragma unroll
                         for (int k = 0; k < 16; ++k)
                             if (k <= static_cast<int>(r)) out[k] = __funnelshift_l(A[k], A[k], sh);
                     }
-                    const uint32_t end = __reduce_max_sync(0xffffffffu, active && r ? pos + 4 + 4 * r : 0u);
-                    __syncwarp();
-                    copy_out(reinterpret_cast<const uint32_t*>(chunk),
-                             reinterpret_cast<uint32_t*>(info.out + p0),
-                             end > p0 ? (end - p0) >> 2 : 0u, lane);
+                    if (bulk) {
+                        const uint32_t head = (16u - shift) & 15u;
+                        const uint32_t body = (bytes - head) & ~15u;
+                        const uint32_t tail = bytes - head - body;
+                        fence_proxy_async_smem();   // the lanes' stores, to the bulk copy
+                        __syncwarp();
+                        const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sbase);
+                        uint32_t* g32 = reinterpret_cast<uint32_t*>(gdst);
+                        if (static_cast<uint32_t>(lane) < head / 4) g32[lane] = s32[lane];
+                        if (lane >= 4 && static_cast<uint32_t>(lane - 4) < tail / 4) {
+                            const uint32_t w = (head + body) / 4 + (lane - 4);
+                            g32[w] = s32[w];
+                        }
+                        if (lane == 0) {
+                            bulk_store(gdst + head, sbase + head, body);
+                            bulk_commit();
+                        }
+                    } else {
+                        __syncwarp();
+                        copy_out(reinterpret_cast<const uint32_t*>(chunk),
+                                 reinterpret_cast<uint32_t*>(info.out + p0), bytes >> 2, lane);
+                    }
                 } else if (active) {
                     const uint32_t valid = min(info.n - (info.b0 + i) * kBlock, uint32_t(kBlock));
                     uint32_t* out = reinterpret_cast<uint32_t*>(info.out + pos);
@@ -842,13 +873,16 @@ __device__ void pack(const Limits& lim, uint32_t count, const ShiftMul& mul, uin
         }
         rot = (rot + chunks) % kPWarps;
         status = __reduce_or_sync(0xffffffffu, status);
-        // Every lane's reads of this buffer are done before lane 0 releases it.
+        // Every lane's reads of this buffer, and the reads of the bulk
+        // copies lane 0 issued, are done before lane 0 releases it.
         __syncwarp();
         if (lane == 0) {
+            bulk_wait_read<0>();
             if (status) atomicOr(&sy.status[b], status);
             mbar_arrive(&sy.packed[b]);
         }
     }
+    if (lane == 0) bulk_wait<0>();
 }
 
 // ---- the kernel --------------------------------------------------------------

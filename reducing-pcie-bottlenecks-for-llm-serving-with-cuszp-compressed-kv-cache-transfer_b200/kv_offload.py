@@ -253,6 +253,41 @@ class _PageRecord:
     raw: tuple[bool, ...] = ()       # per segment: raw BF16 bytes instead of a cuSZp stream
 
 
+def _ptr_array(addrs: np.ndarray) -> C.Array:
+    return (C.c_void_p * len(addrs)).from_buffer_copy(np.asarray(addrs, dtype=np.uint64).tobytes())
+
+
+class _PageRefs:
+    """The destination pages of a restore: their addresses for the pipeline
+    (computed in one vector operation, no per-page tensor indexing), and a
+    1-D tensor view made only for the entries that need one (raw segments,
+    padded pages)."""
+
+    def __init__(self, ptrs: np.ndarray, tensor_of):
+        self.ptrs = np.asarray(ptrs, dtype=np.uint64)
+        self._tensor_of = tensor_of
+
+    @classmethod
+    def of_blocks(cls, kv: torch.Tensor, page_bytes: int, block_ids: np.ndarray) -> "_PageRefs":
+        ids = np.asarray(block_ids, dtype=np.int64)
+        ptrs = np.uint64(kv.data_ptr()) + ids.astype(np.uint64) * np.uint64(page_bytes)
+        return cls(ptrs, lambda i: kv[int(ids[i])].view(-1))
+
+    @classmethod
+    def of_tensors(cls, pages: Sequence[torch.Tensor]) -> "_PageRefs":
+        flat = [p.view(-1) for p in pages]
+        return cls(np.array([p.data_ptr() for p in flat], dtype=np.uint64), lambda i: flat[i])
+
+    def __len__(self) -> int:
+        return len(self.ptrs)
+
+    def tensor(self, i: int) -> torch.Tensor:
+        return self._tensor_of(int(i))
+
+    def ptr_array(self, sel=None) -> C.Array:
+        return _ptr_array(self.ptrs if sel is None else self.ptrs[sel])
+
+
 def prefault_pinned(buffers: Sequence[torch.Tensor], device, piece: int = 256 << 20) -> None:
     """Runs one DMA pass each way over page-locked host buffers (through a
     device scratch buffer of `piece` bytes), so that a job's first copies
@@ -537,19 +572,19 @@ class _Engine:
             ev.record(stream)
             self._held.append((ev, tensors))
 
-    def restore(self, payload: torch.Tensor, offsets, sizes, bounds, raw, dst, after: int,
-                stream) -> int:
+    def restore(self, payload: torch.Tensor, offsets, sizes, bounds, raw, dst: _PageRefs,
+                after: int, stream) -> int:
         """Restores a job's entries (page i, segment g at i * G + g) from
-        `payload` (the pinned bytes after the job header) into the 1-D page
-        tensors `dst`: cuSZp entries through the pipeline, raw entries by
-        copies, padded pages through a staging buffer.  Returns a ticket that
-        covers all of it."""
+        `payload` (the pinned bytes after the job header) into the pages
+        `dst`: cuSZp entries through the pipeline, raw entries by copies,
+        padded pages through a staging buffer.  Returns a ticket that covers
+        all of it."""
         G, count = self.segments, len(dst)
         sptr = stream.cuda_stream
         if self.codec != "cuszp":
             t = C.c_uint64(0)
             offs = (C.c_size_t * count)(*[int(o) for o in offsets])
-            ptrs = _ckv.ptr_array([d.data_ptr() for d in dst])
+            ptrs = dst.ptr_array()
             if self.codec == "int8":
                 self._check(self.lib.ckv_pipe_restore_int8(
                     self.pipe, payload.data_ptr(), offs, count, self.n, ptrs, after, C.byref(t),
@@ -587,14 +622,14 @@ class _Engine:
                         held.append(stage)
                         ptrs = _ckv.ptr_array([stage[k].data_ptr() for k in range(len(sel))])
                     else:
-                        ptrs = _ckv.ptr_array([dst[i].data_ptr() for i in sel])
+                        ptrs = dst.ptr_array(sel)
                     self._check(self.lib.ckv_pipe_restore_bf16(
                         self.pipe, base, o, z, b, len(sel), self.coded, ptrs, after,
                         C.byref(t), sptr), "restore")
                     if self.coded > self.n:
                         self.join(t.value, sptr)
                         for k, i in enumerate(sel):
-                            dst[i].copy_(stage[k, :self.n])
+                            dst.tensor(i).copy_(stage[k, :self.n])
                         extra = True
                 else:
                     k = len(sel) * len(cg)
@@ -603,9 +638,8 @@ class _Engine:
                     b = (C.c_float * k)(*bounds[sel][:, cg].reshape(-1).tolist())
                     self._check(self.lib.ckv_pipe_restore_bf16_groups(
                         self.pipe, base, o, z, b, len(sel), self.idx, self.sel, len(cg),
-                        self.prefix, self.layers, self.epl,
-                        _ckv.ptr_array([dst[i].data_ptr() for i in sel]), after, C.byref(t),
-                        sptr), "restore")
+                        self.prefix, self.layers, self.epl, dst.ptr_array(sel), after,
+                        C.byref(t), sptr), "restore")
                 tickets.append(t.value)
         else:
             # some compressed segments were stored raw: each group's cuSZp
@@ -619,7 +653,7 @@ class _Engine:
                 self._check(self.lib.ckv_pipe_restore_bf16_groups(
                     self.pipe, base, o, z, b, len(sel), (C.c_void_p * 1)(self.idx[j]),
                     (C.c_size_t * 1)(self.sel[j]), 1, self.prefix, self.layers, self.epl,
-                    _ckv.ptr_array([dst[i].data_ptr() for i in sel]), after, C.byref(t), sptr),
+                    dst.ptr_array(sel), after, C.byref(t), sptr),
                     "restore")
                 tickets.append(t.value)
         if raw.any():
@@ -630,11 +664,11 @@ class _Engine:
                     o, nbytes = int(offsets[i, g]), 2 * self.segment_numel(g)
                     src = payload[o:o + nbytes]
                     if self.groups is None:
-                        dst[i].view(torch.uint8).copy_(src, non_blocking=True)
+                        dst.tensor(i).view(torch.uint8).copy_(src, non_blocking=True)
                     else:
                         tmp = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
                         tmp.copy_(src, non_blocking=True)
-                        dst[i].view(self.prefix, self.layers, self.epl).index_copy_(
+                        dst.tensor(i).view(self.prefix, self.layers, self.epl).index_copy_(
                             1, self._index[g],
                             tmp.view(torch.bfloat16).view(self.prefix, len(self.groups[g][1]),
                                                           self.epl))
@@ -793,7 +827,7 @@ class CompressedOffloadingHandler:
             sizes = [z for i in idx for z in recs[i].sizes]
             bounds = [b for i in idx for b in recs[i].bounds]
             raw = [r for i in idx for r in (recs[i].raw or (False,) * e.segments)]
-            dst = [e.kv[int(gpu_ids[i])].view(-1) for i in idx]
+            dst = _PageRefs.of_blocks(e.kv, e.page_bytes, gpu_ids[idx])
             t = e.restore(slab.buffer[slab.payload_at:], offs, sizes, bounds, raw, dst,
                           slab.ticket, stream)
             slab.readers = t
@@ -909,5 +943,5 @@ def restore_job(slab: torch.Tensor, dst_pages: Sequence[torch.Tensor], engine: _
     if not same:
         raise ValueError("job segments do not match the engine's layer groups")
     return engine.restore(slab[job["payload_at"]:], job["offsets"], job["sizes"], job["bounds"],
-                          job["raw"], [p.view(-1) for p in dst_pages], 0,
+                          job["raw"], _PageRefs.of_tensors(dst_pages), 0,
                           torch.cuda.current_stream(engine.device))
