@@ -53,20 +53,36 @@ namespace cg = cooperative_groups;
 namespace ckv {
 namespace {
 
-constexpr uint32_t kSliceBytes = 64 * 1024;
 constexpr uint32_t kMaxCluster = 16;
 constexpr uint32_t kWaitPolls = 1u << 24;
 constexpr uint32_t kMaxPieces = 512;
 constexpr uint8_t kNanFlag = 0x80;
-constexpr uint32_t kBufs = 3;       // slices (and per-unit metadata sets) in flight per CTA
 constexpr uint32_t kXSlots = 2;     // cluster exchange slots (units j and j+1)
 constexpr int kPWarps = 11;         // pack warps
 constexpr int kAWarps = 4;          // analysis warps
 constexpr int kAThreads = kAWarps * 32;
 constexpr int kProducerWarp = kPWarps + kAWarps;
 constexpr int kEncThreads = (kProducerWarp + 1) * 32;
-constexpr uint32_t kMaxRun = 8;     // blocks per analysis thread in the offset scan
 constexpr uint32_t kWaitSpins = 1u << 26;   // polls of a non-suspending wait
+
+// Slice geometry of a launch: bytes of one CTA's slice of a unit, slices
+// (and per-unit metadata sets) in flight per CTA, and the blocks per
+// analysis thread in the offset scan.  Units of up to nine 64 KB slices use
+// three 64 KB buffers; larger units two 100 KB buffers, so that their
+// clusters stay at nine CTAs or fewer (B200 keeps 15 clusters of 7-9 CTAs
+// resident but only 7 of 11-16: 135 SMs against 112).
+struct Geo64 {
+    static constexpr uint32_t kSliceBytes = 64 * 1024;
+    static constexpr uint32_t kBufs = 3;
+    static constexpr uint32_t kMaxRun = 8;
+    static constexpr uint32_t kMetaStride = 4096;
+};
+struct Geo100 {
+    static constexpr uint32_t kSliceBytes = 100 * 1024;
+    static constexpr uint32_t kBufs = 2;
+    static constexpr uint32_t kMaxRun = 13;
+    static constexpr uint32_t kMetaStride = 6400;
+};
 
 template <typename T>
 struct Traits;
@@ -82,12 +98,15 @@ struct Traits<float> {
 };
 
 // Dynamic shared memory: kBufs slices, then kBufs x block extremes (later
-// payload offsets, 4 KB either type), then kBufs x rate bytes.
-template <typename T>
+// payload offsets, 4 bytes a block either type), then kBufs x rate bytes.
+template <typename T, typename G>
 struct Layout {
+    static constexpr uint32_t kBufs = G::kBufs;
+    static constexpr uint32_t kSliceBytes = G::kSliceBytes;
+    static constexpr uint32_t kMaxRun = G::kMaxRun;
     static constexpr uint32_t kBlocks = kSliceBytes / (kBlock * Traits<T>::kBytes);
     static constexpr uint32_t kMeta = kBufs * kSliceBytes;
-    static constexpr uint32_t kMetaStride = 4096;
+    static constexpr uint32_t kMetaStride = G::kMetaStride;
     static constexpr uint32_t kRates = kMeta + kBufs * kMetaStride;
     static constexpr uint32_t kRatesStride = (kBlocks + 15) / 16 * 16;
     static constexpr uint32_t kTotal = kRates + kBufs * kRatesStride;
@@ -158,7 +177,9 @@ struct Job {
 };
 
 // Barriers and exchange slots of one CTA.
+template <typename G>
 struct Sync {
+    static constexpr uint32_t kBufs = G::kBufs;
     uint64_t full[kBufs];      // producer -> analysis: slice landed
     uint64_t ready[kBufs];     // analysis -> pack: offsets, bound, output address
     uint64_t packed[kBufs];    // pack warps -> producer: buffer and metadata free
@@ -472,16 +493,16 @@ __device__ __forceinline__ float elem_at(const uint8_t* blk, int v) {
 // Loads slice j into buffer j % kBufs once unit j - kBufs has been packed out
 // of it, and publishes each unit's status word after its pack.  Returns once
 // the copies it issued have landed.
-template <typename T>
+template <typename T, typename G>
 __device__ void produce(const EncodeArgs& a, const Limits& lim, uint32_t count, uint32_t first,
-                        uint32_t stride, uint32_t rank, uint32_t csize, uint8_t* smem, Sync& sy) {
-    uint32_t last[kBufs];
-    for (uint32_t b = 0; b < kBufs; ++b) last[b] = ~0u;
-    for (uint32_t j = 0; j < count + kBufs; ++j) {
-        const uint32_t b = j % kBufs;
-        if (j >= kBufs) {
-            const uint32_t jj = j - kBufs;
-            if (!mbar_wait_bounded(&sy.packed[b], (jj / kBufs) & 1u, lim.polls)) {
+                        uint32_t stride, uint32_t rank, uint32_t csize, uint8_t* smem, Sync<G>& sy) {
+    uint32_t last[G::kBufs];
+    for (uint32_t b = 0; b < G::kBufs; ++b) last[b] = ~0u;
+    for (uint32_t j = 0; j < count + G::kBufs; ++j) {
+        const uint32_t b = j % G::kBufs;
+        if (j >= G::kBufs) {
+            const uint32_t jj = j - G::kBufs;
+            if (!mbar_wait_bounded(&sy.packed[b], (jj / G::kBufs) & 1u, lim.polls)) {
                 sy.broken = 1;
                 break;
             }
@@ -510,21 +531,21 @@ __device__ void produce(const EncodeArgs& a, const Limits& lim, uint32_t count, 
             job.u = u;
             job.s = s;
             // published by the arrive on full[b] inside issue_load
-            issue_load<T>(unit, map, u, s.e0, s.e1, smem + b * kSliceBytes, &sy.full[b],
+            issue_load<T>(unit, map, u, s.e0, s.e1, smem + b * G::kSliceBytes, &sy.full[b],
                           &sy.tail[b]);
             last[b] = j;
         }
     }
-    for (uint32_t b = 0; b < kBufs; ++b)
-        if (last[b] != ~0u) mbar_wait_bounded(&sy.full[b], (last[b] / kBufs) & 1u, kWaitPolls);
+    for (uint32_t b = 0; b < G::kBufs; ++b)
+        if (last[b] != ~0u) mbar_wait_bounded(&sy.full[b], (last[b] / G::kBufs) & 1u, kWaitPolls);
 }
 
 // ---- analysis warps -------------------------------------------------------------
 
-template <typename T>
+template <typename T, typename G>
 __device__ void analyse(const EncodeArgs& a, const Limits& lim, uint32_t count, uint32_t first,
-                        uint32_t stride, cg::cluster_group& cluster, uint8_t* smem, Sync& sy) {
-    using L = Layout<T>;
+                        uint32_t stride, cg::cluster_group& cluster, uint8_t* smem, Sync<G>& sy) {
+    using L = Layout<T, G>;
     constexpr uint32_t BB = kBlock * Traits<T>::kBytes;  // input bytes per block
     const uint32_t rank = cluster.block_rank();
     const uint32_t csize = cluster.num_blocks();
@@ -532,14 +553,14 @@ __device__ void analyse(const EncodeArgs& a, const Limits& lim, uint32_t count, 
     const int lane = t & 31, awarp = t >> 5;
     const int rho = (sizeof(T) == 2) ? ((t >> 1) & 3) : (t & 3);
     for (uint32_t j = 0; j < count; ++j) {
-        const uint32_t b = j % kBufs, x = j % kXSlots;
+        const uint32_t b = j % G::kBufs, x = j % kXSlots;
         const uint32_t xpar = (j / kXSlots) & 1u;
-        uint8_t* slice = smem + b * kSliceBytes;
+        uint8_t* slice = smem + b * G::kSliceBytes;
         uint8_t* meta = smem + L::kMeta + b * L::kMetaStride;
         uint8_t* rates = smem + L::kRates + b * L::kRatesStride;
 
         // -- slice on chip, block extremes, slice extremes to the cluster
-        const bool landed = mbar_wait_bounded(&sy.full[b], (j / kBufs) & 1u, lim.polls);
+        const bool landed = mbar_wait_bounded(&sy.full[b], (j / G::kBufs) & 1u, lim.polls);
         const Job job = sy.job[b];
         const Slice& s = job.s;
         const uint32_t u = job.u;
@@ -661,10 +682,10 @@ __device__ void analyse(const EncodeArgs& a, const Limits& lim, uint32_t count, 
         const uint32_t run = (s.nbs + kAThreads - 1) / kAThreads;
         const uint32_t i0 = t * run;
         // every load of the run first, then the arithmetic, then the stores
-        float lo[kMaxRun], hi[kMaxRun];
-        uint32_t flag[kMaxRun], sz[kMaxRun];
+        float lo[G::kMaxRun], hi[G::kMaxRun];
+        uint32_t flag[G::kMaxRun], sz[G::kMaxRun];
 #pragma unroll
-        for (uint32_t k = 0; k < kMaxRun; ++k) {
+        for (uint32_t k = 0; k < G::kMaxRun; ++k) {
             lo[k] = hi[k] = 0.0f;
             flag[k] = 0;
             const uint32_t ik = i0 + k;
@@ -683,7 +704,7 @@ __device__ void analyse(const EncodeArgs& a, const Limits& lim, uint32_t count, 
         }
         uint32_t local = 0;
 #pragma unroll
-        for (uint32_t k = 0; k < kMaxRun; ++k) {
+        for (uint32_t k = 0; k < G::kMaxRun; ++k) {
             uint32_t mq = 0;
             if (lo[k] == lo[k]) mq = max(uabs(quantize(lo[k], recip)), uabs(quantize(hi[k], recip)));
             if (flag[k]) mq = max(mq, 1u);
@@ -694,7 +715,7 @@ __device__ void analyse(const EncodeArgs& a, const Limits& lim, uint32_t count, 
             local += sz[k];
         }
 #pragma unroll
-        for (uint32_t k = 0; k < kMaxRun; ++k)
+        for (uint32_t k = 0; k < G::kMaxRun; ++k)
             if (k < run && i0 + k < s.nbs) rates[i0 + k] = static_cast<uint8_t>(flag[k]);
         uint32_t inc = local;
 #pragma unroll
@@ -715,7 +736,7 @@ __device__ void analyse(const EncodeArgs& a, const Limits& lim, uint32_t count, 
         // words now hold payload offsets.
         uint32_t off = pre + inc - local;
 #pragma unroll
-        for (uint32_t k = 0; k < kMaxRun; ++k) {
+        for (uint32_t k = 0; k < G::kMaxRun; ++k) {
             if (k < run && i0 + k < s.nbs) reinterpret_cast<uint32_t*>(meta)[i0 + k] = off;
             off += sz[k];
         }
@@ -772,25 +793,25 @@ __device__ __forceinline__ void copy_out(const uint32_t* src, uint32_t* dst, uin
     }
 }
 
-template <typename T>
+template <typename T, typename G>
 __device__ void pack(const Limits& lim, uint32_t count, const ShiftMul& mul, uint8_t* smem,
-                     Sync& sy) {
-    using L = Layout<T>;
+                     Sync<G>& sy) {
+    using L = Layout<T, G>;
     constexpr uint32_t BB = kBlock * Traits<T>::kBytes;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int rho = (sizeof(T) == 2) ? ((lane >> 1) & 3) : (lane & 3);
     const uint32_t sh = 8u * rho;
     uint32_t rot = 0;   // chunk c of this unit goes to pack warp (c + rot) % kPWarps
     for (uint32_t j = 0; j < count; ++j) {
-        const uint32_t b = j % kBufs;
-        const bool ok = mbar_wait_bounded(&sy.ready[b], (j / kBufs) & 1u, lim.polls);
+        const uint32_t b = j % G::kBufs;
+        const bool ok = mbar_wait_bounded(&sy.ready[b], (j / G::kBufs) & 1u, lim.polls);
         if (!__all_sync(0xffffffffu, ok)) {
             sy.broken = 1;
             if (lane == 0) bulk_wait<0>();
             return;
         }
         const SetInfo info = sy.info[b];
-        uint8_t* slice = smem + b * kSliceBytes;
+        uint8_t* slice = smem + b * G::kSliceBytes;
         const uint32_t* offs = reinterpret_cast<const uint32_t*>(smem + L::kMeta + b * L::kMetaStride);
         const uint8_t* rates = smem + L::kRates + b * L::kRatesStride;
         const uint32_t chunks = (info.nbs + 31) / 32;
@@ -887,10 +908,11 @@ __device__ void pack(const Limits& lim, uint32_t count, const ShiftMul& mul, uin
 
 // ---- the kernel --------------------------------------------------------------
 
-template <typename T>
+template <typename T, typename G>
 __global__ void __launch_bounds__(kEncThreads, 1) encode_kernel(EncodeArgs a) {
+    constexpr uint32_t kBufs = G::kBufs;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ Sync sy;
+    __shared__ Sync<G> sy;
 
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t rank = cluster.block_rank();
@@ -919,11 +941,11 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_kernel(EncodeArgs a) {
     cluster_barrier();   // every barrier of the cluster initialised before any arrive
 
     if (warp == kProducerWarp) {
-        if ((tid & 31) == 0) produce<T>(a, lim, count, first, stride, rank, csize, smem, sy);
+        if ((tid & 31) == 0) produce<T, G>(a, lim, count, first, stride, rank, csize, smem, sy);
     } else if (warp >= kPWarps) {
-        analyse<T>(a, lim, count, first, stride, cluster, smem, sy);
+        analyse<T, G>(a, lim, count, first, stride, cluster, smem, sy);
     } else {
-        pack<T>(lim, count, a.mul, smem, sy);
+        pack<T, G>(lim, count, a.mul, smem, sy);
     }
     // No peer touches this CTA's shared memory once every CTA is here.
     cluster_barrier();
@@ -940,7 +962,7 @@ struct ClusterShape {
     uint32_t clusters;
 };
 
-template <typename T>
+template <typename T, typename G>
 cudaError_t cluster_shape(uint32_t c_min, ClusterShape* out) {
     static std::mutex mu;
     static std::map<uint64_t, ClusterShape> cache;
@@ -954,9 +976,9 @@ cudaError_t cluster_shape(uint32_t c_min, ClusterShape* out) {
         *out = it->second;
         return cudaSuccess;
     }
-    auto kernel = encode_kernel<T>;
-    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               Layout<T>::kTotal);
+    using L = Layout<T, G>;
+    auto kernel = encode_kernel<T, G>;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (err != cudaSuccess) return err;
     err = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (err != cudaSuccess) return err;
@@ -965,7 +987,7 @@ cudaError_t cluster_shape(uint32_t c_min, ClusterShape* out) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(c, 1, 1);
         cfg.blockDim = dim3(kEncThreads, 1, 1);
-        cfg.dynamicSmemBytes = Layout<T>::kTotal;
+        cfg.dynamicSmemBytes = L::kTotal;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = c;
@@ -987,16 +1009,16 @@ cudaError_t cluster_shape(uint32_t c_min, ClusterShape* out) {
     return cudaSuccess;
 }
 
-template <typename T>
-cudaError_t launch_encode_t(const EncodeLaunch& l, cudaStream_t stream) {
-    using L = Layout<T>;
-    const uint32_t nb_max = (l.max_n + kBlock - 1) / kBlock;
-    uint32_t c_min = (nb_max + L::kBlocks - 1) / L::kBlocks;
-    if (c_min == 0) c_min = 1;
-    if (c_min > kMaxCluster || l.num_units == 0) return cudaErrorInvalidValue;
-    ClusterShape shape;
-    cudaError_t err = cluster_shape<T>(c_min, &shape);
-    if (err != cudaSuccess) return err;
+// Slices of a unit of nb blocks under geometry G (0 when it does not fit a
+// cluster).
+template <typename T, typename G>
+uint32_t slices_for(uint32_t nb) {
+    const uint32_t c = (nb + Layout<T, G>::kBlocks - 1) / Layout<T, G>::kBlocks;
+    return c == 0 ? 1u : (c <= kMaxCluster ? c : 0u);
+}
+
+template <typename T, typename G>
+cudaError_t launch_encode_g(const EncodeLaunch& l, const ClusterShape& shape, cudaStream_t stream) {
     EncodeArgs args{l.units, l.maps, l.num_units, l.relative ? 1u : 0u,
                     l.sizes, l.bounds, l.status, shift_mul(),
                     l.test_polls ? l.withhold_unit : ~0u, l.test_polls};
@@ -1004,7 +1026,7 @@ cudaError_t launch_encode_t(const EncodeLaunch& l, cudaStream_t stream) {
     const uint32_t clusters = min(min(l.num_units, shape.clusters), 65535u);
     cfg.gridDim = dim3(shape.c, clusters, 1);
     cfg.blockDim = dim3(kEncThreads, 1, 1);
-    cfg.dynamicSmemBytes = L::kTotal;
+    cfg.dynamicSmemBytes = Layout<T, G>::kTotal;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1014,14 +1036,39 @@ cudaError_t launch_encode_t(const EncodeLaunch& l, cudaStream_t stream) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     note_launch();
-    return cudaLaunchKernelEx(&cfg, encode_kernel<T>, args);
+    return cudaLaunchKernelEx(&cfg, encode_kernel<T, G>, args);
+}
+
+// Three 64 KB buffers per CTA where the unit fits, unless two 100 KB
+// buffers let its clusters cover more SMs (large units, whose 64 KB slices
+// need clusters of more than nine CTAs).
+template <typename T>
+cudaError_t launch_encode_t(const EncodeLaunch& l, cudaStream_t stream) {
+    if (l.num_units == 0) return cudaErrorInvalidValue;
+    const uint32_t nb_max = (l.max_n + kBlock - 1) / kBlock;
+    const uint32_t c64 = slices_for<T, Geo64>(nb_max);
+    const uint32_t c100 = slices_for<T, Geo100>(nb_max);
+    if (c100 == 0) return cudaErrorInvalidValue;
+    ClusterShape s64{0, 0}, s100{0, 0};
+    cudaError_t err = cudaSuccess;
+    if (c64) {
+        err = cluster_shape<T, Geo64>(c64, &s64);
+        if (err != cudaSuccess) return err;
+    }
+    if (!c64 || c64 > 9) {
+        err = cluster_shape<T, Geo100>(c100, &s100);
+        if (err != cudaSuccess) return err;
+    }
+    if (static_cast<uint64_t>(s100.c) * s100.clusters > static_cast<uint64_t>(s64.c) * s64.clusters)
+        return launch_encode_g<T, Geo100>(l, s100, stream);
+    return launch_encode_g<T, Geo64>(l, s64, stream);
 }
 
 }  // namespace
 
 uint32_t encode_max_elements(ElemType type) {
-    return type == ElemType::kBF16 ? kMaxCluster * Layout<__nv_bfloat16>::kBlocks * kBlock
-                                   : kMaxCluster * Layout<float>::kBlocks * kBlock;
+    return type == ElemType::kBF16 ? kMaxCluster * Layout<__nv_bfloat16, Geo100>::kBlocks * kBlock
+                                   : kMaxCluster * Layout<float, Geo100>::kBlocks * kBlock;
 }
 
 cudaError_t launch_encode(const EncodeLaunch& l, cudaStream_t stream) {

@@ -241,6 +241,9 @@ class _Slab:
     ticket: int = 0                  # store ticket that fills it
     readers: int = 0                 # last restore ticket reading it
     pages: set[int] = field(default_factory=set)
+    # the job's CPU block ids and its page table (offsets, sizes, bounds,
+    # raw flags: count x segments), for a load of the same blocks
+    job: tuple | None = None
 
 
 @dataclass
@@ -781,6 +784,11 @@ class CompressedOffloadingHandler:
                     bounds[j] = 0.0
             final = e.record(stream.cuda_stream)
         slab.ticket = final
+        slab.job = (np.asarray(cpu_ids, dtype=np.int64).copy(),
+                    np.ctypeslib.as_array(offsets).reshape(count, G).copy(),
+                    np.ctypeslib.as_array(sizes).reshape(count, G).copy(),
+                    np.ctypeslib.as_array(bounds).reshape(count, G).copy(),
+                    np.asarray(raw, dtype=bool).reshape(count, G))
         JobHeader.write(slab.buffer, e.n, self.error_bound, True, offsets, sizes, bounds,
                         total.value, e.groups, e.prefix, e.layers, raw=raw, coded=e.coded,
                         codec=e.codec)
@@ -811,16 +819,30 @@ class CompressedOffloadingHandler:
 
     def _load(self, cpu_ids: np.ndarray, gpu_ids: np.ndarray) -> tuple[list[int], int]:
         e = self.engine
+        if gpu_ids.size and (gpu_ids.min() < 0 or gpu_ids.max() >= e.kv.shape[0]):
+            raise IndexError("GPU block id out of range")
+        stream = torch.cuda.current_stream(e.device)
+        # A load of exactly the blocks one store job wrote, all still in its
+        # slab, uses that job's page table as stored (no per-page lookups).
+        if cpu_ids.size:
+            slab = self.store.slab(self.store.record(int(cpu_ids[0])).slab)
+            job = slab.job
+            if (job is not None and job[1].shape[1] == e.segments and
+                    len(job[0]) == len(cpu_ids) and len(slab.pages) == len(cpu_ids) and
+                    np.array_equal(job[0], cpu_ids)):
+                _ids, offs, sizes, bounds, raw = job
+                dst = _PageRefs.of_blocks(e.kv, e.page_bytes, gpu_ids)
+                t = e.restore(slab.buffer[slab.payload_at:], offs.reshape(-1), sizes.reshape(-1),
+                              bounds.reshape(-1), raw.reshape(-1), dst, slab.ticket, stream)
+                slab.readers = t
+                return [t], int(sizes.sum())
         recs = [self.store.record(int(c)) for c in cpu_ids]
         if any(len(r.sizes) != e.segments or r.n != e.n for r in recs):
             raise ValueError("stored page does not match the KV cache layout")
-        if gpu_ids.size and (gpu_ids.min() < 0 or gpu_ids.max() >= e.kv.shape[0]):
-            raise IndexError("GPU block id out of range")
         by_slab: dict[int, list[int]] = {}
         for i, r in enumerate(recs):
             by_slab.setdefault(r.slab, []).append(i)
         tickets, nbytes = [], 0
-        stream = torch.cuda.current_stream(e.device)
         for sid, idx in by_slab.items():
             slab = self.store.slab(sid)
             offs = [o for i in idx for o in recs[i].offsets]

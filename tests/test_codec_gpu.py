@@ -183,7 +183,9 @@ def _kv_pages(n, count, seed):
     (172032, 3, 1e-4),     # 21-layer group of the mixed profile
     (57344, 5, 1e-5),      # 7-layer group
     (8192, 33, 1e-4),      # one layer's K+V
-    (524288, 1, 1e-3),     # largest unit of the single-pass encoder
+    (524288, 1, 1e-3),     # largest unit of three 64 KB slices per CTA
+    (600001, 2, 1e-4),     # two 100 KB slices per CTA, ragged last block
+    (819200, 1, 1e-3),     # largest unit of the single-pass encoder
 ])
 def test_encode_decode_match_oracle(cpp, co, n, count, eb):
     host = _kv_pages(n, count, seed=n + count)
@@ -397,3 +399,16 @@ def test_error_behaviour(cpp):
     tiny = torch.randn(16, device="cuda").to(torch.bfloat16)
     assert w.compress_batch_fixed_bf16([tiny], [torch.empty(128, dtype=torch.uint8,
                                                             device="cuda")], [])[0] is False
+
+
+def test_units_above_the_encoder_limit_are_refused(cpp):
+    """Units above 16 slices of 100 KB (819200 BF16 elements) are refused
+    (False, no launch) rather than encoded wrongly."""
+    n = 819201
+    w = make_wrapper(cpp, 1e-4)
+    page = torch.zeros(n, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(int(w.estimate_compressed_buffer_size(n * 4)), dtype=torch.uint8,
+                      device="cuda")
+    before = cpp.kernel_launches()
+    ok, _sizes, _bounds = w.compress_batch_fixed_bf16([page], [out], [1e-4])
+    assert not ok and cpp.kernel_launches() == before
