@@ -362,9 +362,11 @@ CKV_API size_t ckv_pipe_host_capacity_raw(size_t count, size_t page_bytes);
  * lazily, at first use, and that allocates device memory; so call this once
  * per device with batch == 0 (every other argument is then ignored; the
  * device must be current) at start-up, before HBM is reserved and before
- * any stream capture.  That set-up call looks up the array's device address
- * and runs a built-in 32-element unit, held in the array itself, through
- * every launch a real call makes; later calls then allocate nothing.  All
+ * any stream capture.  That set-up call looks up the array's device address,
+ * loads both encoder kernels (one for units of up to nine 64 KB slices per
+ * CTA, one for larger units) and runs a built-in 32-element unit, held in
+ * the array itself, through every launch a real call makes; later calls
+ * then allocate nothing.  All
  * calls share the array: calls that overlap on the GPU race.  Otherwise as
  * ckv_compress_batch_fixed_bf16: `error_bound` and `relative` replace the
  * context's configuration, eps may be NULL, the call blocks until sizes and

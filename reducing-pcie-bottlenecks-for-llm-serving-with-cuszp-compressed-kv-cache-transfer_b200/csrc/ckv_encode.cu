@@ -1071,6 +1071,21 @@ uint32_t encode_max_elements(ElemType type) {
                                    : kMaxCluster * Layout<float, Geo100>::kBlocks * kBlock;
 }
 
+cudaError_t encode_prepare(ElemType type) {
+    // Both geometries' kernels loaded on the current device and their
+    // cluster shapes cached (setting a kernel attribute loads its code).
+    ClusterShape s;
+    cudaError_t e;
+    if (type == ElemType::kBF16) {
+        e = cluster_shape<__nv_bfloat16, Geo64>(1, &s);
+        if (e == cudaSuccess) e = cluster_shape<__nv_bfloat16, Geo100>(1, &s);
+    } else {
+        e = cluster_shape<float, Geo64>(1, &s);
+        if (e == cudaSuccess) e = cluster_shape<float, Geo100>(1, &s);
+    }
+    return e;
+}
+
 cudaError_t launch_encode(const EncodeLaunch& l, cudaStream_t stream) {
     if (l.type == ElemType::kBF16) return launch_encode_t<__nv_bfloat16>(l, stream);
     return launch_encode_t<float>(l, stream);

@@ -71,6 +71,10 @@ uint32_t decode_items(uint32_t n);
 // Largest unit (elements) the single-pass clustered encoder accepts.
 uint32_t encode_max_elements(ElemType type);
 
+// Loads every encoder kernel of an element type on the current device (no
+// launch); the first launch of a kernel would otherwise load it then.
+cudaError_t encode_prepare(ElemType type);
+
 // Enqueue on `stream`; returns cudaSuccess or the launch error.
 cudaError_t launch_encode(const EncodeLaunch& l, cudaStream_t stream);
 cudaError_t launch_decode(const DecodeLaunch& l, cudaStream_t stream);

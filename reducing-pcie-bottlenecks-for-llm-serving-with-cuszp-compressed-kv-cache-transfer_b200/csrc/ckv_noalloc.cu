@@ -20,8 +20,9 @@
 // that device at first use, which allocates device memory.  A launch may
 // also grow the device's local-memory reservation.  The set-up call (batch
 // 0) does all of that at a moment the caller chooses: it looks up the
-// array, then compresses the built-in unit (in and out of the array itself)
-// through every launch a real call makes.  Make it once per device at
+// array, loads both encoder kernels (one for units of up to nine 64 KB
+// slices per CTA, one for larger units), then compresses the built-in unit
+// (in and out of the array itself) through every launch a real call makes.  Make it once per device at
 // start-up, before the engine reserves its HBM and before any stream
 // capture; later calls then allocate nothing.  A real call made first does
 // the same set-up implicitly.
@@ -161,8 +162,11 @@ ckv_status run_noalloc(Scratch* s, const void* const* inputs, uint8_t* const* ou
     return CKV_OK;
 }
 
-// The set-up call: the built-in unit of 32 zeros through every launch.
+// The set-up call: every encoder kernel loaded (units above nine 64 KB
+// slices use a second one), then the built-in unit of 32 zeros through every
+// launch.
 ckv_status warm_up(Scratch* s, cudaStream_t stream) {
+    if (encode_prepare(ElemType::kBF16) != cudaSuccess) return CKV_ERR_CUDA;
     const uint16_t zeros[32] = {};
     if (cudaMemcpyAsync(s->warm_in, zeros, sizeof(zeros), cudaMemcpyHostToDevice, stream) !=
         cudaSuccess)
