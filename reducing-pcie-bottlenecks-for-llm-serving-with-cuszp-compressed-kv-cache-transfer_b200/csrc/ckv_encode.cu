@@ -331,7 +331,12 @@ __device__ __forceinline__ bool masked(int e, int rho, uint32_t valid) {
 // |q| = trunc(|t|) + s and the row is 2 * trunc(|t|) + 3 * s (< 2^16, so the
 // halves never carry into each other): one byte permute gathers both
 // truncations, one sign-replicating byte permute both signs, and one
-// multiply-add forms both rows.
+// multiply-add forms both rows.  The two rows' multiplies are one packed
+// mul.rn.f32x2 and their adds one packed fma.rn.f32x2(r, 1, 0.5), which is
+// r + 0.5 rounded once: ptxas keeps a packed multiply and that FMA apart,
+// whereas it contracts a packed multiply followed by add.rn.f32x2 into one
+// fused multiply-add despite the rounding modifiers (the fma_probe golden
+// case catches that).  Each lane rounds as its scalar form does.
 // prmt.b32 in its default mode, where a selector nibble of 8-15 replicates
 // the sign bit of byte (nibble & 7) over the result byte (the __byte_perm
 // intrinsic uses only the low 3 bits of each nibble).
@@ -341,10 +346,16 @@ __device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t b, uint32_t s
     return d;
 }
 
-__device__ __forceinline__ uint32_t narrow_pair(float x_lo, float x_hi, float recip,
+__device__ __forceinline__ uint32_t narrow_pair(float x_lo, float x_hi, uint64_t recip2,
                                                 const ShiftMul& mul) {
-    const float t_lo = __fadd_rn(__fmul_rn(x_lo, recip), 0.5f);
-    const float t_hi = __fadd_rn(__fmul_rn(x_hi, recip), 0.5f);
+    uint64_t x2, r2, t2;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(x2) : "f"(x_lo), "f"(x_hi));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r2) : "l"(x2), "l"(recip2));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(t2)
+        : "l"(r2), "l"(0x3F8000003F800000ull), "l"(0x3F0000003F000000ull));
+    float t_lo, t_hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(t_lo), "=f"(t_hi) : "l"(t2));
     const float z_lo = __fadd_rz(fabsf(t_lo), 8388608.0f);
     const float z_hi = __fadd_rz(fabsf(t_hi), 8388608.0f);
     const uint32_t trunc2 = __byte_perm(__float_as_uint(z_lo), __float_as_uint(z_hi), 0x5410);
@@ -363,10 +374,12 @@ __device__ __forceinline__ uint32_t narrow_block(const uint32_t (&w)[Traits<T>::
                                                  float recip, const ShiftMul& mul,
                                                  uint32_t (&A)[16]) {
     uint32_t orv = 0;
+    uint64_t recip2;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(recip2) : "f"(recip));
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
         const int e = bitpos(k);
-        A[k] = narrow_pair(elem<T>(w, e), elem<T>(w, e + 16), recip, mul);
+        A[k] = narrow_pair(elem<T>(w, e), elem<T>(w, e + 16), recip2, mul);
         orv |= A[k];
     }
     transpose16_mul(A, mul);
@@ -418,6 +431,10 @@ __device__ __forceinline__ uint32_t wide_block(const uint32_t (&w)[Traits<T>::kW
     return orv;
 }
 
+// Minimum and maximum of a block's values that are not NaN, and whether any
+// is NaN.  BF16: the maximum tree propagates NaN, so one tree gives both the
+// maximum and the NaN flag; a block with a NaN (rare) takes a second,
+// NaN-ignoring maximum tree.
 template <typename T>
 __device__ __forceinline__ void block_extremes(const uint32_t (&w)[Traits<T>::kWords], float& lo,
                                                float& hi, bool& nan);
@@ -425,13 +442,12 @@ __device__ __forceinline__ void block_extremes(const uint32_t (&w)[Traits<T>::kW
 template <>
 __device__ __forceinline__ void block_extremes<__nv_bfloat16>(const uint32_t (&w)[16], float& lo,
                                                               float& hi, bool& nan) {
-    __nv_bfloat162 mn[8], mx[8], mz[8];
+    __nv_bfloat162 mn[8], mz[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&w[2 * k]);
         const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[2 * k + 1]);
         mn[k] = __hmin2(a, b);
-        mx[k] = __hmax2(a, b);
         mz[k] = __hmax2_nan(a, b);
     }
 #pragma unroll
@@ -439,14 +455,26 @@ __device__ __forceinline__ void block_extremes<__nv_bfloat16>(const uint32_t (&w
 #pragma unroll
         for (int k = 0; k < s; ++k) {
             mn[k] = __hmin2(mn[k], mn[k + s]);
-            mx[k] = __hmax2(mx[k], mx[k + s]);
             mz[k] = __hmax2_nan(mz[k], mz[k + s]);
         }
     }
     lo = fminf(__low2float(mn[0]), __high2float(mn[0]));
-    hi = fmaxf(__low2float(mx[0]), __high2float(mx[0]));
     const float a = __low2float(mz[0]), b = __high2float(mz[0]);
     nan = (a != a) || (b != b);
+    hi = fmaxf(a, b);
+    if (nan) {   // the maximum over the values that are not NaN
+        __nv_bfloat162 mx[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            mx[k] = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&w[2 * k]),
+                            *reinterpret_cast<const __nv_bfloat162*>(&w[2 * k + 1]));
+#pragma unroll
+        for (int s = 4; s >= 1; s >>= 1) {
+#pragma unroll
+            for (int k = 0; k < s; ++k) mx[k] = __hmax2(mx[k], mx[k + s]);
+        }
+        hi = fmaxf(__low2float(mx[0]), __high2float(mx[0]));
+    }
 }
 
 __device__ __forceinline__ float nanmax(float a, float b) {
