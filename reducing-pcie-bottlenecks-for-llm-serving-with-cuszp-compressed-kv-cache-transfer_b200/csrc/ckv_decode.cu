@@ -157,8 +157,60 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&p);
 }
 
-__device__ __forceinline__ void store_elem(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
-__device__ __forceinline__ void store_elem(float* p, float v) { *p = v; }
+// A block already rounded to BF16: element 2p in the low half of w[p].
+struct Bf16Words {
+    uint32_t w[16];
+};
+
+// unpack_fast for BF16 output: the same values, rounded to BF16.  Two values
+// share one packed fused multiply-add (fma.rn.f32x2) and one rounding
+// instruction; their signs are applied to the rounded pair, since rounding
+// to nearest even is symmetric (bf16(-x) == -bf16(x)): one byte permute
+// brings both rows' sign bits (row bit 15) to bits 15 and 31.
+template <bool whole>
+__device__ __forceinline__ void unpack_fast_bf16(const uint32_t* words, uint32_t rate, float eb2,
+                                                 float negc, const ShiftMul& mul, Bf16Words& out) {
+    uint32_t A[16];
+#pragma unroll
+    for (int b = 0; b < 15; ++b) A[b] = whole || b < static_cast<int>(rate) ? words[1 + b] : 0u;
+    A[15] = words[0];
+    const uint32_t keep = whole ? (1u << rate) - 1u : 0x7fffu;
+    transpose16_mul(A, mul);
+    uint64_t e2, c2;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(e2) : "f"(eb2));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(c2) : "f"(negc));
+#pragma unroll
+    for (int p = 0; p < 16; ++p) {
+        const int k0 = bitpos(2 * p), k1 = bitpos(2 * p + 1);   // k1 = k0 - 1, same half
+        uint32_t m0, m1, sign;
+        if (k0 < 16) {
+            m0 = A[k0];
+            m1 = A[k1];
+            sign = __byte_perm(A[k0], A[k1], 0x5010);   // bytes 1 -> bytes 1 and 3
+        } else {
+            m0 = __umulhi(A[k0 - 16], mul.r16);
+            m1 = __umulhi(A[k1 - 16], mul.r16);
+            sign = __byte_perm(A[k0 - 16], A[k1 - 16], 0x7030);   // bytes 3 -> 1 and 3
+        }
+        uint64_t x2, y2;
+        asm("mov.b64 %0, {%1, %2};"
+            : "=l"(x2)
+            : "r"(0x4b000000u | (m0 & keep)), "r"(0x4b000000u | (m1 & keep)));
+        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(y2) : "l"(x2), "l"(e2), "l"(c2));
+        float y0, y1;
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(y0), "=f"(y1) : "l"(y2));
+        out.w[p] = pack_bf16x2(y0, y1) ^ (sign & 0x80008000u);
+    }
+}
+
+// Value v of a block at p: from floats (rounded here) or from BF16 words.
+__device__ __forceinline__ void store_elem(__nv_bfloat16* p, const float (&f)[32], int v) {
+    *p = __float2bfloat16_rn(f[v]);
+}
+__device__ __forceinline__ void store_elem(float* p, const float (&f)[32], int v) { *p = f[v]; }
+__device__ __forceinline__ void store_elem(__nv_bfloat16* p, const Bf16Words& b, int v) {
+    *reinterpret_cast<uint16_t*>(p) = static_cast<uint16_t>(b.w[v >> 1] >> (16 * (v & 1)));
+}
 
 template <typename T>
 __device__ __forceinline__ void store_block16(T* dst, const float (&f)[32]) {
@@ -178,10 +230,16 @@ __device__ __forceinline__ void store_block16(T* dst, const float (&f)[32]) {
     }
 }
 
+__device__ __forceinline__ void store_block16(__nv_bfloat16* dst, const Bf16Words& b) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) d[c] = make_uint4(b.w[4 * c], b.w[4 * c + 1], b.w[4 * c + 2], b.w[4 * c + 3]);
+}
+
 // Writes block jb of unit u (its first `valid` values) through its map.
-template <typename T>
+template <typename T, typename Values>
 __device__ __forceinline__ void write_block(const DecodeArgs& a, const SlotMeta& m, uint32_t jb,
-                                            uint32_t valid, const float (&f)[32]) {
+                                            uint32_t valid, const Values& f) {
     const uint32_t e0 = jb * kBlock;
     if (m.kind == kMapIdentity) {
         T* dst = static_cast<T*>(const_cast<void*>(m.elems)) + e0;
@@ -191,7 +249,7 @@ __device__ __forceinline__ void write_block(const DecodeArgs& a, const SlotMeta&
         }
 #pragma unroll
         for (int v = 0; v < 32; ++v)
-            if (static_cast<uint32_t>(v) < valid) store_elem(dst + v, f[v]);
+            if (static_cast<uint32_t>(v) < valid) store_elem(dst + v, f, v);
         return;
     }
     const Map map = a.maps[m.map];
@@ -210,7 +268,7 @@ __device__ __forceinline__ void write_block(const DecodeArgs& a, const SlotMeta&
         if (static_cast<uint32_t>(v) < valid) {
             const uint32_t i = e0 + v;
             const uint32_t r = i / L;
-            store_elem(run_base<T>(unit, map, m.u, r) + (i - r * L), f[v]);
+            store_elem(run_base<T>(unit, map, m.u, r) + (i - r * L), f, v);
         }
     }
 }
@@ -522,6 +580,7 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
             const uint32_t valid = min(m.n - jb * kBlock, uint32_t(kBlock));
             const float eb = m.eb;
             float f[32];
+            bool written = false;
             if (rate) {
                 const uint32_t* words =
                     (m.flags & kInSlot)
@@ -531,10 +590,19 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
                 // float, so one rounding of |q| * 2eb equals the reference's
                 // rounding of |q| * eb followed by an exact doubling.
                 const bool safe = eb >= 7.8886091e-31f && eb <= 1.2676506e30f;
-                if (rate <= 15 && safe) {
+                if (rate <= 15 && safe && sizeof(T) == 2) {
                     const float eb2 = __fmul_rn(eb, 2.0f);
+                    Bf16Words h;
                     // in a slot the words past the block stay inside the slot
                     // (payload cap + offsets + rates follow the payload)
+                    if (m.flags & kInSlot)
+                        unpack_fast_bf16<true>(words, rate, eb2, __fmul_rn(eb2, -8388608.0f), a.mul, h);
+                    else
+                        unpack_fast_bf16<false>(words, rate, eb2, __fmul_rn(eb2, -8388608.0f), a.mul, h);
+                    if constexpr (sizeof(T) == 2) write_block<T>(a, m, jb, valid, h);
+                    written = true;
+                } else if (rate <= 15 && safe) {
+                    const float eb2 = __fmul_rn(eb, 2.0f);
                     if (m.flags & kInSlot)
                         unpack_fast<true>(words, rate, eb2, __fmul_rn(eb2, -8388608.0f), a.mul, f);
                     else
@@ -547,7 +615,7 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
 #pragma unroll
                 for (int v = 0; v < 32; ++v) f[v] = z;
             }
-            write_block<T>(a, m, jb, valid, f);
+            if (!written) write_block<T>(a, m, jb, valid, f);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
