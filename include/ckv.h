@@ -202,6 +202,22 @@ CKV_API ckv_status ckv_unit_status(ckv_ctx* ctx, size_t count, uint32_t* out);
  * normally, nothing faults or hangs, and the context stays usable. */
 CKV_API ckv_status ckv_test_withhold_exchange(ckv_ctx* ctx, uint32_t unit, uint32_t wait_polls);
 
+/* Which BF16 encoder this context's compress calls use (no counterpart in
+ * the reference, whose wrapper has one kernel).  Both write the same bytes,
+ * sizes and bounds.  CKV_ENCODER_AUTO (the default) takes the streaming
+ * encoder for batches of whole pages (every unit a contiguous, 16-byte
+ * aligned page) of at most 16384 elements each, where it is faster, and the
+ * clustered encoder otherwise; CKV_ENCODER_CLUSTER always the clustered one;
+ * CKV_ENCODER_STREAM the streaming one whenever the batch is whole pages.
+ * The streaming encoder handles one unit per CTA and reads it twice (bound,
+ * then bit planes); the clustered one spreads a unit over a thread-block
+ * cluster and reads it once.  When a unit does not fit its buffer both fail
+ * with CKV_ERR_CAPACITY and write nothing past the buffer; the clustered
+ * encoder writes nothing of that unit, the streaming one may have written
+ * its leading chunks. */
+enum { CKV_ENCODER_AUTO = 0, CKV_ENCODER_CLUSTER = 1, CKV_ENCODER_STREAM = 2 };
+CKV_API ckv_status ckv_set_encoder(ckv_ctx* ctx, int choice);
+
 /* Gather `count` compressed units (device pointers srcs[i], sizes[i] bytes)
  * into the device slab `dst` (capacity bytes), unit i starting at
  * offsets[i] = previous end rounded up to `align` bytes (a power of two,

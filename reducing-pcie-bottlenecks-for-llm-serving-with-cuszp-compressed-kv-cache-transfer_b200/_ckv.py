@@ -48,7 +48,7 @@ EXPORTS = (
     "ckv_pipe_store_int8", "ckv_pipe_restore_int8", "ckv_pipe_store_raw", "ckv_pipe_restore_raw",
     "ckv_pipe_host_capacity_int8", "ckv_pipe_host_capacity_raw",
     "ckv_pipe_store_bf16_groups", "ckv_pipe_restore_bf16_groups", "ckv_pipe_host_capacity_groups",
-    "ckv_unit_status", "ckv_test_withhold_exchange",
+    "ckv_unit_status", "ckv_test_withhold_exchange", "ckv_set_encoder",
 )
 
 
@@ -129,6 +129,7 @@ def _declare(lib: C.CDLL) -> None:
         "ckv_pipe_host_capacity_groups": (c_size, [c_size, P, c_size, c_size, c_size]),
         "ckv_unit_status": (c_status, [P, c_size, C.POINTER(C.c_uint32)]),
         "ckv_test_withhold_exchange": (c_status, [P, C.c_uint32, C.c_uint32]),
+        "ckv_set_encoder": (c_status, [P, c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -83,6 +83,7 @@ struct ckv_ctx {
     // failure-path test hook for the next encode launch (0 polls: off)
     uint32_t test_withhold = 0;
     uint32_t test_polls = 0;
+    int encoder = CKV_ENCODER_AUTO;
     // units of the last compress call (their status words stay readable)
     size_t last_units = 0;
 };
@@ -335,6 +336,14 @@ ckv_status run_encode(ckv_ctx* ctx, Batch& b, ckv::ElemType type, size_t* sizes,
     l.bounds = ctx->bounds;
     l.status = ctx->status;
     l.type = type;
+    l.whole_pages = true;
+    for (const Unit& u : b.units)
+        if (u.n == 0 || b.maps[u.map].kind != ckv::kMapIdentity ||
+            (reinterpret_cast<uintptr_t>(u.elems) & 15u)) {
+            l.whole_pages = false;
+            break;
+        }
+    l.encoder = ctx->encoder;
     l.withhold_unit = ctx->test_withhold;
     l.test_polls = ctx->test_polls;
     ctx->test_polls = 0;
@@ -870,6 +879,13 @@ ckv_status ckv_test_withhold_exchange(ckv_ctx* ctx, uint32_t unit, uint32_t wait
     if (check_ctx(ctx) || wait_polls == 0) return CKV_ERR_ARGUMENT;
     ctx->test_withhold = unit;
     ctx->test_polls = wait_polls;
+    return CKV_OK;
+}
+
+ckv_status ckv_set_encoder(ckv_ctx* ctx, int choice) {
+    if (check_ctx(ctx) || choice < CKV_ENCODER_AUTO || choice > CKV_ENCODER_STREAM)
+        return CKV_ERR_ARGUMENT;
+    ctx->encoder = choice;
     return CKV_OK;
 }
 

@@ -114,15 +114,15 @@ __device__ __forceinline__ float bf16_hi(uint32_t w) {
 // Register bit-matrix transposes.  A[i] is row i, bit b its column b.
 
 // Exchanges the bits of b selected by mask with the bits of a selected by
-// mask << J, written as two bit-selects (shift + 3-input logic op each).
+// mask << J: t marks where the two differ, and flipping those bits in both
+// swaps them (t = ((a >> J) ^ b) & mask; b ^= t; a ^= t << J).  Counted on
+// sm_100a, this form issues fewer instructions per swap than two bit-selects.
 template <int J>
 __device__ __forceinline__ void delta_swap(uint32_t& a, uint32_t& b,
                                            uint32_t mask) {
-    const uint32_t hi = mask << J;
-    const uint32_t na = (a & ~hi) | ((b << J) & hi);
-    const uint32_t nb = (b & ~mask) | ((a >> J) & mask);
-    a = na;
-    b = nb;
+    const uint32_t t = ((a >> J) ^ b) & mask;
+    b ^= t;
+    a ^= t << J;
 }
 
 // The 8-bit step as two byte permutes.
@@ -167,31 +167,41 @@ inline ShiftMul shift_mul() {
 }
 
 // delta_swap with the two shifts done as multiplies (lmul = 2^J,
-// rmul = 2^(32-J)).
-template <int J>
+// rmul = 2^(32-J)).  kXor: the flip form above (t << J never carries out, as
+// t lies within mask), fewest instructions, for throughput-bound callers;
+// otherwise two independent bit-selects, the shorter dependency chain.
+template <int J, bool kXor>
 __device__ __forceinline__ void delta_swap_mul(uint32_t& a, uint32_t& b, uint32_t mask,
                                                uint32_t lmul, uint32_t rmul) {
-    const uint32_t hi = mask << J;
-    const uint32_t na = (a & ~hi) | ((b * lmul) & hi);
-    const uint32_t nb = (b & ~mask) | (__umulhi(a, rmul) & mask);
-    a = na;
-    b = nb;
+    if constexpr (kXor) {
+        const uint32_t t = (__umulhi(a, rmul) ^ b) & mask;
+        b ^= t;
+        a ^= t * lmul;
+    } else {
+        const uint32_t hi = mask << J;
+        const uint32_t na = (a & ~hi) | ((b * lmul) & hi);
+        const uint32_t nb = (b & ~mask) | (__umulhi(a, rmul) & mask);
+        a = na;
+        b = nb;
+    }
 }
 
 // transpose16 with its 4-, 2- and 1-bit steps split between the integer
-// ALU (bit selects) and the FMA pipe (shifts as multiplies).
+// ALU and the FMA pipe (shifts as multiplies).  The encoder, bound by
+// instruction issue, takes kXor; the decoder, by dependency latency, not.
+template <bool kXor>
 __device__ __forceinline__ void transpose16_mul(uint32_t (&A)[16], const ShiftMul& m) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) swap8(A[k], A[k + 8]);
 #pragma unroll
     for (int k = 0; k < 16; ++k)
-        if (!(k & 4)) delta_swap_mul<4>(A[k], A[k + 4], 0x0F0F0F0Fu, m.l4, m.r4);
+        if (!(k & 4)) delta_swap_mul<4, kXor>(A[k], A[k + 4], 0x0F0F0F0Fu, m.l4, m.r4);
 #pragma unroll
     for (int k = 0; k < 16; ++k)
-        if (!(k & 2)) delta_swap_mul<2>(A[k], A[k + 2], 0x33333333u, m.l2, m.r2);
+        if (!(k & 2)) delta_swap_mul<2, kXor>(A[k], A[k + 2], 0x33333333u, m.l2, m.r2);
 #pragma unroll
     for (int k = 0; k < 16; ++k)
-        if (!(k & 1)) delta_swap_mul<1>(A[k], A[k + 1], 0x55555555u, m.l1, m.r1);
+        if (!(k & 1)) delta_swap_mul<1, kXor>(A[k], A[k + 1], 0x55555555u, m.l1, m.r1);
 }
 
 // Full 32x32 transpose (rows of up to 32 bits).

@@ -44,6 +44,7 @@
 
 #include <cooperative_groups.h>
 
+#include <atomic>
 #include <cfloat>
 #include <map>
 #include <mutex>
@@ -64,6 +65,10 @@ constexpr int kAThreads = kAWarps * 32;
 constexpr int kProducerWarp = kPWarps + kAWarps;
 constexpr int kEncThreads = (kProducerWarp + 1) * 32;
 constexpr uint32_t kWaitSpins = 1u << 26;   // polls of a non-suspending wait
+// Whole BF16 pages of at most this many elements take the streaming encoder
+// by default: measured on B200, it is faster there (8192: 1.3-1.45x, 16384:
+// 1.05-1.15x) and slower from 32768 elements up (C2 pages: 0.86x).
+constexpr uint32_t kStreamMaxElems = 16384;
 
 // Slice geometry of a launch: bytes of one CTA's slice of a unit, slices
 // (and per-unit metadata sets) in flight per CTA, and the blocks per
@@ -382,7 +387,7 @@ __device__ __forceinline__ uint32_t narrow_block(const uint32_t (&w)[Traits<T>::
         A[k] = narrow_pair(elem<T>(w, e), elem<T>(w, e + 16), recip2, mul);
         orv |= A[k];
     }
-    transpose16_mul(A, mul);
+    transpose16_mul<true>(A, mul);
     return (orv | (orv >> 16)) & 0xffffu;
 }
 
@@ -860,8 +865,12 @@ __device__ void pack(const Limits& lim, uint32_t count, const ShiftMul& mul, uin
                 uint32_t w[Traits<T>::kWords];
                 if (active) load_block<T>(chunk + lane * BB, rho, w);
                 const bool narrow_ok = !(rb & kNanFlag) && r <= 15;
-                // +0 padding quantises to 0 only for a finite 0.5 / eb
-                const bool wide = __any_sync(0xffffffffu, active && !narrow_ok) || !(recip <= FLT_MAX);
+                // +0 padding quantises to 0 only for a finite 0.5 / eb; an
+                // infinite bound (0.5 / eb == 0) turns an infinite value into
+                // NaN * 0, |q| = 1, which the rate from the extremes does not
+                // flag as NaN
+                const bool wide = __any_sync(0xffffffffu, active && !narrow_ok) ||
+                                  !(recip <= FLT_MAX) || recip == 0.0f;
                 if (!wide) {
                     uint32_t A[16];
                     if (active) {
@@ -1092,6 +1101,444 @@ cudaError_t launch_encode_t(const EncodeLaunch& l, cudaStream_t stream) {
     return launch_encode_g<T, Geo64>(l, s64, stream);
 }
 
+// ---- streaming encoder: one CTA per unit ---------------------------------------
+//
+// For batches of whole BF16 pages (identity element map, 16-byte aligned
+// elements): a CTA takes whole units (u = blockIdx.x + k * gridDim.x) and
+// reads each one twice through a ring of 16 KB chunks that thread 0 keeps
+// filled with bulk copies.  The first pass (from HBM) reduces the unit's
+// extremes to its bound; the second (from L2, which the first pass filled)
+// quantises each block, takes its rate from its own values, scans the
+// chunk's block sizes, writes the rate bytes and copies the compacted payload
+// out with one bulk copy per chunk.  The unit's running payload offset lives
+// in one CTA: no cluster, no exchange.  Chunks of unit j's second pass
+// alternate with chunks of unit j+1's first pass, so the first pass's HBM
+// reads are in flight while the second pass computes; two CTAs per SM keep
+// one CTA's barriers under the other's arithmetic.
+//
+// Every block takes the narrow quantiser, which also reports whether all of
+// the block's |t| were below 2^15 (and none NaN): the truncating add then
+// gives 2^23 + trunc(|t|), whose bits 15..31 are those of 2^23.  A chunk with
+// any other block is redone with the exact instruction sequence for those
+// blocks and written straight to global memory.
+
+constexpr uint32_t kSBlocks = kThreads;                      // blocks per chunk
+constexpr uint32_t kSElems = kSBlocks * kBlock;              // 8192 elements
+constexpr uint32_t kSChunk = kSElems * 2;                    // 16 KB of BF16
+constexpr uint32_t kSSlots = 5;                              // chunks in flight (two CTAs per SM)
+constexpr uint32_t kSStage = kSBlocks * 64 + 16;             // compacted chunk + shift
+constexpr uint32_t kSSmem = kSSlots * kSChunk + 2 * kSStage;
+
+struct StreamArgs {
+    const Unit* units;
+    uint32_t num_units;
+    uint32_t relative;
+    uint64_t* sizes;
+    float* bounds;
+    uint32_t* status;
+    ShiftMul mul;
+};
+
+__device__ __forceinline__ uint32_t s_chunks(uint32_t n) { return (n + kSElems - 1) / kSElems; }
+
+// A CTA's chunk order: all of unit 0's first pass, then unit j's second pass
+// interleaved with unit j+1's first pass (second-pass chunk first), for
+// j = 0, 1, ...  `cur` is the unit in its second pass, `nxt` the unit in its
+// first (chunk counts 0 when absent).
+struct SSeq {
+    Unit cur, nxt;
+    uint32_t ucur, unxt;
+    uint32_t ccur, cnxt;
+    uint32_t bi, ai;   // next second-pass chunk of cur, first-pass chunk of nxt
+    uint32_t jn;       // position of nxt in the CTA's unit list
+};
+
+struct SElem {
+    uint32_t c;
+    bool second;    // second pass of cur (else first pass of nxt)
+    bool shifted;   // nxt became cur just before this chunk
+};
+
+__device__ __forceinline__ void seq_load_nxt(const StreamArgs& a, SSeq& s) {
+    s.unxt = blockIdx.x + s.jn * gridDim.x;
+    s.cnxt = 0;
+    if (s.unxt < a.num_units) {
+        s.nxt = a.units[s.unxt];
+        s.cnxt = s_chunks(s.nxt.n);
+    }
+}
+
+__device__ __forceinline__ void seq_init(const StreamArgs& a, SSeq& s) {
+    s.ccur = 0;
+    s.bi = 0;
+    s.ai = 0;
+    s.jn = 0;
+    s.ucur = ~0u;
+    seq_load_nxt(a, s);
+}
+
+__device__ __forceinline__ bool seq_next(const StreamArgs& a, SSeq& s, SElem& e) {
+    e.shifted = false;
+    if (s.bi >= s.ccur && s.ai >= s.cnxt) {
+        if (s.cnxt == 0) return false;
+        s.cur = s.nxt;
+        s.ucur = s.unxt;
+        s.ccur = s.cnxt;
+        s.bi = 0;
+        s.ai = 0;
+        ++s.jn;
+        seq_load_nxt(a, s);
+        e.shifted = true;
+    }
+    if (s.bi < s.ccur && (s.ai >= s.cnxt || s.bi <= s.ai)) {
+        e.second = true;
+        e.c = s.bi++;
+    } else {
+        e.second = false;
+        e.c = s.ai++;
+    }
+    return true;
+}
+
+// Bulk copy of chunk c of `unit` (its 16-byte aligned part) into `slot`.
+__device__ __forceinline__ void s_issue(const Unit& unit, uint32_t c, uint8_t* slot, uint64_t* bar) {
+    const uint32_t e0 = c * kSElems, e1 = min(unit.n, e0 + kSElems);
+    const uint32_t body = ((e1 - e0) * 2u) & ~15u;
+    mbar_arrive_expect_tx(bar, body);
+    if (body) bulk_load(slot, static_cast<const uint8_t*>(unit.elems) + e0 * 2u, body, bar);
+}
+
+// Thread 0: loads the next chunk of the producer's order into the slot it
+// belongs to (chunk k of the order goes to slot k % kSSlots).
+__device__ __forceinline__ void s_produce(const StreamArgs& a, SSeq& ps, uint32_t& issued,
+                                          uint8_t* smem, uint64_t* full) {
+    SElem e;
+    if (!seq_next(a, ps, e)) return;
+    const uint32_t s = issued % kSSlots;
+    s_issue(e.second ? ps.cur : ps.nxt, e.c, smem + s * kSChunk, &full[s]);
+    ++issued;
+}
+
+// The last chunk of a unit: the elements the bulk copy could not take (the
+// last n % 8) from global memory and, with `pad`, +0 up to the end of the
+// last block.  Every thread calls it; ends with a CTA barrier.
+__device__ __forceinline__ void s_fill_tail(const Unit& unit, uint32_t e0, uint8_t* slot, bool pad) {
+    const uint32_t n = unit.n;
+    const uint32_t have = e0 + ((((n - e0) * 2u) & ~15u) >> 1);
+    const uint32_t end = pad ? (n + kBlock - 1) / kBlock * kBlock : n;
+    const uint16_t* src = static_cast<const uint16_t*>(unit.elems);
+    uint16_t* dst = reinterpret_cast<uint16_t*>(slot);
+    for (uint32_t e = have + threadIdx.x; e < end; e += kThreads)
+        dst[e - e0] = e < n ? src[e] : uint16_t(0);
+    __syncthreads();
+}
+
+// narrow_pair that also ORs both truncating sums into `orz`.
+__device__ __forceinline__ uint32_t narrow_pair_z(float x_lo, float x_hi, uint64_t recip2,
+                                                  const ShiftMul& mul, uint32_t& orz) {
+    uint64_t x2, r2, t2;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(x2) : "f"(x_lo), "f"(x_hi));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r2) : "l"(x2), "l"(recip2));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(t2)
+        : "l"(r2), "l"(0x3F8000003F800000ull), "l"(0x3F0000003F000000ull));
+    float t_lo, t_hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(t_lo), "=f"(t_hi) : "l"(t2));
+    const uint32_t z_lo = __float_as_uint(__fadd_rz(fabsf(t_lo), 8388608.0f));
+    const uint32_t z_hi = __float_as_uint(__fadd_rz(fabsf(t_hi), 8388608.0f));
+    orz |= z_lo | z_hi;
+    const uint32_t trunc2 = __byte_perm(z_lo, z_hi, 0x5410);
+    const uint32_t neg2 = prmt_sign(__float_as_uint(t_lo), __float_as_uint(t_hi), 0xffbbu);
+    return trunc2 * mul.l1 + (neg2 & 0x00030003u);
+}
+
+// narrow_block (BF16) that also says whether the narrow quantiser was exact
+// for every element of the block.
+__device__ __forceinline__ uint32_t narrow_block_checked(const uint32_t (&w)[16], float recip,
+                                                         const ShiftMul& mul, uint32_t (&A)[16],
+                                                         bool& exact) {
+    uint32_t orv = 0, orz = 0;
+    uint64_t recip2;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(recip2) : "f"(recip));
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const int e = bitpos(k);
+        A[k] = narrow_pair_z(elem<__nv_bfloat16>(w, e), elem<__nv_bfloat16>(w, e + 16), recip2,
+                             mul, orz);
+        orv |= A[k];
+    }
+    transpose16_mul<true>(A, mul);
+    exact = (orz & 0xFFFF8000u) == 0x4B000000u;
+    return (orv | (orv >> 16)) & 0xffffu;
+}
+
+// Exclusive scan of v over the CTA (one barrier: `scratch` alternates between
+// two halves on consecutive calls), with the OR of two per-thread flags.
+__device__ __forceinline__ uint32_t s_scan(uint32_t v, uint32_t flags, uint32_t* scratch,
+                                           uint32_t& total, uint32_t& all_flags) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, d);
+        if (lane >= d) x += y;
+    }
+    const uint32_t wf = __reduce_or_sync(0xffffffffu, flags);
+    if (lane == 31) scratch[warp] = x | (wf << 24);   // a warp's total is below 2^24
+    __syncthreads();
+    uint32_t prefix = 0, sum = 0, f = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+        const uint32_t sv = scratch[w];
+        prefix += w < warp ? (sv & 0xFFFFFFu) : 0u;
+        sum += sv & 0xFFFFFFu;
+        f |= sv >> 24;
+    }
+    total = sum;
+    all_flags = f;
+    return prefix + x - v;
+}
+
+__global__ void __launch_bounds__(kThreads, 2) encode_stream_kernel(StreamArgs a) {
+    using T = __nv_bfloat16;
+    constexpr uint32_t BB = kBlock * 2;   // bytes per block
+    enum : uint32_t { kFlagWait = 1, kFlagWide = 2 };
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[kSSlots];
+    __shared__ uint32_t scan[2][kWarps];
+    __shared__ float red_lo[kWarps], red_hi[kWarps];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rho = (lane >> 1) & 3;
+    const uint32_t sh = 8u * rho;
+    uint8_t* const stage = smem + kSSlots * kSChunk;
+
+    SSeq ps;   // thread 0: the producer's position
+    uint32_t issued = 0;
+    if (tid == 0) {
+        for (uint32_t s = 0; s < kSSlots; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+        seq_init(a, ps);
+        for (uint32_t s = 0; s < kSSlots; ++s) s_produce(a, ps, issued, smem, full);
+    }
+    __syncthreads();
+
+    SSeq cs;   // every thread: the consumers' position
+    seq_init(a, cs);
+    uint32_t q = 0;          // chunks consumed
+    uint32_t nscan = 0;      // scans done (scratch half)
+    uint32_t stage_q = 0;    // staged chunks
+    bool broken = false;
+    // first pass of nxt
+    float tlo = FLT_MAX, thi = -FLT_MAX;
+    float neb = 0.0f, nrecip = 0.0f;
+    // second pass of cur
+    float eb = 0.0f, recip = 0.0f;
+    uint32_t run = 0, bits = 0;
+    bool fits = true;
+    SElem e;
+    while (seq_next(a, cs, e)) {
+        if (e.shifted) {
+            eb = neb;
+            recip = nrecip;
+            run = 0;
+            bits = 0;
+            fits = true;
+            tlo = FLT_MAX;
+            thi = -FLT_MAX;
+        }
+        const Unit& unit = e.second ? cs.cur : cs.nxt;
+        const uint32_t n = unit.n, nb = (n + kBlock - 1) / kBlock;
+        const uint32_t chunks = e.second ? cs.ccur : cs.cnxt;
+        const uint32_t s = q % kSSlots;
+        uint8_t* slot = smem + s * kSChunk;
+        const bool ok = mbar_wait_bounded(&full[s], (q / kSSlots) & 1u, kWaitPolls);
+        ++q;
+        const bool last = e.c + 1 == chunks;
+        if (last) s_fill_tail(unit, e.c * kSElems, slot, e.second);
+        const uint32_t b0 = e.c * kSBlocks;
+        const bool active = static_cast<uint32_t>(tid) < min(kSBlocks, nb - b0);
+        const uint32_t valid = active ? min(n - (b0 + tid) * kBlock, uint32_t(kBlock)) : 0u;
+
+        if (!e.second) {
+            // -- first pass: extremes
+            if (active) {
+                const uint8_t* blk = slot + tid * BB;
+                float lo, hi;
+                if (valid == kBlock) {
+                    uint32_t w[16];
+                    bool nan;
+                    load_block<T>(blk, rho, w);
+                    block_extremes<T>(w, lo, hi, nan);
+                } else {
+                    lo = __int_as_float(0x7fffffff);
+                    hi = lo;
+                    for (uint32_t v = 0; v < valid; ++v) {
+                        const float xv = elem_at<T>(blk, v);
+                        lo = fminf(lo, xv);
+                        hi = fmaxf(hi, xv);
+                    }
+                }
+                tlo = fminf(tlo, lo);
+                thi = fmaxf(thi, hi);
+            }
+            if (__syncthreads_or(!ok)) {   // also: every read of the slot is done
+                broken = true;
+                break;
+            }
+            if (tid == 0) s_produce(a, ps, issued, smem, full);
+            if (last) {   // the unit's bound
+#pragma unroll
+                for (int d = 16; d > 0; d >>= 1) {
+                    tlo = fminf(tlo, __shfl_xor_sync(0xffffffffu, tlo, d));
+                    thi = fmaxf(thi, __shfl_xor_sync(0xffffffffu, thi, d));
+                }
+                if (lane == 0) {
+                    red_lo[warp] = tlo;
+                    red_hi[warp] = thi;
+                }
+                __syncthreads();
+                float lo = FLT_MAX, hi = -FLT_MAX;
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) {
+                    lo = fminf(lo, red_lo[w]);
+                    hi = fmaxf(hi, red_hi[w]);
+                }
+                neb = resolve_bound(unit.eb, lo, hi, a.relative != 0);
+                nrecip = __fdiv_rn(0.5f, neb);
+                // red_* are read before they are next written: the next
+                // write follows this unit's whole second pass.
+            }
+            continue;
+        }
+
+        // -- second pass: rates, offsets, payload
+        uint32_t w[16], A[16];
+        uint32_t r = 0;
+        bool wide = false;
+        if (active) {
+            load_block<T>(slot + tid * BB, rho, w);
+            bool exact = false;
+            const uint32_t orv = narrow_block_checked(w, recip, a.mul, A, exact);
+            if (exact && recip <= FLT_MAX) {
+                r = 32u - __clz(orv >> 1);
+            } else {
+                wide = true;
+                uint32_t m = 0;
+                for (int k = 0; k < kBlock; ++k) m |= uabs(exact_q<T>(w, k, rho, recip, valid));
+                r = 32u - __clz(m);
+            }
+        }
+        const uint32_t size = r ? 4u + 4u * r : 0u;
+        // The staging buffer of this chunk is free once the bulk copy of two
+        // chunks ago has read it (ordered before the writes below by the
+        // scan's barrier).
+        if (tid == 0) bulk_wait_read<1>();
+        uint32_t total, flags;
+        const uint32_t off = s_scan(size, (ok ? 0u : kFlagWait) | (wide ? kFlagWide : 0u),
+                                    scan[nscan++ & 1u], total, flags);
+        if (flags & kFlagWait) {
+            broken = true;
+            break;
+        }
+        if (tid == 0) s_produce(a, ps, issued, smem, full);   // every read of the slot is done
+        if (fits && static_cast<uint64_t>(unit.capacity) < static_cast<uint64_t>(((n + kGroup - 1) / kGroup * (kGroup / kBlock))) + run + total) {
+            fits = false;
+            bits |= kErrCapacity;
+        }
+        if (fits) {
+            const uint32_t hdr = ((n + kGroup - 1) / kGroup * (kGroup / kBlock));
+            if (active) unit.stream[b0 + tid] = static_cast<uint8_t>(r);
+            uint8_t* gdst = unit.stream + hdr + run;
+            if (!(flags & kFlagWide)) {
+                uint8_t* sb = stage + (stage_q & 1u) * kSStage;
+                const uint32_t shift = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(gdst) & 15u);
+                if (r) {
+                    uint32_t* o = reinterpret_cast<uint32_t*>(sb + shift + off);
+#pragma unroll
+                    for (int k = 0; k < 16; ++k)
+                        if (k <= static_cast<int>(r)) o[k] = __funnelshift_l(A[k], A[k], sh);
+                }
+                fence_proxy_async_smem();   // the threads' stores, to the bulk copy
+                __syncthreads();
+                const uint32_t head = min((16u - shift) & 15u, total);
+                const uint32_t body = (total - head) & ~15u;
+                const uint32_t tail = total - head - body;
+                const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sb + shift);
+                uint32_t* g32 = reinterpret_cast<uint32_t*>(gdst);
+                if (static_cast<uint32_t>(tid) < head / 4) g32[tid] = s32[tid];
+                if (tid >= 32 && static_cast<uint32_t>(tid - 32) < tail / 4) {
+                    const uint32_t wd = (head + body) / 4 + (tid - 32);
+                    g32[wd] = s32[wd];
+                }
+                if (tid == 0 && body) {
+                    bulk_store(gdst + head, sb + shift + head, body);
+                    bulk_commit();
+                }
+                ++stage_q;
+            } else if (r) {
+                uint32_t* out = reinterpret_cast<uint32_t*>(gdst + off);
+                if (wide) {
+                    wide_block<T>(w, rho, recip, valid, r, out);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 16; ++k)
+                        if (k <= static_cast<int>(r)) out[k] = __funnelshift_l(A[k], A[k], sh);
+                }
+            }
+        }
+        run += total;
+        if (last) {
+            const uint32_t hdr = ((n + kGroup - 1) / kGroup * (kGroup / kBlock));
+            if (fits)
+                for (uint32_t k = nb + tid; k < hdr; k += kThreads) unit.stream[k] = 0;
+            if (tid == 0) {
+                a.sizes[cs.ucur] = static_cast<uint64_t>(hdr) + run;
+                a.bounds[cs.ucur] = eb;
+                if (bits) *reinterpret_cast<volatile uint32_t*>(&a.status[cs.ucur]) = bits;
+            }
+        }
+    }
+    if (tid == 0) {
+        if (broken) {
+            for (uint32_t u = blockIdx.x; u < a.num_units; u += gridDim.x)
+                *reinterpret_cast<volatile uint32_t*>(&a.status[u]) = kErrTimeout;
+            // the copies still in flight land before the CTA leaves
+            for (uint32_t k = q; k < issued; ++k)
+                mbar_wait_bounded(&full[k % kSSlots], (k / kSSlots) & 1u, kWaitPolls);
+        }
+        bulk_wait<0>();
+    }
+}
+
+cudaError_t launch_encode_stream(const EncodeLaunch& l, cudaStream_t stream) {
+    constexpr int kMaxDevices = 64;
+    static std::atomic<int> sms_cache[kMaxDevices];
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    // resident CTAs of the whole device
+    int slots = dev >= 0 && dev < kMaxDevices ? sms_cache[dev].load(std::memory_order_acquire) : 0;
+    if (slots <= 0) {
+        err = cudaFuncSetAttribute(encode_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kSSmem);
+        if (err != cudaSuccess) return err;
+        int sms = 0, per_sm = 0;
+        err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (err != cudaSuccess) return err;
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, encode_stream_kernel, kThreads,
+                                                            kSSmem);
+        if (err != cudaSuccess) return err;
+        slots = sms * (per_sm > 0 ? per_sm : 1);
+        if (dev >= 0 && dev < kMaxDevices) sms_cache[dev].store(slots, std::memory_order_release);
+    }
+    StreamArgs args{l.units, l.num_units, l.relative ? 1u : 0u, l.sizes, l.bounds, l.status,
+                    shift_mul()};
+    const uint32_t grid = min(l.num_units, static_cast<uint32_t>(slots));
+    note_launch();
+    encode_stream_kernel<<<grid, kThreads, kSSmem, stream>>>(args);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 uint32_t encode_max_elements(ElemType type) {
@@ -1115,6 +1562,9 @@ cudaError_t encode_prepare(ElemType type) {
 }
 
 cudaError_t launch_encode(const EncodeLaunch& l, cudaStream_t stream) {
+    const bool streamable = l.type == ElemType::kBF16 && l.whole_pages && !l.test_polls;
+    if (streamable && (l.encoder == 2 || (l.encoder == 0 && l.max_n <= kStreamMaxElems)))
+        return launch_encode_stream(l, stream);
     if (l.type == ElemType::kBF16) return launch_encode_t<__nv_bfloat16>(l, stream);
     return launch_encode_t<float>(l, stream);
 }

@@ -20,6 +20,11 @@ struct EncodeLaunch {
     float* bounds;             // device-visible, one per unit
     uint32_t* status;          // device-visible, one per unit
     ElemType type;
+    // Every unit a whole page: identity element map, elements 16-byte
+    // aligned, n > 0 (BF16 batches like this may use the streaming encoder).
+    bool whole_pages;
+    // 0 automatic, 1 clustered encoder, 2 streaming encoder (whole pages only)
+    int encoder;
     // Failure-path test hook (0: off): the cluster that owns unit
     // withhold_unit never completes that unit's bound exchange, and its
     // waits give up after test_polls polls (kErrTimeout on its units).
