@@ -518,6 +518,9 @@ class OurCodec:
         self.t_store = 0
         self.t_restore = 0
         self.side = torch.cuda.Stream(device)
+        self.cont_pages = None
+        self.cont_ptrs = None
+        self.slab_set = [0, 0]   # which copy of the pages each host slab holds
 
     def _check(self, status: int, what: str):
         if status != 0:
@@ -555,9 +558,22 @@ class OurCodec:
         self.restore(ins)
         return total
 
-    def step_e2e_pipelined(self):
+    def e2e_sets(self):
+        """The pages and two rotations of them (same pages, other addresses):
+        steps that cycle through the three read 352 MB of inputs, more than
+        L2 holds, so back-to-back steps need no flush between them."""
+        if self.cont_ptrs is None:
+            self.cont_pages = [self.pages] + [self.pages.roll(i, 0).contiguous() for i in (1, 2)]
+            self.cont_ptrs = [self.ckv.ptr_array([p[i].data_ptr() for i in range(self.count)])
+                              for p in self.cont_pages]
+        return self.cont_ptrs
+
+    def step_e2e_pipelined(self, pages_set=None, join=True):
         """Store this step's pages into one host slab while the previous
-        step's slab is restored: both directions of the link at once."""
+        step's slab is restored: both directions of the link at once.
+        join=False leaves the step's work in flight (the next step's calls
+        are ordered after it on the device by the pipeline's tickets)."""
+        in_ptrs = self.in_ptrs if pages_set is None else self.e2e_sets()[pages_set]
         k = self.e2e_k
         self.e2e_k += 1
         main = torch.cuda.current_stream(self.device)
@@ -577,27 +593,95 @@ class OurCodec:
             restored = b["total"].value
         t_store = C.c_uint64(0)
         self._check(self.lib.ckv_pipe_store_bf16(
-            self.pipe, self.in_ptrs, None, self.count, self.n, self.hslab[k % 2].data_ptr(),
+            self.pipe, in_ptrs, None, self.count, self.n, self.hslab[k % 2].data_ptr(),
             self.hslab[k % 2].numel(), a["offsets"], a["sizes"], a["bounds"],
             C.byref(a["total"]), prev_restore, C.byref(t_store), main.cuda_stream), "pipe store")
         self.t_store = t_store.value
+        self.slab_set[k % 2] = pages_set or 0
+        if join:
+            self.finish_e2e()
+        return a["total"].value, restored
+
+    def finish_e2e(self):
+        """The caller's stream waits for the last store and restore."""
+        main = torch.cuda.current_stream(self.device)
         self._check(self.lib.ckv_pipe_join(self.pipe, self.t_store, main.cuda_stream),
                     "pipe join")
         main.wait_stream(self.side)
-        return a["total"].value, restored
 
-    def step_store_only(self):
+    def e2e_continuous(self, steps: int, warmup: int = 3):
+        """`steps` pipelined steps back to back, as a serving engine offloads
+        and reloads continuously: no synchronisation between steps, inputs
+        cycling through the three copies of the pages.  Device time from
+        before the first call to the join after the last (seconds), and the
+        steps' (stored, restored) byte counts."""
+        main = torch.cuda.current_stream(self.device)
+        self.e2e_sets()
+        for i in range(warmup):
+            self.step_e2e_pipelined(pages_set=i % 3, join=False)
+        self.finish_e2e()
+        torch.cuda.synchronize(self.device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        collect = gc.isenabled()
+        gc.disable()
+        try:
+            start.record(main)
+            totals = [self.step_e2e_pipelined(pages_set=i % 3, join=False) for i in range(steps)]
+            self.finish_e2e()
+            end.record(main)
+            end.synchronize()
+        finally:
+            if collect:
+                gc.enable()
+        return start.elapsed_time(end) / 1e3, totals
+
+    def run_continuous(self, step, steps: int, warmup: int = 3) -> float:
+        """step(i) for `steps` steps back to back (no synchronisation between
+        them), joined at the end: device seconds."""
+        main = torch.cuda.current_stream(self.device)
+        for i in range(warmup):
+            step(i)
+        self.finish_e2e()
+        torch.cuda.synchronize(self.device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        collect = gc.isenabled()
+        gc.disable()
+        try:
+            start.record(main)
+            for i in range(steps):
+                step(i)
+            self.finish_e2e()
+            end.record(main)
+            end.synchronize()
+        finally:
+            if collect:
+                gc.enable()
+        return start.elapsed_time(end) / 1e3
+
+    def e2e_continuous_matches(self) -> bool:
+        """The last restore of e2e_continuous decoded the slab stored one step
+        before the last, which held copy j of the pages: bit for bit the
+        kernel path's restore of the same pages, rotated by j."""
+        torch.cuda.synchronize(self.device)
+        j = self.slab_set[(self.e2e_k - 2) % 2]
+        want = self.restored.roll(j, 0)
+        return bool(torch.equal(self.restored_e2e.view(torch.int16), want.view(torch.int16)))
+
+    def step_store_only(self, pages_set=None, join=True):
         """One direction alone: every page stored into host slab 0 (device to
         host), nothing else on the link."""
         main = torch.cuda.current_stream(self.device)
+        in_ptrs = self.in_ptrs if pages_set is None else self.e2e_sets()[pages_set]
         a = self.hmeta[0]
         t_store = C.c_uint64(0)
         self._check(self.lib.ckv_pipe_store_bf16(
-            self.pipe, self.in_ptrs, None, self.count, self.n, self.hslab[0].data_ptr(),
+            self.pipe, in_ptrs, None, self.count, self.n, self.hslab[0].data_ptr(),
             self.hslab[0].numel(), a["offsets"], a["sizes"], a["bounds"], C.byref(a["total"]),
             self.t_restore, C.byref(t_store), main.cuda_stream), "pipe store")
         self.t_store = t_store.value
-        self._check(self.lib.ckv_pipe_join(self.pipe, self.t_store, main.cuda_stream), "pipe join")
+        if join:
+            self._check(self.lib.ckv_pipe_join(self.pipe, self.t_store, main.cuda_stream),
+                        "pipe join")
         return a["total"].value
 
     def step_restore_only(self):
@@ -1743,6 +1827,13 @@ def main() -> int:
         e2e_ms, totals = timed_steps(
             codec.step_e2e_pipelined if pipelined else codec.step_e2e, args.steps, flush, device)
         barrier()
+        cont_s = None
+        e2e_match = None
+        if pipelined:
+            e2e_match = codec.e2e_matches()
+            cont_s, totals = codec.e2e_continuous(args.steps)
+            e2e_match = e2e_match and codec.e2e_continuous_matches()
+            barrier()
     launches_total = codec.launches() - launches0
     e2e_serial_ms = None
     c2_dirs = {}
@@ -1755,14 +1846,24 @@ def main() -> int:
         for fn in (codec.step_store_only, codec.step_restore_only):
             fn()
         barrier()
+        # each alone, steps back to back (inputs cycling through the three
+        # copies of the pages), and each step synchronised with an L2 flush
+        st_c = codec.run_continuous(
+            lambda i: codec.step_store_only(pages_set=i % 3, join=False), args.steps)
+        barrier()
+        rs_c = codec.run_continuous(lambda i: codec.step_restore_only(), args.steps)
+        barrier()
         st_ms, _ = timed_steps(codec.step_store_only, args.steps, flush, device)
         barrier()
         rs_ms, _ = timed_steps(codec.step_restore_only, args.steps, flush, device)
         barrier()
         t_d2h1, t_h2d1 = raw_one_way(pages_dev, min(args.steps, 10), flush, device, dist)
-        t_st1, t_rs1 = slowest_rank([sum(st_ms) / 1e3, sum(rs_ms) / 1e3], dist, device)
+        t_st1, t_rs1, t_st_iso, t_rs_iso = slowest_rank(
+            [st_c, rs_c, sum(st_ms) / 1e3, sum(rs_ms) / 1e3], dist, device)
         c2_dirs = direction_fields(world, raw_bytes, args.steps, t_st1, t_rs1, raw_bytes,
                                    min(args.steps, 10), t_d2h1, t_h2d1)
+        c2_dirs["store_gbps_isolated"] = round(world * raw_bytes * args.steps / t_st_iso / 1e9, 3)
+        c2_dirs["restore_gbps_isolated"] = round(world * raw_bytes * args.steps / t_rs_iso / 1e9, 3)
         barrier()
     if impl == "ours":
         pack_ms.append(codec.kernel_ms(2))
@@ -1819,12 +1920,13 @@ def main() -> int:
         gc.collect()
         torch.cuda.empty_cache()
 
-    e2e_match = codec.e2e_matches() if pipelined else None
-    t_step, t_e2e, t_serial = slowest_rank(
-        [sum(step_ms) / 1e3, sum(e2e_ms) / 1e3, sum(e2e_serial_ms) / 1e3 if e2e_serial_ms else 0.0],
-        dist, device)
+    t_step, t_e2e_iso, t_serial, t_cont = slowest_rank(
+        [sum(step_ms) / 1e3, sum(e2e_ms) / 1e3, sum(e2e_serial_ms) / 1e3 if e2e_serial_ms else 0.0,
+         cont_s or 0.0], dist, device)
+    t_e2e = t_cont if pipelined else t_e2e_iso
     value = job_rate(world, raw_bytes, args.steps, t_step)
     e2e = job_rate(world, raw_bytes, args.steps, t_e2e)
+    e2e_iso = job_rate(world, raw_bytes, args.steps, t_e2e_iso)
     e2e_serial = job_rate(world, raw_bytes, args.steps, t_serial) if t_serial else None
     # the link ceilings at the same GPU count: every rank copies at once (GPUs
     # may share a PCIe switch and the host's memory), slowest rank's time
@@ -1869,8 +1971,12 @@ def main() -> int:
                 "ms_per_step": round(t_e2e * 1e3 / args.steps, 4),
                 "path": ("ckv_pipe_store_bf16 of step k's pages into one pinned slab, "
                          "overlapped with ckv_pipe_restore_bf16 of step k-1's slab; "
-                         f"{codec.chunk} pages per chunk") if pipelined else
+                         f"{codec.chunk} pages per chunk; the steps back to back with no "
+                         "synchronisation between them, inputs cycling through three copies "
+                         "of the pages (352 MB, more than L2) instead of an L2 flush") if pipelined else
                         "compress, torch.cat pack, one D2H, one H2D, decompress (in order)",
+                "per_step_isolated_value": round(e2e_iso, 3) if pipelined else None,
+                "per_step_isolated_ms": round(t_e2e_iso * 1e3 / args.steps, 4) if pipelined else None,
                 "serial_value": round(e2e_serial, 3) if e2e_serial else None,
                 "restore_matches_kernel_path": e2e_match,
                 "pcie_raw_gbps": round(pcie, 3) if pcie else None,

@@ -937,6 +937,11 @@ struct ckv_pipe {
     cudaEvent_t ev_packed[2] = {nullptr, nullptr}, ev_copied[2] = {nullptr, nullptr};
     cudaEvent_t ev_landed[2] = {nullptr, nullptr}, ev_decoded[2] = {nullptr, nullptr};
     bool copied_used[2] = {false, false}, decoded_used[2] = {false, false};
+    // chunks staged / landed so far, over every call: consecutive chunks, also
+    // of consecutive jobs, alternate between the two buffers, so a job's
+    // compression overlaps the previous job's copy out (and a restore's copy
+    // in the previous one's decode)
+    uint64_t store_seq = 0, restore_seq = 0;
     cudaEvent_t ev_in = nullptr;
     static constexpr int kTickets = 64;
     cudaEvent_t tickets[kTickets] = {};
@@ -1104,8 +1109,8 @@ ckv_status pipe_store_units(ckv_pipe* p, size_t count, size_t per_page,
     if (e != cudaSuccess) return cuda_fail(ctx, "ordering the pipeline store", e);
     if (ckv_status st = pipe_after(p, after, p->s_d2h)) return st;
     size_t pos = 0;
-    for (size_t c0 = 0, c = 0; c0 < count; c0 += p->chunk, ++c) {
-        const int k = static_cast<int>(c & 1);
+    for (size_t c0 = 0; c0 < count; c0 += p->chunk) {
+        const int k = static_cast<int>(p->store_seq++ & 1u);
         const size_t cnt = std::min(p->chunk, count - c0);
         const size_t units = cnt * per_page, u0 = c0 * per_page;
         // the staging of chunk c - 2 has been copied out
@@ -1174,8 +1179,8 @@ ckv_status pipe_restore_units(ckv_pipe* p, const uint8_t* host, const size_t* of
     if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_dec, p->ev_in, 0);
     if (e != cudaSuccess) return cuda_fail(ctx, "ordering the pipeline restore", e);
     if (ckv_status st = pipe_after(p, after, p->s_h2d)) return st;
-    for (size_t c0 = 0, c = 0; c0 < count; c0 += p->chunk, ++c) {
-        const int k = static_cast<int>(c & 1);
+    for (size_t c0 = 0; c0 < count; c0 += p->chunk) {
+        const int k = static_cast<int>(p->restore_seq++ & 1u);
         const size_t cnt = std::min(p->chunk, count - c0);
         const size_t units = cnt * per_page, u0 = c0 * per_page;
         size_t lo = SIZE_MAX, hi = 0;
@@ -1402,8 +1407,8 @@ ckv_status pipe_store_fixed(ckv_pipe* p, size_t count, size_t stride, uint8_t* h
     if (e != cudaSuccess) return cuda_fail(ctx, "ordering the pipeline store", e);
     if (ckv_status st = pipe_after(p, after, p->s_d2h)) return st;
     size_t pos = 0;
-    for (size_t c0 = 0, c = 0; c0 < count; c0 += p->chunk, ++c) {
-        const int k = static_cast<int>(c & 1);
+    for (size_t c0 = 0; c0 < count; c0 += p->chunk) {
+        const int k = static_cast<int>(p->store_seq++ & 1u);
         const size_t cnt = std::min(p->chunk, count - c0);
         if (p->copied_used[k] && (e = cudaStreamWaitEvent(p->s_enc, p->ev_copied[k], 0)))
             return cuda_fail(ctx, "ordering the pipeline store", e);
@@ -1450,8 +1455,8 @@ ckv_status pipe_restore_fixed(ckv_pipe* p, const uint8_t* host, const size_t* of
     if (e == cudaSuccess) e = cudaStreamWaitEvent(p->s_dec, p->ev_in, 0);
     if (e != cudaSuccess) return cuda_fail(ctx, "ordering the pipeline restore", e);
     if (ckv_status st = pipe_after(p, after, p->s_h2d)) return st;
-    for (size_t c0 = 0, c = 0; c0 < count; c0 += p->chunk, ++c) {
-        const int k = static_cast<int>(c & 1);
+    for (size_t c0 = 0; c0 < count; c0 += p->chunk) {
+        const int k = static_cast<int>(p->restore_seq++ & 1u);
         const size_t cnt = std::min(p->chunk, count - c0);
         size_t lo = SIZE_MAX, hi = 0;
         for (size_t i = c0; i < c0 + cnt; ++i) {
