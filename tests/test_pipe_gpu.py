@@ -138,6 +138,58 @@ def test_pipe_overlapped_store_and_restore(env):
         lib.ckv_pipe_destroy(pipe)
 
 
+def test_pipe_back_to_back_single_chunk_jobs(env):
+    """Jobs of one chunk each, stored on one stream and restored on another
+    with no host synchronisation between them: consecutive jobs alternate
+    the pipeline's staging and landing buffers, so job k+1 compresses while
+    job k is still being copied out.  Every stored byte and every restored
+    page matches the plain calls."""
+    _ckv, lib, ctx = env
+    count, n, jobs = 24, 65536, 8
+    batches = [_pages(count, n, seed=300 + k).cuda() for k in range(4)]
+    refs = [_reference(_ckv, lib, ctx, b) for b in batches]
+    pipe = C.c_void_p()
+    assert lib.ckv_pipe_create(ctx, count, C.byref(pipe)) == 0
+    side = torch.cuda.Stream()
+    try:
+        cap = int(lib.ckv_pipe_host_capacity(count, n))
+        slabs = [torch.zeros(cap, dtype=torch.uint8, pin_memory=True) for _ in range(jobs)]
+        meta = [{"o": (C.c_size_t * count)(), "s": (C.c_size_t * count)(),
+                 "b": (C.c_float * count)(), "t": C.c_size_t(0)} for _ in range(jobs)]
+        outs = [torch.empty(count, n, dtype=torch.bfloat16, device="cuda") for _ in range(jobs)]
+        main = torch.cuda.current_stream().cuda_stream
+        stored = [0] * jobs
+        for k in range(jobs + 1):
+            if k < jobs:
+                m = meta[k]
+                b = batches[k % len(batches)]
+                ts = C.c_uint64(0)
+                assert lib.ckv_pipe_store_bf16(
+                    pipe, _ckv.ptr_array([b[i].data_ptr() for i in range(count)]), None, count, n,
+                    slabs[k].data_ptr(), cap, m["o"], m["s"], m["b"], C.byref(m["t"]), 0,
+                    C.byref(ts), main) == 0
+                stored[k] = ts.value
+            if k >= 1:   # restore job k-1 on the side stream, after its store
+                r = k - 1
+                m = meta[r]
+                tr = C.c_uint64(0)
+                assert lib.ckv_pipe_restore_bf16(
+                    pipe, slabs[r].data_ptr(), m["o"], m["s"], m["b"], count, n,
+                    _ckv.ptr_array([outs[r][i].data_ptr() for i in range(count)]), stored[r],
+                    C.byref(tr), side.cuda_stream) == 0
+        torch.cuda.synchronize()
+        for r in range(jobs):
+            ref_outs, ref_sizes, ref_bounds, ref_restored = refs[r % len(batches)]
+            assert list(meta[r]["s"]) == ref_sizes, f"job {r}"
+            assert torch.equal(outs[r].view(torch.int16), ref_restored.view(torch.int16)), f"job {r}"
+            host = ref_outs.cpu()
+            for i in range(count):
+                o, sz = meta[r]["o"][i], ref_sizes[i]
+                assert torch.equal(slabs[r][o:o + sz], host[i, :sz]), f"job {r} page {i}"
+    finally:
+        lib.ckv_pipe_destroy(pipe)
+
+
 def test_pipe_rejects_small_host_buffer(env):
     _ckv, lib, ctx = env
     count, n = 4, 32768
