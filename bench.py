@@ -350,6 +350,7 @@ def reference_arm(args, world: int) -> dict:
         "compression_ratio": round(raw / max(1, comp), 4),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
+        "host": host_info(),
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "reference_impl": ("the reference's codec is CUDA (integration/cuszp_wrapper/"
                            "cuszp_batched_fixed.cu); its C restatement, byte-identical on the "
@@ -1732,6 +1733,20 @@ def bind_host_threads(physical: int, local: int, local_world: int):
         return None
 
 
+def host_info() -> dict:
+    """The host's CPU count and model (/proc/cpuinfo), for the CPU baselines."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"nproc": os.cpu_count(), "cpu_model": model}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -1961,6 +1976,7 @@ def main() -> int:
         "data": "synthetic (seeded CPU generation, BASELINE.json configs[1] shapes)",
         "config": config_block(args.pages),
         "host_cpus_per_rank": affinity,
+        "host": host_info(),
         "compression_ratio": round(raw_bytes / compressed, 4),
         "store_restore_ok": ok,
         "e2e": {"value": round(e2e, 3), "unit": "GB/s",
