@@ -135,7 +135,7 @@ __device__ __forceinline__ void unpack_fast(const uint32_t* words, uint32_t rate
     for (int b = 0; b < 15; ++b) A[b] = whole || b < static_cast<int>(rate) ? words[1 + b] : 0u;
     A[15] = words[0];
     const uint32_t keep = whole ? (1u << rate) - 1u : 0x7fffu;
-    transpose16_mul<false>(A, mul);
+    transpose16_mul<false, true>(A, mul);
 #pragma unroll
     for (int v = 0; v < 32; ++v) {
         const int k = bitpos(v);
@@ -175,7 +175,7 @@ __device__ __forceinline__ void unpack_fast_bf16(const uint32_t* words, uint32_t
     for (int b = 0; b < 15; ++b) A[b] = whole || b < static_cast<int>(rate) ? words[1 + b] : 0u;
     A[15] = words[0];
     const uint32_t keep = whole ? (1u << rate) - 1u : 0x7fffu;
-    transpose16_mul<false>(A, mul);
+    transpose16_mul<false, true>(A, mul);
     uint64_t e2, c2;
     asm("mov.b64 %0, {%1, %1};" : "=l"(e2) : "f"(eb2));
     asm("mov.b64 %0, {%1, %1};" : "=l"(c2) : "f"(negc));

@@ -168,8 +168,8 @@ inline ShiftMul shift_mul() {
 
 // delta_swap with the two shifts done as multiplies (lmul = 2^J,
 // rmul = 2^(32-J)).  kXor: the flip form above (t << J never carries out, as
-// t lies within mask), fewest instructions, for throughput-bound callers;
-// otherwise two independent bit-selects, the shorter dependency chain.
+// t lies within mask), fewest instructions; otherwise two independent
+// bit-selects, the shorter dependency chain.
 template <int J, bool kXor>
 __device__ __forceinline__ void delta_swap_mul(uint32_t& a, uint32_t& b, uint32_t mask,
                                                uint32_t lmul, uint32_t rmul) {
@@ -187,21 +187,24 @@ __device__ __forceinline__ void delta_swap_mul(uint32_t& a, uint32_t& b, uint32_
 }
 
 // transpose16 with its 4-, 2- and 1-bit steps split between the integer
-// ALU and the FMA pipe (shifts as multiplies).  The encoder, bound by
-// instruction issue, takes kXor; the decoder, by dependency latency, not.
-template <bool kXor>
+// ALU and the FMA pipe (shifts as multiplies).  kXor4 / kXor21: the flip
+// form for the 4-bit step / the 2- and 1-bit steps.  Measured on B200: the
+// encoder, bound by instruction issue, is fastest with the flip form
+// throughout; the decoder with bit-selects in the 4-bit step and flips in
+// the other two (flips throughout cost it 2-3 %).
+template <bool kXor4, bool kXor21>
 __device__ __forceinline__ void transpose16_mul(uint32_t (&A)[16], const ShiftMul& m) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) swap8(A[k], A[k + 8]);
 #pragma unroll
     for (int k = 0; k < 16; ++k)
-        if (!(k & 4)) delta_swap_mul<4, kXor>(A[k], A[k + 4], 0x0F0F0F0Fu, m.l4, m.r4);
+        if (!(k & 4)) delta_swap_mul<4, kXor4>(A[k], A[k + 4], 0x0F0F0F0Fu, m.l4, m.r4);
 #pragma unroll
     for (int k = 0; k < 16; ++k)
-        if (!(k & 2)) delta_swap_mul<2, kXor>(A[k], A[k + 2], 0x33333333u, m.l2, m.r2);
+        if (!(k & 2)) delta_swap_mul<2, kXor21>(A[k], A[k + 2], 0x33333333u, m.l2, m.r2);
 #pragma unroll
     for (int k = 0; k < 16; ++k)
-        if (!(k & 1)) delta_swap_mul<1, kXor>(A[k], A[k + 1], 0x55555555u, m.l1, m.r1);
+        if (!(k & 1)) delta_swap_mul<1, kXor21>(A[k], A[k + 1], 0x55555555u, m.l1, m.r1);
 }
 
 // Full 32x32 transpose (rows of up to 32 bits).

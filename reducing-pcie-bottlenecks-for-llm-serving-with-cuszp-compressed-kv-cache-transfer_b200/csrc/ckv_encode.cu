@@ -387,7 +387,7 @@ __device__ __forceinline__ uint32_t narrow_block(const uint32_t (&w)[Traits<T>::
         A[k] = narrow_pair(elem<T>(w, e), elem<T>(w, e + 16), recip2, mul);
         orv |= A[k];
     }
-    transpose16_mul<true>(A, mul);
+    transpose16_mul<true, true>(A, mul);
     return (orv | (orv >> 16)) & 0xffffu;
 }
 
@@ -1267,7 +1267,7 @@ __device__ __forceinline__ uint32_t narrow_block_checked(const uint32_t (&w)[16]
                              mul, orz);
         orv |= A[k];
     }
-    transpose16_mul<true>(A, mul);
+    transpose16_mul<true, true>(A, mul);
     exact = (orz & 0xFFFF8000u) == 0x4B000000u;
     return (orv | (orv >> 16)) & 0xffffu;
 }
