@@ -976,6 +976,10 @@ __global__ void __launch_bounds__(kEncThreads, 1) encode_kernel(EncodeArgs a) {
         fence_mbar_init();
     }
     cluster_barrier();   // every barrier of the cluster initialised before any arrive
+    // A streaming-encoder launch of the batch's remainder units, queued after
+    // this one as a programmatic dependent, may start on the SMs no cluster
+    // holds once every CTA here is resident (it reads nothing written here).
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == kProducerWarp) {
         if ((tid & 31) == 0) produce<T, G>(a, lim, count, first, stride, rank, csize, smem, sy);
@@ -1076,6 +1080,42 @@ cudaError_t launch_encode_g(const EncodeLaunch& l, const ClusterShape& shape, cu
     return cudaLaunchKernelEx(&cfg, encode_kernel<T, G>, args);
 }
 
+cudaError_t launch_encode_stream(const EncodeLaunch& l, cudaStream_t stream, bool tail);
+cudaError_t stream_free_slots(uint32_t busy_sms, uint32_t* slots);
+
+// The clustered launch, and where it pays, its last round's units handed to
+// the streaming encoder on the SMs no cluster holds.  `rounds` of the
+// clustered encoder are ceil(units / clusters); when units % clusters of
+// them would run a round alone, they run instead beside the others as one
+// streaming CTA each, provided the clustered rounds that remain (at least
+// 1.8 x the cluster size of them) outlast one unit in one CTA (measured on
+// B200 for C2 pages: 17 rounds 83 us, one unit in one streaming CTA 66 us).
+template <typename T, typename G>
+cudaError_t launch_encode_split(const EncodeLaunch& l, const ClusterShape& shape,
+                                cudaStream_t stream) {
+    const uint32_t clusters = shape.clusters;
+    const uint32_t r = clusters ? l.num_units % clusters : 0u;
+    const uint32_t rounds = clusters ? l.num_units / clusters : 0u;
+    uint32_t free_slots = 0;
+    const bool split = sizeof(T) == 2 && l.whole_pages && !l.test_polls && l.encoder == 0 &&
+                       r > 0 && rounds * 5 >= 9 * shape.c &&
+                       stream_free_slots(shape.c * clusters, &free_slots) == cudaSuccess &&
+                       r <= free_slots;
+    if (!split) return launch_encode_g<T, G>(l, shape, stream);
+    EncodeLaunch head = l;
+    head.num_units = l.num_units - r;
+    cudaError_t err = launch_encode_g<T, G>(head, shape, stream);
+    if (err != cudaSuccess) return err;
+    EncodeLaunch tail = l;
+    const uint32_t u0 = head.num_units;
+    tail.units = l.units + u0;
+    tail.sizes = l.sizes + u0;
+    tail.bounds = l.bounds + u0;
+    tail.status = l.status + u0;
+    tail.num_units = r;
+    return launch_encode_stream(tail, stream, true);
+}
+
 // Three 64 KB buffers per CTA where the unit fits, unless two 100 KB
 // buffers let its clusters cover more SMs (large units, whose 64 KB slices
 // need clusters of more than nine CTAs).
@@ -1097,8 +1137,8 @@ cudaError_t launch_encode_t(const EncodeLaunch& l, cudaStream_t stream) {
         if (err != cudaSuccess) return err;
     }
     if (static_cast<uint64_t>(s100.c) * s100.clusters > static_cast<uint64_t>(s64.c) * s64.clusters)
-        return launch_encode_g<T, Geo100>(l, s100, stream);
-    return launch_encode_g<T, Geo64>(l, s64, stream);
+        return launch_encode_split<T, Geo100>(l, s100, stream);
+    return launch_encode_split<T, Geo64>(l, s64, stream);
 }
 
 // ---- streaming encoder: one CTA per unit ---------------------------------------
@@ -1137,6 +1177,10 @@ struct StreamArgs {
     float* bounds;
     uint32_t* status;
     ShiftMul mul;
+    // launched as the programmatic dependent of a clustered launch (the
+    // batch's remainder units): every CTA waits for that grid to complete
+    // before it exits, so that work queued after this launch follows both
+    uint32_t tail;
 };
 
 __device__ __forceinline__ uint32_t s_chunks(uint32_t n) { return (n + kSElems - 1) / kSElems; }
@@ -1508,35 +1552,64 @@ __global__ void __launch_bounds__(kThreads, 2) encode_stream_kernel(StreamArgs a
         }
         bulk_wait<0>();
     }
+    if (a.tail && tid == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
-cudaError_t launch_encode_stream(const EncodeLaunch& l, cudaStream_t stream) {
+// Device-wide figures of the streaming kernel, once per device: resident
+// CTAs per SM and SMs.
+cudaError_t stream_shape(int* per_sm, int* sms) {
     constexpr int kMaxDevices = 64;
-    static std::atomic<int> sms_cache[kMaxDevices];
+    static std::atomic<int> cache[kMaxDevices];
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
-    // resident CTAs of the whole device
-    int slots = dev >= 0 && dev < kMaxDevices ? sms_cache[dev].load(std::memory_order_acquire) : 0;
-    if (slots <= 0) {
+    int v = dev >= 0 && dev < kMaxDevices ? cache[dev].load(std::memory_order_acquire) : 0;
+    if (v <= 0) {
         err = cudaFuncSetAttribute(encode_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kSSmem);
         if (err != cudaSuccess) return err;
-        int sms = 0, per_sm = 0;
-        err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        int n = 0, p = 0;
+        err = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
         if (err != cudaSuccess) return err;
-        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, encode_stream_kernel, kThreads,
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&p, encode_stream_kernel, kThreads,
                                                             kSSmem);
         if (err != cudaSuccess) return err;
-        slots = sms * (per_sm > 0 ? per_sm : 1);
-        if (dev >= 0 && dev < kMaxDevices) sms_cache[dev].store(slots, std::memory_order_release);
+        v = (n << 8) | (p > 0 ? (p & 0xff) : 1);
+        if (dev >= 0 && dev < kMaxDevices) cache[dev].store(v, std::memory_order_release);
     }
+    *per_sm = v & 0xff;
+    *sms = v >> 8;
+    return cudaSuccess;
+}
+
+// Streaming CTAs that fit on the SMs that `busy_sms` clustered CTAs leave.
+cudaError_t stream_free_slots(uint32_t busy_sms, uint32_t* slots) {
+    int per_sm = 0, sms = 0;
+    cudaError_t err = stream_shape(&per_sm, &sms);
+    if (err != cudaSuccess) return err;
+    *slots = static_cast<uint32_t>(sms) > busy_sms ? (sms - busy_sms) * per_sm : 0u;
+    return cudaSuccess;
+}
+
+cudaError_t launch_encode_stream(const EncodeLaunch& l, cudaStream_t stream, bool tail) {
+    int per_sm = 0, sms = 0;
+    cudaError_t err = stream_shape(&per_sm, &sms);
+    if (err != cudaSuccess) return err;
     StreamArgs args{l.units, l.num_units, l.relative ? 1u : 0u, l.sizes, l.bounds, l.status,
-                    shift_mul()};
-    const uint32_t grid = min(l.num_units, static_cast<uint32_t>(slots));
+                    shift_mul(), tail ? 1u : 0u};
+    const uint32_t grid = min(l.num_units, static_cast<uint32_t>(sms * per_sm));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = tail ? 1 : 0;
     note_launch();
-    encode_stream_kernel<<<grid, kThreads, kSSmem, stream>>>(args);
-    return cudaGetLastError();
+    return cudaLaunchKernelEx(&cfg, encode_stream_kernel, args);
 }
 
 }  // namespace
@@ -1564,7 +1637,7 @@ cudaError_t encode_prepare(ElemType type) {
 cudaError_t launch_encode(const EncodeLaunch& l, cudaStream_t stream) {
     const bool streamable = l.type == ElemType::kBF16 && l.whole_pages && !l.test_polls;
     if (streamable && (l.encoder == 2 || (l.encoder == 0 && l.max_n <= kStreamMaxElems)))
-        return launch_encode_stream(l, stream);
+        return launch_encode_stream(l, stream, false);
     if (l.type == ElemType::kBF16) return launch_encode_t<__nv_bfloat16>(l, stream);
     return launch_encode_t<float>(l, stream);
 }

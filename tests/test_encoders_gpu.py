@@ -120,6 +120,23 @@ def test_automatic_choice_matches_both(lib_ckv):
             assert torch.equal(ref[3][i, :s], auto[3][i, :s])
 
 
+@pytest.mark.parametrize("count", [256, 271])
+def test_remainder_units_on_the_streaming_kernel(lib_ckv, count):
+    """Large batches whose last clustered round would hold a few units alone
+    hand those units to the streaming encoder, launched beside the clustered
+    one: the automatic choice writes the bytes of the clustered encoder."""
+    lib, _ckv = lib_ckv
+    n = 229376
+    pages = _pages(count, n, seed=count, kind="kv").cuda()
+    cap = _capacity(lib, n)
+    ref = _compress(lib, _ckv, pages, 1e-5, True, CLUSTER, cap)
+    auto = _compress(lib, _ckv, pages, 1e-5, True, 0, cap)
+    assert ref[0] == 0 and auto[0] == 0
+    assert auto[1] == ref[1] and auto[2] == ref[2]
+    for i, s in enumerate(ref[1]):
+        assert torch.equal(ref[3][i, :s], auto[3][i, :s]), f"unit {i}"
+
+
 def test_unaligned_pages_take_the_clustered_encoder(lib_ckv):
     """Pages that do not start on 16 bytes are not whole pages: forcing the
     streaming encoder falls back to the clustered one, same bytes."""
