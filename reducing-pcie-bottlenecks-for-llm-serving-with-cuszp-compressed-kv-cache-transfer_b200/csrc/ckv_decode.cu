@@ -403,19 +403,38 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
     }
 
     // The first item's payload offset: the sizes of all blocks before it,
-    // summed by the whole CTA.
+    // summed by the whole CTA.  The producer first starts the copies of its
+    // first items' rate bytes, which need only the item's position.
     uint32_t u0, s0;
     locate(a, begin, u0, s0);
+    RateCursor rc;
+    if (warp == kConsumerWarps) {
+        rc_open(a, u0, s0, rc);
+        for (int i = 0; i < kAhead; ++i) {
+            if (begin + i < end) rc_fetch(a, rc, rring[i]);
+            cp_async_commit();
+        }
+    }
     uint64_t first_start;
     bool first_ok;
     {
         const Unit unit = a.units[u0];
         const uint32_t* words = reinterpret_cast<const uint32_t*>(unit.stream);
+        const uint32_t lim = s0 * (kItemBlocks / 4);
         uint32_t acc = 0, bad = 0;
-        for (uint32_t w = tid; w < s0 * (kItemBlocks / 4); w += kCtaThreads) {
-            const uint32_t x = __ldg(words + w);
-            acc += __dp4a(x, 0x01010101u, 0u) + __dp4a(__vsetne4(x, 0u), 0x01010101u, 0u);
-            bad |= __vcmpgtu4(x, 0x1f1f1f1fu);
+        // eight loads in flight per thread before their sums
+        for (uint32_t w0 = tid; w0 < lim; w0 += 8 * kCtaThreads) {
+            uint32_t x[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t w = w0 + j * kCtaThreads;
+                x[j] = w < lim ? __ldg(words + w) : 0u;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                acc += __dp4a(x[j], 0x01010101u, 0u) + __dp4a(__vsetne4(x[j], 0u), 0x01010101u, 0u);
+                bad |= __vcmpgtu4(x[j], 0x1f1f1f1fu);
+            }
         }
 #pragma unroll
         for (int d = 16; d > 0; d >>= 1) {
@@ -444,12 +463,6 @@ __global__ void __launch_bounds__(kCtaThreads, kCtasPerSm) decode_kernel(DecodeA
         uint32_t status = 0;
         PItem cur, nxt;
         p_open(a, u0, s0, cur);
-        RateCursor rc;
-        rc_open(a, u0, s0, rc);
-        for (int i = 0; i < kAhead; ++i) {
-            if (begin + i < end) rc_fetch(a, rc, rring[i]);
-            cp_async_commit();
-        }
         uint64_t start = first_start;
         bool unit_ok = first_ok;
         if (!first_ok && lane == 0) atomicOr(&a.status[cur.u], kErrBadStream);
