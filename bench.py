@@ -521,6 +521,7 @@ class OurCodec:
         self.side = torch.cuda.Stream(device)
         self.cont_pages = None
         self.cont_ptrs = None
+        self._stream = None
         self.slab_set = [0, 0]   # which copy of the pages each host slab holds
 
     def _check(self, status: int, what: str):
@@ -528,7 +529,11 @@ class OurCodec:
             raise RuntimeError(f"{what}: {self.ckv.error_message(self.lib, self.ctx, status)}")
 
     def stream(self) -> int:
-        return torch.cuda.current_stream(self.device).cuda_stream
+        """The CUDA stream the calls run on (the device's current stream, as a
+        serving engine keeps its handle rather than looking it up per call)."""
+        if self._stream is None:
+            self._stream = torch.cuda.current_stream(self.device).cuda_stream
+        return self._stream
 
     def store(self):
         self._check(self.lib.ckv_compress_batch_fixed_bf16(
