@@ -88,6 +88,8 @@ CASES = [(n, kind, eb, rel) for n in (1, 31, 32, 33, 1000, 8191, 8192, 8193, 163
 CASES += [(n, kind, 1e-5, True) for n in (4096, 16384, 40001)
           for kind in ("one_sided", "specials", "const", "zero")]
 CASES += [(8192, "specials", 1e-3, False), (16384, "one_sided", 1e-4, False)]
+# C5 and C4 page sizes (the clustered encoder's 100 KB slice geometry)
+CASES += [(327680, "kv", 1e-4, True), (458752, "kv", 1e-5, True)]
 
 
 @pytest.mark.parametrize("n,kind,eb,relative", CASES)
@@ -120,13 +122,12 @@ def test_automatic_choice_matches_both(lib_ckv):
             assert torch.equal(ref[3][i, :s], auto[3][i, :s])
 
 
-@pytest.mark.parametrize("count", [256, 271])
-def test_remainder_units_on_the_streaming_kernel(lib_ckv, count):
+@pytest.mark.parametrize("count,n", [(256, 229376), (271, 229376), (256, 327680)])
+def test_remainder_units_on_the_streaming_kernel(lib_ckv, count, n):
     """Large batches whose last clustered round would hold a few units alone
     hand those units to the streaming encoder, launched beside the clustered
     one: the automatic choice writes the bytes of the clustered encoder."""
     lib, _ckv = lib_ckv
-    n = 229376
     pages = _pages(count, n, seed=count, kind="kv").cuda()
     cap = _capacity(lib, n)
     ref = _compress(lib, _ckv, pages, 1e-5, True, CLUSTER, cap)
