@@ -1940,6 +1940,13 @@ def main() -> int:
         gc.collect()
         torch.cuda.empty_cache()
 
+    # every rank's device-resident step time (the line's value uses the slowest)
+    step_by_rank = [statistics.median(step_ms)]
+    if dist is not None:
+        mine = torch.tensor([statistics.median(step_ms)], dtype=torch.float64, device=device)
+        allr = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        step_by_rank = [float(x.item()) for x in allr]
     t_step, t_e2e_iso, t_serial, t_cont = slowest_rank(
         [sum(step_ms) / 1e3, sum(e2e_ms) / 1e3, sum(e2e_serial_ms) / 1e3 if e2e_serial_ms else 0.0,
          cont_s or 0.0], dist, device)
@@ -1974,6 +1981,7 @@ def main() -> int:
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(t_step * 1e3 / args.steps, 4),
+        "median_ms_per_step_by_rank": [round(x, 4) for x in step_by_rank],
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
