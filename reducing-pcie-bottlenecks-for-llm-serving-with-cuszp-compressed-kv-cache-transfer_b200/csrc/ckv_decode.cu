@@ -236,6 +236,13 @@ __device__ __forceinline__ void store_block16(__nv_bfloat16* dst, const Bf16Word
     for (int c = 0; c < 4; ++c) d[c] = make_uint4(b.w[4 * c], b.w[4 * c + 1], b.w[4 * c + 2], b.w[4 * c + 3]);
 }
 
+// e / L for a run length L: a shift when L is a power of two (KV layers and
+// heads), zero when e lies in the first run (one destination per page).
+__device__ __forceinline__ uint32_t run_of(uint32_t e, uint32_t L) {
+    if ((L & (L - 1u)) == 0u) return e >> (__ffs(L) - 1);
+    return e < L ? 0u : e / L;
+}
+
 // Writes block jb of unit u (its first `valid` values) through its map.
 template <typename T, typename Values>
 __device__ __forceinline__ void write_block(const DecodeArgs& a, const SlotMeta& m, uint32_t jb,
@@ -257,7 +264,7 @@ __device__ __forceinline__ void write_block(const DecodeArgs& a, const SlotMeta&
     unit.elems = m.elems;
     unit.n = m.n;
     const uint32_t L = map.run;
-    const uint32_t r0 = e0 / L, off = e0 - r0 * L;
+    const uint32_t r0 = run_of(e0, L), off = e0 - r0 * L;
     T* dst = run_base<T>(unit, map, m.u, r0) + off;
     if (valid == kBlock && off + kBlock <= L && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
         store_block16(dst, f);
@@ -267,7 +274,7 @@ __device__ __forceinline__ void write_block(const DecodeArgs& a, const SlotMeta&
     for (int v = 0; v < 32; ++v) {
         if (static_cast<uint32_t>(v) < valid) {
             const uint32_t i = e0 + v;
-            const uint32_t r = i / L;
+            const uint32_t r = run_of(i, L);
             store_elem(run_base<T>(unit, map, m.u, r) + (i - r * L), f, v);
         }
     }
