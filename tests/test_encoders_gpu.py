@@ -122,7 +122,7 @@ def test_automatic_choice_matches_both(lib_ckv):
             assert torch.equal(ref[3][i, :s], auto[3][i, :s])
 
 
-@pytest.mark.parametrize("count,n", [(256, 229376), (271, 229376), (256, 327680)])
+@pytest.mark.parametrize("count,n", [(256, 229376), (271, 229376), (256, 327680), (512, 327680)])
 def test_remainder_units_on_the_streaming_kernel(lib_ckv, count, n):
     """Large batches whose last clustered round would hold a few units alone
     hand those units to the streaming encoder, launched beside the clustered
