@@ -1427,11 +1427,13 @@ def layer_groups_c3(codec, steps: int, flush: torch.Tensor, device, repeat: int 
         lib.ckv_pipe_destroy(pipe)
 
 
-# BASELINE.json configs[3] (C4) and configs[4] (C5, one GPU's shard): jobs of 2048 pages.
+# BASELINE.json configs[3] (C4: one job per request, 2048 pages) and configs[4] (C5, one GPU's
+# 8192-page shard, moved as 16 jobs of 512 pages: the store of job k overlaps the restore of job
+# k-1, so only the first store and the last restore run alone).
 STREAMED = {
-    "C4": {"layers": 28, "heads": 4, "jobs": 16, "eps": 1e-5, "seed": 1000,
+    "C4": {"layers": 28, "heads": 4, "jobs": 16, "pages_per_job": 2048, "eps": 1e-5, "seed": 1000,
            "what": "Qwen2.5-7B KV, 16 requests x 32k tokens (2048 pages each), REL 1e-5"},
-    "C5": {"layers": 80, "heads": 1, "jobs": 4, "eps": 1e-4, "seed": 2000,
+    "C5": {"layers": 80, "heads": 1, "jobs": 16, "pages_per_job": 512, "eps": 1e-4, "seed": 2000,
            "what": "Llama-3-70B KV at 128k tokens, TP=8 shard of one GPU (8192 pages), REL 1e-4"},
 }
 
@@ -1454,9 +1456,22 @@ def make_job_pages(layers: int, heads: int, pages: int, seed: int, device) -> to
     return out.view(pages, -1)
 
 
-def streamed_host_bytes(name: str, pages_per_job: int = 2048) -> int:
+def streamed_shape(name: str, job_pages: int = 0) -> tuple:
+    """(jobs, pages per job) of a C4 / C5 leg: the config's, or its pages split into jobs of
+    job_pages pages."""
+    cfg = STREAMED[name]
+    if job_pages <= 0:
+        return cfg["jobs"], cfg["pages_per_job"]
+    total = cfg["jobs"] * cfg["pages_per_job"]
+    if total % job_pages:
+        raise ValueError(f"{name}: {total} pages do not split into jobs of {job_pages}")
+    return total // job_pages, job_pages
+
+
+def streamed_host_bytes(name: str, job_pages: int = 0) -> int:
     """Page-locked bytes a rank's C4 / C5 leg holds (two raw-size job slabs)."""
     cfg = STREAMED[name]
+    pages_per_job = streamed_shape(name, job_pages)[1]
     return 2 * pages_per_job * 2 * cfg["layers"] * cfg["heads"] * TOKENS * HEAD_DIM * 2
 
 
@@ -1469,16 +1484,16 @@ def host_memory_available() -> int:
 
 
 def streamed_jobs(codec, name: str, steps: int, flush: torch.Tensor, device, rank: int = 0,
-                  chunk_pages: int = 256, pages_per_job: int = 2048, dist=None,
+                  chunk_pages: int = 256, job_pages: int = 0, dist=None,
                   world: int = 1) -> dict:
-    """C4 / C5 through the pipeline: a step stores every job (2048 pages each) from its own KV
+    """C4 / C5 through the pipeline: a step stores every job (streamed_shape) from its own KV
     pages into one of two page-locked slabs on the caller's stream while the previous job is
     restored on a second stream (background store, on-demand restore), so the link carries a
     store and a restore at once.  Restores are checked per element against their page's bound.
     Each rank runs its own jobs (its own seeds, as a tensor-parallel shard would)."""
     cfg = STREAMED[name]
     lib, ck = codec.lib, codec.ckv
-    jobs = cfg["jobs"]
+    jobs, pages_per_job = streamed_shape(name, job_pages)
     pages = [make_job_pages(cfg["layers"], cfg["heads"], pages_per_job,
                             cfg["seed"] + rank * jobs + r, device)
              for r in range(jobs)]
@@ -1768,6 +1783,9 @@ def main() -> int:
                          "at every N, 'none' neither")
     ap.add_argument("--chunk-pages", type=int, default=0,
                     help="pages per pipeline chunk (0: the whole job in one chunk)")
+    ap.add_argument("--job-pages", type=int, default=0,
+                    help="pages per job of the C4 / C5 legs (0: each config's own: C4 one "
+                         "2048-page job per request, C5 16 jobs of 512 pages)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1919,14 +1937,15 @@ def main() -> int:
             continue
         # every rank runs its own shard; all ranks take the same branch
         fits = torch.tensor([1 if host_memory_available() >= world * 2 *
-                             streamed_host_bytes(name) else 0], device=device)
+                             streamed_host_bytes(name, args.job_pages) else 0], device=device)
         if dist is not None:
             dist.all_reduce(fits, op=dist.ReduceOp.MIN)
         if not int(fits.item()):
             streamed[name] = {"workload": name, "skipped": "not enough host memory"}
             continue
         barrier()
-        leg = streamed_jobs(codec, name, 3, flush, device, rank=rank, dist=dist, world=world)
+        leg = streamed_jobs(codec, name, 3, flush, device, rank=rank, dist=dist, world=world,
+                            job_pages=args.job_pages)
         t_st, t_rs, t_d2h, t_h2d = leg.pop("direction_seconds")
         (t_leg, t_st, t_rs) = slowest_rank([leg.pop("seconds"), t_st, t_rs], dist, device)
         leg["e2e_gbps_rank0"] = leg.pop("e2e_gbps")
