@@ -208,8 +208,9 @@ CKV_API ckv_status ckv_test_withhold_exchange(ckv_ctx* ctx, uint32_t unit, uint3
  * encoder for batches of whole pages (every unit a contiguous, 16-byte
  * aligned page) of at most 16384 elements each, where it is faster, and the
  * clustered encoder otherwise (a large batch of whole pages may hand the
- * clustered encoder's last, nearly empty round of units to the streaming
- * encoder, which then runs beside it on the SMs no cluster holds);
+ * clustered encoder's last, nearly empty round of units, and for long
+ * batches whole further rounds, to the streaming encoder, which then runs
+ * beside it on the SMs no cluster holds);
  * CKV_ENCODER_CLUSTER always the clustered one alone;
  * CKV_ENCODER_STREAM the streaming one whenever the batch is whole pages.
  * The streaming encoder handles one unit per CTA and reads it twice (bound,
