@@ -1783,6 +1783,8 @@ def main() -> int:
                          "at every N, 'none' neither")
     ap.add_argument("--chunk-pages", type=int, default=0,
                     help="pages per pipeline chunk (0: the whole job in one chunk)")
+    ap.add_argument("--job-chunk-pages", type=int, default=256,
+                    help="pages per pipeline chunk of the C4 / C5 jobs")
     ap.add_argument("--job-pages", type=int, default=0,
                     help="pages per job of the C4 / C5 legs (0: each config's own: C4 one "
                          "2048-page job per request, C5 16 jobs of 512 pages)")
@@ -1945,7 +1947,7 @@ def main() -> int:
             continue
         barrier()
         leg = streamed_jobs(codec, name, 3, flush, device, rank=rank, dist=dist, world=world,
-                            job_pages=args.job_pages)
+                            job_pages=args.job_pages, chunk_pages=args.job_chunk_pages)
         t_st, t_rs, t_d2h, t_h2d = leg.pop("direction_seconds")
         (t_leg, t_st, t_rs) = slowest_rank([leg.pop("seconds"), t_st, t_rs], dist, device)
         leg["e2e_gbps_rank0"] = leg.pop("e2e_gbps")
