@@ -698,7 +698,16 @@ class _Engine:
 class CompressedOffloadingHandler:
     """One transfer direction.  ``transfer_async(job_id, (src_spec, dst_spec))``
     with GPU block ids on the GPU side and CPU block ids (keys of the page
-    store) on the CPU side."""
+    store) on the CPU side.
+
+    Each direction issues its jobs on a CUDA stream of its own, ordered after
+    the work already on the caller's current stream (the model's writes to
+    the blocks), and never makes the caller's stream wait: as in the
+    reference (vllm_v1_compressed_offload.py:2365-2385, a worker thread's
+    stream after a ready event), a job's blocks are the caller's again once
+    get_finished reports it or wait returns.  So a store and a load issued
+    one after the other overlap instead of queueing behind each other, and
+    jobs of one direction run in issue order."""
 
     def __init__(self, engine: _Engine, store: CompressedPageStore, gpu_to_cpu: bool,
                  error_bound: float | None = None):
@@ -711,6 +720,7 @@ class CompressedOffloadingHandler:
         self._finished: list[TransferResult] = []
         self._lock = threading.Lock()
         self._finalize: dict[int, list] = {}   # INT8 store ticket -> its page entries
+        self._stream: torch.cuda.Stream | None = None           # created by the first job
 
     def _components(self, g: int) -> tuple[BundleComponent, ...]:
         e = self.engine
@@ -866,10 +876,17 @@ class CompressedOffloadingHandler:
         with self.engine.lock:
             if len(src_ids) == 0:
                 tickets, nbytes = [], 0
-            elif self.gpu_to_cpu:
-                tickets, nbytes = self._store(src_ids, dst_ids)
             else:
-                tickets, nbytes = self._load(src_ids, dst_ids)
+                dev = self.engine.device
+                if self._stream is None:
+                    self._stream = torch.cuda.Stream(dev)
+                self._stream.wait_stream(torch.cuda.current_stream(dev))
+                # _store / _load issue on the current stream, here this direction's
+                with torch.cuda.stream(self._stream):
+                    if self.gpu_to_cpu:
+                        tickets, nbytes = self._store(src_ids, dst_ids)
+                    else:
+                        tickets, nbytes = self._load(src_ids, dst_ids)
         with self._lock:
             self._pending[int(job_id)] = (tickets, nbytes)
         return True
