@@ -296,6 +296,44 @@ def test_handlers_overlapping_jobs_and_slab_reuse():
 
 
 @pytest.mark.gpu
+def test_handlers_order_jobs_after_the_callers_stream():
+    """Each direction issues on a stream of its own: a store must still see
+    the blocks as the caller's stream last wrote them (here after a ~10 ms
+    sleep kernel, so a store that did not wait would compress the old
+    values), and the caller's current stream is left as it was."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    shape = (2, 4, 2, 16, 128)
+    kv = _kv(64, shape, seed=13).cuda()
+    new = _kv(32, shape, seed=14).cuda()
+    h = ko.CompressedCpuGpuOffloadingHandlers(kv, error_bound=1e-4, device_id=0, chunk_pages=8)
+    try:
+        caller = torch.cuda.current_stream()
+        torch.cuda._sleep(20_000_000)
+        kv[:32].copy_(new)
+        h.gpu_to_cpu_handler.transfer_async(1, (np.arange(0, 32), np.arange(1000, 1032)))
+        assert torch.cuda.current_stream() == caller
+        h.cpu_to_gpu_handler.transfer_async(2, (np.arange(1000, 1032), np.arange(32, 64)))
+        assert torch.cuda.current_stream() == caller
+        h.gpu_to_cpu_handler.wait({1})
+        h.cpu_to_gpu_handler.wait({2})
+        torch.cuda.synchronize()
+        first = kv[32:64].clone()
+        x = new.float()
+        err = (first.float() - x).abs()
+        assert bool((err <= 1e-4 * 2 * x.abs().amax() + 1e-7 + x.abs() * 2 ** -8).all())
+        # the same blocks stored and loaded again with nothing pending on the
+        # caller's stream: bit for bit the same restore
+        h.gpu_to_cpu_handler.transfer_async(3, (np.arange(0, 32), np.arange(3000, 3032)))
+        h.cpu_to_gpu_handler.transfer_async(4, (np.arange(3000, 3032), np.arange(32, 64)))
+        h.cpu_to_gpu_handler.wait({4})
+        torch.cuda.synchronize()
+        assert torch.equal(kv[32:64].view(torch.int16), first.view(torch.int16))
+    finally:
+        h.shutdown()
+
+
+@pytest.mark.gpu
 def test_handlers_layer_groups_match_plain_calls():
     """The mixed per-layer profile (7 layers at 1e-5, 21 at 1e-4) through the
     handlers: two segments per page equal compress_batch_fixed_bf16_indexed
