@@ -804,24 +804,28 @@ class CompressedOffloadingHandler:
                         codec=e.codec)
         comps = [self._components(g) for g in range(G)]
         req = [self.error_bound] if e.groups is None else [b for b, _sel in e.groups]
+        numels = [e.segment_numel(g) for g in range(G)]
+        codeds = [e.coded if e.groups is None else numels[g] for g in range(G)]
+        # the page table as Python lists once: per-page records are then
+        # plain slices (the job's host bookkeeping runs while its copies fly)
+        ids_l, offs_l, sizes_l = slab.job[0].tolist(), slab.job[1].ravel().tolist(), \
+            slab.job[2].ravel().tolist()
+        bounds_l, buf = slab.job[3].ravel().tolist(), slab.buffer
         entries = []
         for i in range(count):
-            span = range(i * G, i * G + G)
-            rec = _PageRecord(sid, tuple(int(offsets[j]) for j in span),
-                              tuple(int(sizes[j]) for j in span),
-                              tuple(float(bounds[j]) for j in span), e.n,
-                              tuple(raw[j] for j in span))
+            j0, j1 = i * G, i * G + G
+            ro, rs, rr = tuple(offs_l[j0:j1]), tuple(sizes_l[j0:j1]), tuple(raw[j0:j1])
+            rb = tuple(bounds_l[j0:j1])
+            rec = _PageRecord(sid, ro, rs, rb, e.n, rr)
             segs = []
             for g in range(G):
-                numel = e.segment_numel(g)
-                coded = e.coded if e.groups is None else numel
-                payload = slab.buffer[hdr + rec.offsets[g]: hdr + rec.offsets[g] + rec.sizes[g]]
-                encoding = "raw" if rec.raw[g] else e.codec
-                segs.append(EncodedSegment(payload, rec.sizes[g], rec.bounds[g], encoding,
-                                           comps[g], numel, coded, numel * 2, req[g],
+                encoding = "raw" if rr[g] else e.codec
+                segs.append(EncodedSegment(buf[hdr + ro[g]: hdr + ro[g] + rs[g]], rs[g], rb[g],
+                                           encoding, comps[g], numels[g], codeds[g],
+                                           numels[g] * 2, req[g],
                                            cuszp_mode="fixed" if encoding == "cuszp" else None))
-            entries.append((int(cpu_ids[i]),
-                            rec, CompressedBundle(tuple(segs), sum(rec.sizes), e.page_bytes)))
+            entries.append((ids_l[i], rec,
+                            CompressedBundle(tuple(segs), sum(rs), e.page_bytes)))
         self.store.put_many_packed(entries)
         if e.codec == "int8":
             self._finalize[final] = entries
